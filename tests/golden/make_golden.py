@@ -1,0 +1,267 @@
+"""Generate golden fixtures by running SplatForge's own Torch provider.
+
+Run in a container where the reference source tree is present:
+
+    python tests/golden/make_golden.py /root/reference/src
+
+It imports the reference read-only (no files are written into it), evaluates
+its renderers, operators and tile binning on seeded synthetic inputs, and
+writes compressed ``.npz`` fixtures next to this script.  The fixtures pin the
+CPU oracle (``oracle/``) in ``tests/test_oracle_golden.py``; GPU parity tests
+then compare the CUDA path against that pinned oracle.
+
+Fixtures (all float32 unless noted):
+
+* ``binning.npz``   -- the reference's rng(703) tangency fixture plus larger
+                       random cases: bounds in, CSR tile lists out (int64).
+* ``ops.npz``       -- covariance@1, sh_color@1 (deg 0..3), pixel_rays@1,
+                       ray_peak@1, alpha_composite@3 (all profiles, with input
+                       gradients), opacity_field@1.
+* ``render_<mode>.npz`` -- ``TorchRenderer`` on the 48-Gaussian demo scene, three
+                       24x24 views: every image channel, projected means and
+                       radii, and the parameter gradients of a seeded linear loss
+                       over every channel, plus ``projected_means.grad/.absgrad``.
+* ``train_<mode>.npz``  -- ``BatchedTorchRenderer.render_training`` on the same
+                       scene (the per-mode distortion profile).
+* ``crop_<mode>.npz``   -- ``BatchedTorchRenderer`` on a 48x32 tile-aligned crop of
+                       a 20k-Gaussian surface scene (gradients stored sparsely).
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+
+
+def _setup(src):
+    sys.path.insert(0, str(src))
+    sys.path.insert(0, str(REPO))
+    sys.dont_write_bytecode = True
+    torch.set_num_threads(1)
+
+
+def binning_cases():
+    from splatforge.studio.tile_binning import tile_members
+
+    out = {}
+    rng = np.random.default_rng(703)
+    b = rng.normal(size=(250, 4)).astype(np.float32)
+    b[:, :2] = b[:, :2] * 35 + 16
+    b[:, 2] = rng.uniform(0, 45, len(b))
+    b[:, 3] = rng.uniform(-1, 10, len(b))
+    b[0] = [16, 16, 0, 2]
+    b[1] = [40, 24, 7, 2]
+    cases = [("fixture703", b, 33, 21, 0.01, 9.0)]
+    rng = np.random.default_rng(11)
+    for k, (n, w, h) in enumerate(((4000, 200, 150), (3000, 97, 61))):
+        bb = np.empty((n, 4), np.float32)
+        bb[:, 0] = rng.uniform(-40, w + 40, n)
+        bb[:, 1] = rng.uniform(-40, h + 40, n)
+        bb[:, 2] = rng.exponential(8.0, n)
+        bb[:, 3] = rng.choice(np.linspace(-0.5, 12.0, 300), n)  # many exact depth ties
+        bb[:8, :] = [[16, 16, 0, 2], [32, 0, 16, 1], [0, 32, 16, 1], [w, h, 0, 1],
+                     [w + 1, h, 1, 1], [-1, -1, 1, 1], [48, 48, 16, 0.01], [48, 48, 16, 12.0]]
+        cases.append((f"random{k}", bb, w, h, 0.01, 10.0))
+    for name, bounds, w, h, near, far in cases:
+        members = tile_members(bounds, width=w, height=h, tile_size=16, near=near, far=far)
+        offsets = np.concatenate(([0], np.cumsum([len(m) for m in members]))).astype(np.int64)
+        ids = np.concatenate(members).astype(np.int64) if len(members) else np.zeros(0, np.int64)
+        out[f"{name}/bounds"] = bounds
+        out[f"{name}/meta"] = np.array([w, h, 16, near, far], np.float64)
+        out[f"{name}/offsets"] = offsets
+        out[f"{name}/ids"] = ids
+    np.savez_compressed(HERE / "binning.npz", **out)
+
+
+def op_cases():
+    from splatforge.gaussian import SurfaceOperators
+
+    ops = SurfaceOperators()
+    out = {}
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(64, 4, generator=g)
+    s = torch.rand(64, 3, generator=g) * 0.5 + 0.05
+    out["cov/quats"], out["cov/scales"] = q.numpy(), s.numpy()
+    out["cov/out"] = ops("gaussian.covariance@1", q, s).numpy()
+    sh = torch.randn(64, 16, 3, generator=g) * 0.3
+    d = torch.randn(64, 3, generator=g)
+    out["sh/coeffs"], out["sh/dirs"] = sh.numpy(), d.numpy()
+    for deg in range(4):
+        shv = sh.clone().requires_grad_()
+        dv = d.clone().requires_grad_()
+        col = ops("gaussian.sh_color@1", shv, dv, degree=deg)
+        up = torch.randn(col.shape, generator=g)
+        gs, gd = torch.autograd.grad((col * up).sum(), (shv, dv), allow_unused=True)
+        gd = torch.zeros_like(dv) if gd is None else gd
+        out[f"sh/deg{deg}/out"] = col.detach().numpy()
+        out[f"sh/deg{deg}/up"] = up.numpy()
+        out[f"sh/deg{deg}/gcoeffs"] = gs.numpy()
+        out[f"sh/deg{deg}/gdirs"] = gd.numpy()
+    K = torch.tensor([[30.0, 0, 17.0], [0, 28.0, 11.0], [0, 0, 1]])
+    out["rays/K"] = K.numpy()
+    out["rays/out"] = ops("camera.pixel_rays@1", K, width=33, height=21).numpy()
+    # ray peak
+    m = torch.randn(7, 3, generator=g)
+    A = torch.randn(7, 3, 3, generator=g)
+    Q = A @ A.transpose(-1, -2) + torch.eye(3)
+    o = torch.randn(5, 3, generator=g)
+    dd = torch.randn(5, 3, generator=g)
+    t, r, n = ops("gaussian.ray_peak@1", m, Q, o, dd)
+    out.update({"peak/means": m.numpy(), "peak/Q": Q.numpy(), "peak/o": o.numpy(),
+                "peak/d": dd.numpy(), "peak/t": t.numpy(), "peak/r": r.numpy(), "peak/n": n.numpy()})
+    # composite @3, every profile, with adjoints
+    B, N, P = 3, 9, 11
+    a0 = torch.rand(B, N, P, generator=g) * 0.6
+    a0[0, 2, :4] = 0.9995  # clamp at 0.999
+    a0[1, 3, :3] = -0.01  # clamp at 0
+    c0 = torch.rand(B, N, 3, generator=g)
+    d0 = torch.rand(B, N, P, generator=g) * 4 + 1
+    n0 = torch.randn(B, N, P, 3, generator=g)
+    out.update({"comp/a": a0.numpy(), "comp/c": c0.numpy(), "comp/d": d0.numpy(), "comp/n": n0.numpy()})
+    ups = None
+    for prof in ("none", "l1", "l2", "both"):
+        ins = [t.clone().requires_grad_() for t in (a0, c0, d0, n0)]
+        res = ops("splat.alpha_composite@3", *ins, distortions=prof)
+        if ups is None:
+            ups = [torch.randn(r.shape, generator=g) for r in res]
+            for i, u in enumerate(ups):
+                out[f"comp/up{i}"] = u.numpy()
+        loss = sum((r * u).sum() for r, u in zip(res, ups))
+        grads = torch.autograd.grad(loss, ins)
+        for i, r in enumerate(res):
+            out[f"comp/{prof}/out{i}"] = r.detach().numpy()
+        for name, gr in zip("acdn", grads):
+            out[f"comp/{prof}/g{name}"] = gr.numpy()
+    # opacity field
+    pts = torch.randn(40, 3, generator=g) * 0.6
+    mm = torch.randn(25, 3, generator=g) * 0.5
+    L = torch.randn(25, 3, 3, generator=g) * 0.1
+    C = L @ L.transpose(-1, -2) + 0.01 * torch.eye(3)
+    Qf = torch.linalg.inv(C)
+    op = torch.rand(25, generator=g)
+    origins = torch.randn(3, 3, generator=g) * 3
+    field = ops("gaussian.opacity_field@1", pts, mm, Qf, op, origins)
+    out.update({"field/p": pts.numpy(), "field/m": mm.numpy(), "field/Q": Qf.numpy(),
+                "field/o": op.numpy(), "field/origins": origins.numpy(), "field/out": field.numpy()})
+    np.savez_compressed(HERE / "ops.npz", **out)
+
+
+CHANNELS = ("rgb", "alpha", "depth", "normals", "distortion_l1", "distortion_l2",
+            "median_depth", "ray_color", "ambiguity_mask")
+
+
+def _view_from(params, GaussianView):
+    return GaussianView(params.means, params.quats, params.log_scales.exp(),
+                        params.opacity_logits.sigmoid(), params.sh, params.sh_degree)
+
+
+def _camera(cam, Camera):
+    return Camera(cam.K, cam.world_to_camera, cam.width, cam.height, cam.name)
+
+
+def _run(renderer_call, params, cams, Camera, GaussianView, seed, sparse=False):
+    out = {}
+    for v, cam in enumerate(cams):
+        p = params.detach_clone().requires_grad_()
+        view = _view_from(p, GaussianView)
+        n = p.means.shape[0]
+        selected = torch.arange(n) % 2 == 0
+        res = renderer_call(view, _camera(cam, Camera), selected)
+        g = torch.Generator().manual_seed(seed + v)
+        loss = 0
+        for ch in CHANNELS:
+            img = getattr(res, ch)
+            up = torch.randn(img.shape, generator=g)
+            out[f"v{v}/up_{ch}"] = up.numpy()
+            out[f"v{v}/{ch}"] = img.detach().numpy()
+            loss = loss + (img * up).sum()
+        names = ("means", "log_scales", "quats", "opacity_logits", "sh")
+        grads = torch.autograd.grad(loss, list(p.tensors()))
+        pm = res.projected_means
+        # projected_means carries .grad via retain_grad and .absgrad via hooks
+        loss2 = 0
+        p2 = params.detach_clone().requires_grad_()
+        res2 = renderer_call(_view_from(p2, GaussianView), _camera(cam, Camera), selected)
+        g = torch.Generator().manual_seed(seed + v)
+        for ch in CHANNELS:
+            img = getattr(res2, ch)
+            up = torch.randn(img.shape, generator=g)
+            loss2 = loss2 + (img * up).sum()
+        loss2.backward()
+        pm2 = res2.projected_means
+        out[f"v{v}/projected_means"] = pm.detach().numpy()
+        out[f"v{v}/projected_radii"] = res.projected_radii.detach().numpy()
+        if sparse:
+            rows = np.flatnonzero(
+                np.abs(np.concatenate([gr.reshape(n, -1).numpy() for gr in grads], 1)).sum(1) > 0
+            )
+            out[f"v{v}/rows"] = rows.astype(np.int64)
+            for name, gr in zip(names, grads):
+                out[f"v{v}/grad_{name}"] = gr.numpy()[rows]
+            out[f"v{v}/means2d_grad"] = pm2.grad.numpy()[rows]
+            out[f"v{v}/absgrad"] = pm2.absgrad.numpy()[rows]
+        else:
+            for name, gr in zip(names, grads):
+                out[f"v{v}/grad_{name}"] = gr.numpy()
+            out[f"v{v}/means2d_grad"] = pm2.grad.numpy()
+            out[f"v{v}/absgrad"] = pm2.absgrad.numpy()
+    return out
+
+
+def render_cases():
+    from splatforge.studio.batched_renderer import BatchedTorchRenderer
+    from splatforge.studio.cameras import Camera
+    from splatforge.studio.config import RenderConfig
+    from splatforge.studio.renderers import GaussianView, TorchRenderer
+    from splatforge_b200 import scenes
+
+    params, cams = scenes.workload("demo48", seed=0)
+    cams = cams[:3]
+    for mode in ("radegs", "gof", "ambisur"):
+        cfg = RenderConfig()
+        r = TorchRenderer(cfg, mode=mode, trunc_sigma=2.0)
+        out = _run(lambda v, c, s: r.render(v, c, selected=s), params, cams, Camera, GaussianView, 100)
+        out["params/" + "means"] = params.means.numpy()
+        for name, t in zip(("means", "log_scales", "quats", "opacity_logits", "sh"), params.tensors()):
+            out[f"params/{name}"] = t.numpy()
+        for v, c in enumerate(cams):
+            out[f"cam{v}/K"] = c.K.numpy()
+            out[f"cam{v}/w2c"] = c.world_to_camera.numpy()
+            out[f"cam{v}/size"] = np.array([c.width, c.height])
+        np.savez_compressed(HERE / f"render_{mode}.npz", **out)
+        b = BatchedTorchRenderer(cfg, mode=mode, trunc_sigma=2.0)
+        out = _run(lambda v, c, s: b.render_training(v, c, selected=s, geometric=True),
+                   params, cams[:1], Camera, GaussianView, 200)
+        np.savez_compressed(HERE / f"train_{mode}.npz", **out)
+    # a tile-aligned crop of a denser surface scene (config-2 distributions)
+    params = scenes.surfaces(20_000, seed=3)
+    cam = scenes.orbit_cameras(1, 800, 800, 50.0, radius=3.0, seed=3)[0]
+    crop = cam.crop(384, 384, 48, 32)
+    for mode in ("radegs", "gof"):
+        cfg = RenderConfig()
+        b = BatchedTorchRenderer(cfg, mode=mode, trunc_sigma=2.0)
+        out = _run(lambda v, c, s: b.render(v, c, selected=s, distortions="both"),
+                   params, [crop], Camera, GaussianView, 300, sparse=True)
+        out["crop/K"] = crop.K.numpy()
+        out["crop/w2c"] = crop.world_to_camera.numpy()
+        out["crop/size"] = np.array([crop.width, crop.height])
+        np.savez_compressed(HERE / f"crop_{mode}.npz", **out)
+
+
+if __name__ == "__main__":
+    _setup(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    which = sys.argv[2:] or ["binning", "ops", "render"]
+    if "binning" in which:
+        binning_cases()
+    if "ops" in which:
+        op_cases()
+    if "render" in which:
+        render_cases()
+    for f in sorted(HERE.glob("*.npz")):
+        print(f.name, f.stat().st_size)

@@ -1,0 +1,134 @@
+"""Pins the CPU oracle against fixtures produced by the reference itself.
+
+The fixtures (``tests/golden/*.npz``) come from ``tests/golden/make_golden.py``,
+which ran SplatForge's Torch provider: ``TorchRenderer``,
+``BatchedTorchRenderer``, the ``gaussian.*``/``splat.*`` operators and
+``tile_members``.  Everything here runs on CPU.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import binning, ops
+from oracle import render as oracle_render
+from splatforge_b200 import scenes
+from tests._util import CHANNELS, PARAM_NAMES, camera_from, linear_loss, params_from
+
+
+@pytest.mark.parametrize("case", ["fixture703", "random0", "random1"])
+def test_binning_matches_reference_tile_members(golden, case):
+    fix = golden("binning")
+    w, h, ts, near, far = fix[f"{case}/meta"]
+    offsets, ids, keys = binning.tile_lists(
+        fix[f"{case}/bounds"], width=int(w), height=int(h), tile_size=int(ts), near=near, far=far
+    )
+    np.testing.assert_array_equal(offsets, fix[f"{case}/offsets"])
+    np.testing.assert_array_equal(ids, fix[f"{case}/ids"])
+    # keys are sorted and carry the tile id in their high word
+    assert np.all(np.diff(keys.astype(np.uint64)) >= 0) or len(keys) < 2
+    assert np.all((keys >> np.uint64(32)).astype(np.int64) == np.repeat(np.arange(len(offsets) - 1), np.diff(offsets)))
+
+
+def test_covariance_and_rays(golden):
+    f = golden("ops")
+    cov = ops.covariance(torch.from_numpy(f["cov/quats"]), torch.from_numpy(f["cov/scales"]))
+    np.testing.assert_allclose(cov.numpy(), f["cov/out"], rtol=0, atol=1e-6)
+    rays = ops.pixel_rays(torch.from_numpy(f["rays/K"]), width=33, height=21)
+    np.testing.assert_allclose(rays.numpy(), f["rays/out"], rtol=0, atol=1e-7)
+    t, r, n = ops.ray_peak(*(torch.from_numpy(f[k]) for k in ("peak/means", "peak/Q", "peak/o", "peak/d")))
+    np.testing.assert_allclose(t.numpy(), f["peak/t"], rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(r.numpy(), f["peak/r"], rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(n.numpy(), f["peak/n"], rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("degree", [0, 1, 2, 3])
+def test_sh_color(golden, degree):
+    f = golden("ops")
+    sh = torch.from_numpy(f["sh/coeffs"]).requires_grad_()
+    d = torch.from_numpy(f["sh/dirs"]).requires_grad_()
+    col = ops.sh_color(sh, d, degree=degree)
+    np.testing.assert_allclose(col.detach().numpy(), f[f"sh/deg{degree}/out"], atol=1e-6)
+    gs, gd = torch.autograd.grad((col * torch.from_numpy(f[f"sh/deg{degree}/up"])).sum(), (sh, d), allow_unused=True)
+    gd = torch.zeros_like(d) if gd is None else gd
+    np.testing.assert_allclose(gs.numpy(), f[f"sh/deg{degree}/gcoeffs"], atol=1e-6)
+    np.testing.assert_allclose(gd.numpy(), f[f"sh/deg{degree}/gdirs"], atol=1e-5)
+
+
+@pytest.mark.parametrize("profile", ["none", "l1", "l2", "both"])
+def test_alpha_composite(golden, profile):
+    f = golden("ops")
+    ins = [torch.from_numpy(f[f"comp/{k}"]).requires_grad_() for k in "acdn"]
+    res = ops.alpha_composite_batch(*ins, distortions=profile)
+    for i, r in enumerate(res):
+        np.testing.assert_allclose(r.detach().numpy(), f[f"comp/{profile}/out{i}"], atol=1e-6)
+    loss = sum((r * torch.from_numpy(f[f"comp/up{i}"])).sum() for i, r in enumerate(res))
+    grads = torch.autograd.grad(loss, ins)
+    for name, g in zip("acdn", grads):
+        np.testing.assert_allclose(g.numpy(), f[f"comp/{profile}/g{name}"], atol=2e-5)
+
+
+def test_opacity_field(golden):
+    f = golden("ops")
+    out = ops.opacity_field(*(torch.from_numpy(f[f"field/{k}"]) for k in ("p", "m", "Q", "o", "origins")))
+    np.testing.assert_allclose(out.numpy(), f["field/out"], atol=1e-6)
+
+
+def _oracle_views(fix, mode, *, prefix, cams, distortions, seed_views):
+    params = params_from(fix, "params/") if "params/means" in fix else None
+    return params
+
+
+def _check_render(fix, params, cams, mode, distortions, n_views, sparse=False):
+    for v in range(n_views):
+        p = params.detach_clone().requires_grad_()
+        view = scenes.activated(p)
+        n = p.means.shape[0]
+        sel = torch.arange(n) % 2 == 0
+        out = oracle_render.render(view, cams[v], mode=mode, selected=sel, distortions=distortions)
+        for ch in CHANNELS:
+            np.testing.assert_allclose(
+                out[ch].detach().numpy(), fix[f"v{v}/{ch}"], atol=2e-6, rtol=1e-5, err_msg=f"{mode} v{v} {ch}"
+            )
+        np.testing.assert_allclose(out["projected_means"].detach().numpy(), fix[f"v{v}/projected_means"], atol=1e-5)
+        np.testing.assert_allclose(out["projected_radii"].detach().numpy(), fix[f"v{v}/projected_radii"], rtol=1e-5, atol=1e-5)
+        ups = {ch: torch.from_numpy(fix[f"v{v}/up_{ch}"]) for ch in CHANNELS}
+        linear_loss(out, ups).backward()
+        rows = fix[f"v{v}/rows"] if sparse else slice(None)
+        for name, t in zip(PARAM_NAMES, p.tensors()):
+            want = fix[f"v{v}/grad_{name}"]
+            got = t.grad.numpy()[rows]
+            scale = max(np.abs(want).max(), 1e-6)
+            np.testing.assert_allclose(got, want, atol=2e-5 * scale, rtol=1e-4, err_msg=f"{mode} v{v} d{name}")
+        xy = out["projected_means"]
+        np.testing.assert_allclose(xy.grad.numpy()[rows], fix[f"v{v}/means2d_grad"], atol=1e-5, rtol=1e-4)
+        np.testing.assert_allclose(xy.absgrad.numpy()[rows], fix[f"v{v}/absgrad"], atol=1e-5, rtol=1e-4)
+
+
+@pytest.mark.parametrize("mode", ["radegs", "gof", "ambisur"])
+def test_oracle_renderer_matches_reference_torch_renderer(golden, mode):
+    torch.set_num_threads(1)
+    fix = golden(f"render_{mode}")
+    params = params_from(fix)
+    cams = [camera_from(fix, f"cam{v}/") for v in range(3)]
+    _check_render(fix, params, cams, mode, "both", 3)
+
+
+@pytest.mark.parametrize("mode", ["radegs", "gof", "ambisur"])
+def test_oracle_training_profile_matches_reference(golden, mode):
+    torch.set_num_threads(1)
+    fix = golden(f"render_{mode}")
+    params = params_from(fix)
+    cams = [camera_from(fix, "cam0/")]
+    _check_render(golden(f"train_{mode}"), params, cams, mode, oracle_render.training_profile(mode), 1)
+
+
+@pytest.mark.parametrize("mode", ["radegs", "gof"])
+def test_oracle_crop_of_surface_scene(golden, mode):
+    torch.set_num_threads(1)
+    fix = golden(f"crop_{mode}")
+    params = scenes.surfaces(20_000, seed=3)
+    cam = camera_from(fix, "crop/")
+    _check_render(fix, params, [cam], mode, "both", 1, sparse=True)
