@@ -1,0 +1,216 @@
+/*
+ * splatforge_b200 -- C ABI of the B200 (sm_100a) Gaussian-splatting rasterizer.
+ *
+ * Every entry point takes DEVICE pointers (float32, contiguous, row-major), plain
+ * sizes, a cudaStream_t passed as void*, and returns an int status (SF_OK == 0).
+ * On failure the message of the calling thread is available from
+ * sf_b200_last_error().  Nothing here allocates device memory: scratch space is
+ * sized by the *_workspace_bytes() queries and passed in by the caller.  Inputs are
+ * never written.  Kernels run on the given stream; no entry point synchronises the
+ * device except where its comment says so.
+ *
+ * Reference interfaces replaced (paths relative to the SplatForge project):
+ *   gaussian.covariance@1      src/splatforge/providers/torch/gaussian/reference.py:33-35
+ *   gaussian.sh_color@1        src/splatforge/providers/torch/gaussian/reference.py:85-113
+ *   projection + conic/radius/ src/splatforge/studio/renderers.py:76-107,
+ *     SH colour + mode extras  src/splatforge/studio/batched_renderer.py:51-115
+ *   tile binning               src/splatforge/studio/tile_binning.py:10-34 and the
+ *                              bounds host copy batched_renderer.py:121-150
+ *   per-tile evaluation +      src/splatforge/studio/batched_renderer.py:169-338,
+ *     splat.alpha_composite@3  src/splatforge/providers/torch/gaussian/composite_cuda.cu:26-98
+ *   backward (autograd)        same functions, reverse mode
+ *   gaussian.opacity_field@1   src/splatforge/providers/torch/gaussian/reference.py:194-222
+ */
+#ifndef SPLATFORGE_B200_H
+#define SPLATFORGE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SF_B200_ABI_VERSION 1
+
+/* rendering modes: the Studio ``rendering_mode`` (src/splatforge/studio/methods/*.py) */
+enum { SF_MODE_RADEGS = 0, SF_MODE_GOF = 1, SF_MODE_AMBISUR = 2 };
+/* distortion selection bits: splat.alpha_composite@3 ``distortions`` none/l1/l2/both */
+enum { SF_DIST_L1 = 1, SF_DIST_L2 = 2 };
+/* status codes */
+enum {
+  SF_OK = 0,
+  SF_ERR_ARGUMENT = 1,  /* invalid size, pointer or setting */
+  SF_ERR_CUDA = 2,      /* a CUDA runtime call or launch failed */
+  SF_ERR_CAPACITY = 3,  /* caller-provided buffer too small (see message) */
+  SF_ERR_KERNEL = 4     /* a kernel reported an internal error word */
+};
+
+/* floats per Gaussian record written by sf_b200_project_forward and read by the
+ * raster kernels, and per gradient record written by sf_b200_raster_backward */
+#define SF_RECORD_FLOATS 20
+/* floats per pixel of the forward state kept for the backward pass */
+#define SF_PIXEL_STATE_FLOATS 16
+/* floats per stored L1 sample: depth, weight, list position, and the two adjoint
+ * factors written by sf_b200_l1_resolve (stored column-wise, see raster_forward) */
+#define SF_L1_SAMPLE_FLOATS 5
+
+/* Pinhole camera, OpenCV convention (src/splatforge/studio/cameras.py:8-22). */
+typedef struct sf_camera {
+  float R[9];      /* world-to-camera rotation, row-major */
+  float t[3];      /* world-to-camera translation */
+  float K[9];      /* intrinsics, row-major */
+  float Kinv[9];   /* inverse of K (the caller computes it once, on the host) */
+  float origin[3]; /* camera centre in world coordinates: inv(world_to_camera)[:3,3] */
+  int32_t width;
+  int32_t height;
+} sf_camera;
+
+/* The hot-path fields of RenderConfig (src/splatforge/studio/config.py:29-40) plus
+ * the mode / distortion selection of a render call. */
+typedef struct sf_settings {
+  int32_t mode;         /* SF_MODE_* */
+  int32_t distortions;  /* SF_DIST_* bits */
+  int32_t tile_size;    /* must be 16 */
+  int32_t sh_degree;    /* 0..3 */
+  int32_t sh_coeffs;    /* K of sh[N,K,3]; K >= (sh_degree+1)^2 */
+  int32_t antialiased;  /* opacity * sqrt(det(screen)/det(filtered)) */
+  float extent;         /* sigma_extent (3.0), or trunc_sigma for AmbiSuR */
+  float extent_sq;      /* float32(extent**2) as the host computes it (mask squared <= extent^2) */
+  float eps2d;          /* 0.3 */
+  float near_plane;     /* 0.01 */
+  float far_plane;      /* 1e4 */
+  float background[3];
+  float t_stop;         /* a pixel stops once its transmittance falls below this (0: never) */
+} sf_settings;
+
+const char* sf_b200_last_error(void);
+int sf_b200_abi_version(void);
+
+/* ---- gaussian.covariance@1 (reference.py:33-35): cov[N,3,3] = R diag(s^2) R^T ---- */
+int sf_b200_covariance_forward(const float* quats, const float* scales, int64_t n,
+                               float* cov, void* stream);
+/* grad_quats / grad_scales are overwritten (not accumulated). */
+int sf_b200_covariance_backward(const float* quats, const float* scales, int64_t n,
+                                const float* grad_cov, float* grad_quats,
+                                float* grad_scales, void* stream);
+
+/* ---- gaussian.sh_color@1 (reference.py:85-113): rgb[N,3] = max(0, 0.5 + SH(dir)) ---- */
+int sf_b200_sh_color_forward(const float* coeffs, int32_t coeff_count, const float* dirs,
+                             int64_t n, int32_t degree, float* rgb, void* stream);
+/* grad_coeffs [N,K,3] and grad_dirs [N,3] are overwritten; either may be NULL. */
+int sf_b200_sh_color_backward(const float* coeffs, int32_t coeff_count, const float* dirs,
+                              int64_t n, int32_t degree, const float* grad_rgb,
+                              float* grad_coeffs, float* grad_dirs, void* stream);
+
+/* ---- projection, conic, radius, SH colour and mode extras -------------------------
+ * renderers.py:76-107 + batched_renderer.py:57-115.  Per Gaussian writes:
+ *   means2d[N,2], radii[N], records[N,SF_RECORD_FLOATS],
+ *   tile_rect[N,4] (inclusive tile rectangle, int32), tile_count[N] (0 when culled),
+ *   depth_key[N] (float bits of camera z; 0xFFFFFFFF when culled).
+ * selected may be NULL (no ambiguity selection).  nonfinite (device int, may be NULL)
+ * is incremented for every Gaussian whose projected bounds are not finite; such a
+ * Gaussian is culled and the caller raises, as tile_binning.py:17-18 does. */
+int sf_b200_project_forward(const float* means, const float* quats, const float* scales,
+                            const float* opacities, const float* sh, const uint8_t* selected,
+                            int64_t n, const sf_camera* camera, const sf_settings* settings,
+                            float* means2d, float* radii, float* records, int32_t* tile_rect,
+                            int32_t* tile_count, uint32_t* depth_key, int32_t* nonfinite,
+                            void* stream);
+
+/* Reverse of sf_b200_project_forward.  grad_means2d [N,2] is the total adjoint of the
+ * projected means; grad_records [N,SF_RECORD_FLOATS] comes from sf_b200_raster_backward.
+ * Outputs are overwritten; any output may be NULL. */
+int sf_b200_project_backward(const float* means, const float* quats, const float* scales,
+                             const float* opacities, const float* sh, int64_t n,
+                             const sf_camera* camera, const sf_settings* settings,
+                             const float* grad_means2d, const float* grad_records,
+                             float* grad_means, float* grad_quats, float* grad_scales,
+                             float* grad_opacities, float* grad_sh, void* stream);
+
+/* ---- tile binning (tile_binning.py:10-34) ----------------------------------------
+ * Bounds form (x, y, radius, z) per Gaussian, as the reference's host array; used by
+ * the standalone binning entry point and its bit-exact tests.  Writes tile_rect,
+ * tile_count, depth_key exactly like sf_b200_project_forward does. */
+int sf_b200_bin_rects(const float* bounds, int64_t n, int32_t width, int32_t height,
+                      int32_t tile_size, float near_plane, float far_plane,
+                      int32_t* tile_rect, int32_t* tile_count, uint32_t* depth_key,
+                      int32_t* nonfinite, void* stream);
+
+/* Scratch needed by sf_b200_bin_order / sf_b200_bin_emit for n Gaussians, n_isect
+ * intersections and n_tiles tiles. */
+int sf_b200_bin_workspace_bytes(int64_t n, int64_t n_isect, int32_t n_tiles, size_t* bytes);
+
+/* Stable depth order of the Gaussians and the exclusive scan of their tile counts in
+ * that order.  order[N] (Gaussian ids), offsets[N+1] (int64); offsets[N] is the
+ * intersection total, which the caller reads back to size the emit buffers. */
+int sf_b200_bin_order(const int32_t* tile_count, const uint32_t* depth_key, int64_t n,
+                      int32_t* order, int64_t* offsets, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Emits every (tile, Gaussian) intersection in depth order, sorts them stably by tile
+ * and writes per-tile [start,end) ranges.  isect_ids[n_isect] (Gaussian ids, tile-major,
+ * depth order within a tile), tile_ranges[n_tiles,2]. */
+int sf_b200_bin_emit(const int32_t* order, const int64_t* offsets, const int32_t* tile_rect,
+                     int64_t n, int64_t n_isect, int32_t tiles_x, int32_t n_tiles,
+                     int32_t* isect_ids, int32_t* tile_ranges, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* 64-bit keys tile<<32 | depth bits of the sorted intersections (diagnostics/tests). */
+int sf_b200_bin_keys(const int32_t* isect_ids, const int32_t* tile_ranges,
+                     const uint32_t* depth_key, int32_t n_tiles, int64_t n_isect,
+                     uint64_t* keys, void* stream);
+
+/* ---- raster forward (batched_renderer.py:169-338 + alpha_composite@3) -----------
+ * One CTA per 16x16 tile.  Images are HWC float32: rgb/normals [H,W,3], the rest
+ * [H,W].  pixel_state [H*W, SF_PIXEL_STATE_FLOATS] is kept for the backward pass.
+ * L1 (settings->distortions & SF_DIST_L1) stores each pixel's contributing samples in
+ * l1_samples, laid out [SF_L1_SAMPLE_FLOATS, l1_slots]: with l1_offsets == NULL the
+ * 256 pixels of tile t own slots [(t*l1_cap + k)*256 + pixel-in-tile] for k < l1_cap
+ * (l1_slots = n_tiles*l1_cap*256); otherwise pixel p (row-major) owns slots
+ * [l1_offsets[p], l1_offsets[p+1]) and l1_slots = l1_offsets[H*W].  l1_needed (device
+ * int, may be NULL) receives the largest per-pixel sample count; when it exceeds the
+ * capacity the caller reruns the forward with CSR offsets (the L1 result of this
+ * call is then incomplete). */
+int sf_b200_raster_forward(const float* records, int64_t n, const int32_t* isect_ids,
+                           const int32_t* tile_ranges, const sf_camera* camera,
+                           const sf_settings* settings, float* rgb, float* alpha,
+                           float* depth, float* normals, float* distortion_l1,
+                           float* distortion_l2, float* median_depth, float* ray_color,
+                           float* ambiguity, float* pixel_state, float* l1_samples,
+                           int64_t l1_slots, const int64_t* l1_offsets, int32_t l1_cap,
+                           int32_t* l1_needed, void* stream);
+
+/* Per-pixel sample counts (pixel_state column) -> CSR offsets[H*W+1] (int64) for the
+ * rerun of an L1 forward whose capacity was exceeded.  workspace as for binning with
+ * n = H*W. */
+int sf_b200_l1_offsets(const sf_camera* camera, const float* pixel_state, int64_t* offsets,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Sorts every pixel's stored samples by depth, writes distortion_l1 and replaces
+ * each sample by the two factors the backward pass needs. */
+int sf_b200_l1_resolve(const sf_camera* camera, const sf_settings* settings,
+                       float* pixel_state, float* l1_samples, int64_t l1_slots,
+                       const int64_t* l1_offsets, int32_t l1_cap, float* distortion_l1,
+                       void* stream);
+
+/* ---- raster backward ---------------------------------------------------------------
+ * Upstream image adjoints may each be NULL (zero).  grad_records [N,SF_RECORD_FLOATS]
+ * and absgrad [N,2] are ACCUMULATED into (the caller zeroes them); grad_means2d [N,2]
+ * is overwritten with the adjoint of the projected means. */
+int sf_b200_raster_backward(const float* records, int64_t n, const int32_t* isect_ids,
+                            const int32_t* tile_ranges, const sf_camera* camera,
+                            const sf_settings* settings, const float* pixel_state,
+                            const float* l1_samples, int64_t l1_slots,
+                            const int64_t* l1_offsets, int32_t l1_cap,
+                            const float* grad_rgb, const float* grad_alpha,
+                            const float* grad_depth, const float* grad_normals,
+                            const float* grad_l1, const float* grad_l2,
+                            const float* grad_median, const float* grad_ray_color,
+                            const float* grad_ambiguity, float* grad_records,
+                            float* grad_means2d, float* absgrad, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPLATFORGE_B200_H */

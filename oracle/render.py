@@ -51,25 +51,111 @@ CHANNELS = (
 
 
 def project(view, camera, eps2d, near):
-    """World -> camera, EWA Jacobian with the z <= near guard, screen covariance."""
-    R = camera.world_to_camera[:3, :3]
-    m = view.means @ R.T + camera.world_to_camera[:3, 3]
-    cov = ops.covariance(view.quats, view.scales)
-    cov_cam = R @ cov @ R.T
+    """World -> camera, EWA Jacobian with the z <= near guard, screen covariance
+    (renderers.py:76-107).
+
+    Every quantity that feeds a discrete decision downstream (depth order, the
+    tile rectangle, the ``squared <= extent^2`` mask) is evaluated here as a
+    fixed sequence of correctly rounded float32 operations -- sums over the
+    inner index in ascending order, no fused multiply-add -- so that the CUDA
+    kernels, which perform the same sequence with ``__fmul_rn``/``__fadd_rn``,
+    reproduce those decisions bit for bit.  The matrix products are the same
+    products the reference writes with ``@``.
+    """
+    W = camera.world_to_camera
+    R, t = W[:3, :3], W[:3, 3]
+    mu = view.means
+    m = torch.stack(
+        [((R[i, 0] * mu[:, 0] + R[i, 1] * mu[:, 1]) + R[i, 2] * mu[:, 2]) + t[i] for i in range(3)], -1
+    )
+    cov = covariance_explicit(view.quats, view.scales)
+    A = [[(R[i, 0] * cov[:, 0, j] + R[i, 1] * cov[:, 1, j]) + R[i, 2] * cov[:, 2, j] for j in range(3)] for i in range(3)]
+    cov_cam = torch.stack(
+        [torch.stack([(A[i][0] * R[j, 0] + A[i][1] * R[j, 1]) + A[i][2] * R[j, 2] for j in range(3)], -1) for i in range(3)],
+        -2,
+    )
     x, y, z = m.unbind(-1)
     active = z > near
     zs = torch.where(active, z, torch.ones_like(z))
     x = torch.where(active, x, torch.zeros_like(x))
     y = torch.where(active, y, torch.zeros_like(y))
     zero = torch.zeros_like(z)
-    fx, fy = camera.K[0, 0], camera.K[1, 1]
-    J = torch.stack(
-        (fx / zs, zero, -fx * x / zs.square(), zero, fy / zs, -fy * y / zs.square()), -1
-    ).reshape(-1, 2, 3)
-    xy = torch.stack((fx * x / zs + camera.K[0, 2], fy * y / zs + camera.K[1, 2]), -1)
-    screen = J @ cov_cam @ J.transpose(-1, -2)
-    filtered = screen + torch.eye(2, device=m.device, dtype=m.dtype) * eps2d
+    K = camera.K
+    fx, fy = K[0, 0], K[1, 1]
+    zz = zs * zs
+    j00, j02 = fx / zs, (-fx * x) / zz
+    j11, j12 = fy / zs, (-fy * y) / zz
+    J = torch.stack((j00, zero, j02, zero, j11, j12), -1).reshape(-1, 2, 3)
+    xy = torch.stack(((fx * x) / zs + K[0, 2], (fy * y) / zs + K[1, 2]), -1)
+    c = cov_cam
+    T0 = [j00 * c[:, 0, k] + j02 * c[:, 2, k] for k in range(3)]
+    T1 = [j11 * c[:, 1, k] + j12 * c[:, 2, k] for k in range(3)]
+    s00 = T0[0] * j00 + T0[2] * j02
+    s01 = T0[1] * j11 + T0[2] * j12
+    s11 = T1[1] * j11 + T1[2] * j12
+    screen = torch.stack((s00, s01, s01, s11), -1).reshape(-1, 2, 2)
+    filtered = torch.stack((s00 + eps2d, s01, s01, s11 + eps2d), -1).reshape(-1, 2, 2)
     return m, cov_cam, J, xy, screen, filtered
+
+
+def _sqrt_rn(x):
+    """Correctly rounded float32 square root (torch's vectorised float32 sqrt is not
+    always correctly rounded; via float64 it is, since 53 >= 2*24 + 2)."""
+    return x.double().sqrt().to(x.dtype) if x.dtype == torch.float32 else x.sqrt()
+
+
+def covariance_explicit(quats, scales):
+    """``gaussian.covariance@1`` (reference.py:15-35) as explicit float32 sums:
+    ``n = sqrt(((w^2 + x^2) + y^2) + z^2)``, the reference's rotation formula,
+    ``M = R diag(s*s)``, ``C_ij = (M_i0 R_j0 + M_i1 R_j1) + M_i2 R_j2``."""
+    w, x, y, z = quats.unbind(-1)
+    n = _sqrt_rn(((w * w + x * x) + y * y) + z * z).clamp_min(1e-12)
+    w, x, y, z = w / n, x / n, y / n, z / n
+    R = [
+        [1 - 2 * (y * y + z * z), 2 * (x * y - w * z), 2 * (x * z + w * y)],
+        [2 * (x * y + w * z), 1 - 2 * (x * x + z * z), 2 * (y * z - w * x)],
+        [2 * (x * z - w * y), 2 * (y * z + w * x), 1 - 2 * (x * x + y * y)],
+    ]
+    s2 = [scales[:, k] * scales[:, k] for k in range(3)]
+    M = [[R[i][k] * s2[k] for k in range(3)] for i in range(3)]
+    C = [[(M[i][0] * R[j][0] + M[i][1] * R[j][1]) + M[i][2] * R[j][2] for j in range(3)] for i in range(3)]
+    return torch.stack([torch.stack(row, -1) for row in C], -2)
+
+
+def conic_and_radius(filtered, extent):
+    """Explicit 2x2 inverse and largest eigenvalue of the filtered covariance
+    (batched_renderer.py:57-59 writes ``linalg.inv`` and ``eigvalsh``)."""
+    fa, fb, fc = filtered[:, 0, 0], filtered[:, 0, 1], filtered[:, 1, 1]
+    det = fa * fc - fb * fb
+    conic = torch.stack((fc / det, -fb / det, -fb / det, fa / det), -1).reshape(-1, 2, 2)
+    mid = 0.5 * (fa + fc)
+    half = 0.5 * (fa - fc)
+    lam = mid + _sqrt_rn(half * half + fb * fb)
+    return conic, extent * _sqrt_rn(lam.clamp_min(0))
+
+
+def pixel_grid(camera, Kinv, top, left, h, w):
+    """Rays ``inv(K)(u+.5, v+.5, 1)`` and the pixel coordinates ``K ray`` of one
+    tile, as explicit float32 sums (renderers.py:233-234, reference.py:49-56)."""
+    dev, dt = camera.K.device, camera.K.dtype
+    v, u = torch.meshgrid(
+        torch.arange(top, top + h, device=dev, dtype=dt) + 0.5,
+        torch.arange(left, left + w, device=dev, dtype=dt) + 0.5,
+        indexing="ij",
+    )
+    u, v = u.reshape(-1), v.reshape(-1)
+    Ki, K = Kinv, camera.K
+    r = [(u * Ki[i, 0] + v * Ki[i, 1]) + Ki[i, 2] for i in range(3)]
+    px = (r[0] * K[0, 0] + r[1] * K[0, 1]) + r[2] * K[0, 2]
+    py = (r[0] * K[1, 0] + r[1] * K[1, 1]) + r[2] * K[1, 2]
+    return torch.stack(r, -1), torch.stack((px, py), -1)
+
+
+def mahalanobis2(delta, conic):
+    """``delta^T Q delta`` as ``dx (Q delta)_x + dy (Q delta)_y``."""
+    dx, dy = delta[..., 0], delta[..., 1]
+    qa, qb, qc = conic[..., 0, 0], conic[..., 0, 1], conic[..., 1, 1]
+    return dx * (qa * dx + qb * dy) + dy * (qb * dx + qc * dy)
 
 
 def render(
@@ -90,9 +176,8 @@ def render(
     if xy.requires_grad:
         xy.retain_grad()
         xy.absgrad = torch.zeros_like(xy)
-    conic = torch.linalg.inv(filtered)
     extent = trunc_sigma if mode == "ambisur" else s.sigma_extent
-    radii = extent * torch.linalg.eigvalsh(filtered)[:, -1].clamp_min(0).sqrt()
+    conic, radii = conic_and_radius(filtered, extent)
     opacity = view.opacities
     if s.antialiased:
         opacity = opacity * (
@@ -101,7 +186,7 @@ def render(
     origin = camera.origin
     colors = ops.sh_color(view.sh, view.means - origin, degree=view.sh_degree)
     ray_colors = ops.sh_color(view.sh, view.means.detach() - origin, degree=view.sh_degree)
-    rays = ops.pixel_rays(camera.K, width=camera.width, height=camera.height)
+    Kinv = torch.linalg.inv(camera.K.cpu()).to(camera.K.device)
     n = len(m)
     normals = m.new_zeros((n, 3))
     gain = m.new_zeros((n, 2))
@@ -144,9 +229,9 @@ def render(
                 ids_all[offsets[tile_index] : offsets[tile_index + 1]], device=m.device
             )
             tile_index += 1
-            trays = rays[top : top + h, left : left + w].reshape(-1, 3)
+            trays, pix = pixel_grid(camera, Kinv, top, left, h, w)
             out = _tile(
-                ids, trays, camera, xy, conic, colors, ray_colors, opacity, m, normals,
+                ids, trays, pix, camera, xy, conic, colors, ray_colors, opacity, m, normals,
                 gain, qinv, plane, sel, focal, bg, mode, extent, s, distortions,
             )
             row.append(out.reshape(h, w, -1))
@@ -160,12 +245,11 @@ def render(
     return result
 
 
-def _tile(ids, trays, camera, xy, conic, colors, ray_colors, opacity, m, normals,
+def _tile(ids, trays, pix, camera, xy, conic, colors, ray_colors, opacity, m, normals,
           gain, qinv, plane, sel, focal, bg, mode, extent, s, distortions):
     """One tile: [L, P] evaluation, compositing and epilogue (batched_renderer.py:185-338)."""
-    pix = (trays @ camera.K.T)[:, :2]
     delta = pix.unsqueeze(0) - xy[ids][:, None, :]
-    sq = torch.einsum("lpi,lij,lpj->lp", delta, conic[ids], delta)
+    sq = mahalanobis2(delta, conic[ids][:, None])
     P = trays.shape[0]
     if mode == "gof":
         pxy = (xy[ids] - camera.K[:2, 2]) * m[ids, 2:3] / focal

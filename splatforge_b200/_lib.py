@@ -1,0 +1,136 @@
+"""ctypes binding of ``libsf_b200.so`` (the C ABI in include/splatforge_b200.h).
+
+Loading fails loudly when the library is missing: there is no CPU or Torch fallback
+anywhere in this package.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_float, c_int32, c_int64, c_size_t, c_uint8, c_void_p
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libsf_b200.so"
+
+SF_OK = 0
+MODE = {"radegs": 0, "gof": 1, "ambisur": 2}
+DISTORTIONS = {"none": 0, "l1": 1, "l2": 2, "both": 3}
+RECORD_FLOATS = 20
+PIXEL_STATE_FLOATS = 16
+L1_SAMPLE_FLOATS = 5
+
+
+class Camera(ctypes.Structure):
+    _fields_ = [
+        ("R", c_float * 9),
+        ("t", c_float * 3),
+        ("K", c_float * 9),
+        ("Kinv", c_float * 9),
+        ("origin", c_float * 3),
+        ("width", c_int32),
+        ("height", c_int32),
+    ]
+
+
+class Settings(ctypes.Structure):
+    _fields_ = [
+        ("mode", c_int32),
+        ("distortions", c_int32),
+        ("tile_size", c_int32),
+        ("sh_degree", c_int32),
+        ("sh_coeffs", c_int32),
+        ("antialiased", c_int32),
+        ("extent", c_float),
+        ("extent_sq", c_float),
+        ("eps2d", c_float),
+        ("near_plane", c_float),
+        ("far_plane", c_float),
+        ("background", c_float * 3),
+        ("t_stop", c_float),
+    ]
+
+
+P = c_void_p  # every device pointer travels as an untyped address
+_SIGNATURES = {
+    "sf_b200_last_error": (ctypes.c_char_p, []),
+    "sf_b200_abi_version": (ctypes.c_int, []),
+    "sf_b200_covariance_forward": (ctypes.c_int, [P, P, c_int64, P, P]),
+    "sf_b200_covariance_backward": (ctypes.c_int, [P, P, c_int64, P, P, P, P]),
+    "sf_b200_sh_color_forward": (ctypes.c_int, [P, c_int32, P, c_int64, c_int32, P, P]),
+    "sf_b200_sh_color_backward": (ctypes.c_int, [P, c_int32, P, c_int64, c_int32, P, P, P, P]),
+    "sf_b200_project_forward": (
+        ctypes.c_int,
+        [P, P, P, P, P, P, c_int64, POINTER(Camera), POINTER(Settings), P, P, P, P, P, P, P, P],
+    ),
+    "sf_b200_project_backward": (
+        ctypes.c_int,
+        [P, P, P, P, P, c_int64, POINTER(Camera), POINTER(Settings), P, P, P, P, P, P, P, P],
+    ),
+    "sf_b200_bin_rects": (
+        ctypes.c_int,
+        [P, c_int64, c_int32, c_int32, c_int32, c_float, c_float, P, P, P, P, P],
+    ),
+    "sf_b200_bin_workspace_bytes": (ctypes.c_int, [c_int64, c_int64, c_int32, POINTER(c_size_t)]),
+    "sf_b200_bin_order": (ctypes.c_int, [P, P, c_int64, P, P, P, c_size_t, P]),
+    "sf_b200_bin_emit": (
+        ctypes.c_int,
+        [P, P, P, c_int64, c_int64, c_int32, c_int32, P, P, P, c_size_t, P],
+    ),
+    "sf_b200_bin_keys": (ctypes.c_int, [P, P, P, c_int32, c_int64, P, P]),
+    "sf_b200_raster_forward": (
+        ctypes.c_int,
+        [P, c_int64, P, P, POINTER(Camera), POINTER(Settings)]
+        + [P] * 10
+        + [P, c_int64, P, c_int32, P, P],
+    ),
+    "sf_b200_l1_offsets": (ctypes.c_int, [POINTER(Camera), P, P, P, c_size_t, P]),
+    "sf_b200_l1_resolve": (
+        ctypes.c_int,
+        [POINTER(Camera), POINTER(Settings), P, P, c_int64, P, c_int32, P, P],
+    ),
+    "sf_b200_raster_backward": (
+        ctypes.c_int,
+        [P, c_int64, P, P, POINTER(Camera), POINTER(Settings), P, P, c_int64, P, c_int32]
+        + [P] * 9
+        + [P, P, P, P],
+    ),
+}
+
+_lib = None
+
+
+class NativeError(RuntimeError):
+    """A non-zero status from libsf_b200 (message from sf_b200_last_error)."""
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH.name} is not built; run `python -m splatforge_b200.build` "
+                "(the B200 provider has no CPU fallback)"
+            )
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        if handle.sf_b200_abi_version() != 1:
+            raise ImportError("libsf_b200.so ABI version mismatch")
+        _lib = handle
+    return _lib
+
+
+def call(name, *args):
+    rc = getattr(lib(), name)(*args)
+    if rc != SF_OK:
+        msg = lib().sf_b200_last_error().decode(errors="replace")
+        if rc == 1:
+            raise ValueError(f"{name}: {msg}")
+        raise NativeError(f"{name} failed ({rc}): {msg}")
+
+
+def declared_symbols():
+    return sorted(_SIGNATURES)

@@ -1,0 +1,280 @@
+// The extern "C" boundary of libsf_b200.so: argument validation, error strings,
+// launches on the caller's stream.  See include/splatforge_b200.h.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "sf_kernels.h"
+
+namespace {
+
+thread_local char g_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return SF_OK;
+  if (e == cudaErrorInvalidValue)
+    return fail(SF_ERR_ARGUMENT, "%s: invalid size or workspace (%s)", where, cudaGetErrorString(e));
+  return fail(SF_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int check_settings(const sf_settings* st, const char* where) {
+  if (!st) return fail(SF_ERR_ARGUMENT, "%s: settings is NULL", where);
+  if (st->mode < SF_MODE_RADEGS || st->mode > SF_MODE_AMBISUR)
+    return fail(SF_ERR_ARGUMENT, "%s: unsupported rendering mode %d", where, st->mode);
+  if (st->distortions < 0 || st->distortions > 3)
+    return fail(SF_ERR_ARGUMENT, "%s: distortions must be none/l1/l2/both", where);
+  if (st->tile_size != 16) return fail(SF_ERR_ARGUMENT, "%s: tile_size must be 16", where);
+  if (st->sh_degree < 0 || st->sh_degree > 3) return fail(SF_ERR_ARGUMENT, "%s: SH degree must be 0..3", where);
+  if (st->sh_coeffs < (st->sh_degree + 1) * (st->sh_degree + 1) || st->sh_coeffs > 16)
+    return fail(SF_ERR_ARGUMENT, "%s: sh coefficient count %d invalid for degree %d (at most 16)", where,
+                st->sh_coeffs, st->sh_degree);
+  if (!(st->extent > 0.f)) return fail(SF_ERR_ARGUMENT, "%s: extent must be positive", where);
+  return SF_OK;
+}
+
+int check_camera(const sf_camera* c, const char* where) {
+  if (!c) return fail(SF_ERR_ARGUMENT, "%s: camera is NULL", where);
+  if (c->width <= 0 || c->height <= 0) return fail(SF_ERR_ARGUMENT, "%s: width/height must be positive", where);
+  return SF_OK;
+}
+
+int tiles_of(const sf_camera* c, int* tx) {
+  *tx = (c->width + 15) / 16;
+  return *tx * ((c->height + 15) / 16);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* sf_b200_last_error(void) { return g_error; }
+int sf_b200_abi_version(void) { return SF_B200_ABI_VERSION; }
+
+int sf_b200_covariance_forward(const float* quats, const float* scales, int64_t n, float* cov, void* stream) {
+  if (n < 0 || (n > 0 && (!quats || !scales || !cov))) return fail(SF_ERR_ARGUMENT, "covariance_forward: bad arguments");
+  return cuda_status(sf::launch_covariance_forward(quats, scales, n, cov, as_stream(stream)), "covariance_forward");
+}
+
+int sf_b200_covariance_backward(const float* quats, const float* scales, int64_t n, const float* grad_cov,
+                                float* grad_quats, float* grad_scales, void* stream) {
+  if (n < 0 || (n > 0 && (!quats || !scales || !grad_cov))) return fail(SF_ERR_ARGUMENT, "covariance_backward: bad arguments");
+  return cuda_status(sf::launch_covariance_backward(quats, scales, n, grad_cov, grad_quats, grad_scales, as_stream(stream)),
+                     "covariance_backward");
+}
+
+int sf_b200_sh_color_forward(const float* coeffs, int32_t coeff_count, const float* dirs, int64_t n, int32_t degree,
+                             float* rgb, void* stream) {
+  if (degree < 0 || degree > 3) return fail(SF_ERR_ARGUMENT, "sh_color_forward: SH degree must be 0..3");
+  if (coeff_count < (degree + 1) * (degree + 1) || coeff_count > 16)
+    return fail(SF_ERR_ARGUMENT, "sh_color_forward: coefficient count %d invalid for degree %d", coeff_count, degree);
+  if (n < 0 || (n > 0 && (!coeffs || !dirs || !rgb))) return fail(SF_ERR_ARGUMENT, "sh_color_forward: bad arguments");
+  return cuda_status(sf::launch_sh_forward(coeffs, coeff_count, dirs, n, degree, rgb, as_stream(stream)), "sh_color_forward");
+}
+
+int sf_b200_sh_color_backward(const float* coeffs, int32_t coeff_count, const float* dirs, int64_t n, int32_t degree,
+                              const float* grad_rgb, float* grad_coeffs, float* grad_dirs, void* stream) {
+  if (degree < 0 || degree > 3) return fail(SF_ERR_ARGUMENT, "sh_color_backward: SH degree must be 0..3");
+  if (coeff_count < (degree + 1) * (degree + 1) || coeff_count > 16)
+    return fail(SF_ERR_ARGUMENT, "sh_color_backward: coefficient count %d invalid for degree %d", coeff_count, degree);
+  if (n < 0 || (n > 0 && (!coeffs || !dirs || !grad_rgb))) return fail(SF_ERR_ARGUMENT, "sh_color_backward: bad arguments");
+  return cuda_status(sf::launch_sh_backward(coeffs, coeff_count, dirs, n, degree, grad_rgb, grad_coeffs, grad_dirs,
+                                            as_stream(stream)),
+                     "sh_color_backward");
+}
+
+int sf_b200_project_forward(const float* means, const float* quats, const float* scales, const float* opacities,
+                            const float* sh, const uint8_t* selected, int64_t n, const sf_camera* camera,
+                            const sf_settings* settings, float* means2d, float* radii, float* records,
+                            int32_t* tile_rect, int32_t* tile_count, uint32_t* depth_key, int32_t* nonfinite,
+                            void* stream) {
+  int rc;
+  if ((rc = check_settings(settings, "project_forward")) || (rc = check_camera(camera, "project_forward"))) return rc;
+  if (n < 0) return fail(SF_ERR_ARGUMENT, "project_forward: negative count");
+  if (n > 0 && (!means || !quats || !scales || !opacities || !sh || !means2d || !radii || !records || !tile_rect ||
+                !tile_count || !depth_key))
+    return fail(SF_ERR_ARGUMENT, "project_forward: NULL buffer");
+  if (!aligned(quats, 16) || !aligned(records, 16) || !aligned(tile_rect, 16) || !aligned(means2d, 8))
+    return fail(SF_ERR_ARGUMENT, "project_forward: quats/records/tile_rect need 16-byte and means2d 8-byte alignment");
+  return cuda_status(sf::launch_project_forward(means, quats, scales, opacities, sh, selected, n, *camera, *settings,
+                                                means2d, radii, records, tile_rect, tile_count, depth_key, nonfinite,
+                                                as_stream(stream)),
+                     "project_forward");
+}
+
+int sf_b200_project_backward(const float* means, const float* quats, const float* scales, const float* opacities,
+                             const float* sh, int64_t n, const sf_camera* camera, const sf_settings* settings,
+                             const float* grad_means2d, const float* grad_records, float* grad_means, float* grad_quats,
+                             float* grad_scales, float* grad_opacities, float* grad_sh, void* stream) {
+  int rc;
+  if ((rc = check_settings(settings, "project_backward")) || (rc = check_camera(camera, "project_backward"))) return rc;
+  if (n < 0) return fail(SF_ERR_ARGUMENT, "project_backward: negative count");
+  if (n > 0 && (!means || !quats || !scales || !opacities || !sh || !grad_means2d || !grad_records))
+    return fail(SF_ERR_ARGUMENT, "project_backward: NULL buffer");
+  if (!aligned(grad_records, 16) || !aligned(grad_quats, 16))
+    return fail(SF_ERR_ARGUMENT, "project_backward: grad_records/grad_quats need 16-byte alignment");
+  return cuda_status(sf::launch_project_backward(means, quats, scales, opacities, sh, n, *camera, *settings,
+                                                 grad_means2d, grad_records, grad_means, grad_quats, grad_scales,
+                                                 grad_opacities, grad_sh, as_stream(stream)),
+                     "project_backward");
+}
+
+int sf_b200_bin_rects(const float* bounds, int64_t n, int32_t width, int32_t height, int32_t tile_size,
+                      float near_plane, float far_plane, int32_t* tile_rect, int32_t* tile_count,
+                      uint32_t* depth_key, int32_t* nonfinite, void* stream) {
+  if (tile_size != 16) return fail(SF_ERR_ARGUMENT, "bin_rects: tile_size must be 16");
+  if (width <= 0 || height <= 0 || n < 0) return fail(SF_ERR_ARGUMENT, "bin_rects: bad sizes");
+  if (n > 0 && (!bounds || !tile_rect || !tile_count || !depth_key)) return fail(SF_ERR_ARGUMENT, "bin_rects: NULL buffer");
+  if (!aligned(bounds, 16) || !aligned(tile_rect, 16)) return fail(SF_ERR_ARGUMENT, "bin_rects: 16-byte alignment needed");
+  return cuda_status(sf::launch_bin_rects(bounds, n, width, height, tile_size, near_plane, far_plane, tile_rect,
+                                          tile_count, depth_key, nonfinite, as_stream(stream)),
+                     "bin_rects");
+}
+
+int sf_b200_bin_workspace_bytes(int64_t n, int64_t n_isect, int32_t n_tiles, size_t* bytes) {
+  if (n < 0 || n_isect < 0 || n_tiles < 0 || !bytes) return fail(SF_ERR_ARGUMENT, "bin_workspace_bytes: bad arguments");
+  if (n_isect > 0x7fffffffLL || n > 0x7fffffffLL)
+    return fail(SF_ERR_CAPACITY, "bin_workspace_bytes: %lld intersections exceed the 32-bit list index",
+                (long long)n_isect);
+  *bytes = sf::bin_workspace_bytes(n, n_isect, n_tiles);
+  return SF_OK;
+}
+
+int sf_b200_bin_order(const int32_t* tile_count, const uint32_t* depth_key, int64_t n, int32_t* order,
+                      int64_t* offsets, void* workspace, size_t workspace_bytes, void* stream) {
+  if (n < 0 || !offsets || (n > 0 && (!tile_count || !depth_key || !order || !workspace)))
+    return fail(SF_ERR_ARGUMENT, "bin_order: bad arguments");
+  if (workspace_bytes < sf::bin_workspace_bytes(n, 0, 0))
+    return fail(SF_ERR_CAPACITY, "bin_order: workspace of %zu bytes, %zu needed", workspace_bytes,
+                sf::bin_workspace_bytes(n, 0, 0));
+  return cuda_status(sf::bin_order(tile_count, depth_key, n, order, offsets, workspace, workspace_bytes,
+                                   as_stream(stream)),
+                     "bin_order");
+}
+
+int sf_b200_bin_emit(const int32_t* order, const int64_t* offsets, const int32_t* tile_rect, int64_t n,
+                     int64_t n_isect, int32_t tiles_x, int32_t n_tiles, int32_t* isect_ids, int32_t* tile_ranges,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (n < 0 || n_isect < 0 || n_tiles <= 0 || tiles_x <= 0 || !tile_ranges ||
+      (n_isect > 0 && (!order || !offsets || !tile_rect || !isect_ids || !workspace)))
+    return fail(SF_ERR_ARGUMENT, "bin_emit: bad arguments");
+  if (n_isect > 0x7fffffffLL) return fail(SF_ERR_CAPACITY, "bin_emit: too many intersections for 32-bit lists");
+  if (workspace_bytes < sf::bin_workspace_bytes(0, n_isect, n_tiles))
+    return fail(SF_ERR_CAPACITY, "bin_emit: workspace of %zu bytes, %zu needed", workspace_bytes,
+                sf::bin_workspace_bytes(0, n_isect, n_tiles));
+  if (!aligned(tile_rect, 16) || !aligned(tile_ranges, 8)) return fail(SF_ERR_ARGUMENT, "bin_emit: alignment");
+  return cuda_status(sf::bin_emit(order, offsets, tile_rect, n, n_isect, tiles_x, n_tiles, isect_ids, tile_ranges,
+                                  workspace, workspace_bytes, as_stream(stream)),
+                     "bin_emit");
+}
+
+int sf_b200_bin_keys(const int32_t* isect_ids, const int32_t* tile_ranges, const uint32_t* depth_key, int32_t n_tiles,
+                     int64_t n_isect, uint64_t* keys, void* stream) {
+  if (n_tiles < 0 || n_isect < 0 || (n_isect > 0 && (!isect_ids || !tile_ranges || !depth_key || !keys)))
+    return fail(SF_ERR_ARGUMENT, "bin_keys: bad arguments");
+  return cuda_status(sf::bin_keys(isect_ids, tile_ranges, depth_key, n_tiles, n_isect, keys, as_stream(stream)),
+                     "bin_keys");
+}
+
+int sf_b200_raster_forward(const float* records, int64_t n, const int32_t* isect_ids, const int32_t* tile_ranges,
+                           const sf_camera* camera, const sf_settings* settings, float* rgb, float* alpha,
+                           float* depth, float* normals, float* distortion_l1, float* distortion_l2,
+                           float* median_depth, float* ray_color, float* ambiguity, float* pixel_state,
+                           float* l1_samples, int64_t l1_slots, const int64_t* l1_offsets, int32_t l1_cap,
+                           int32_t* l1_needed, void* stream) {
+  int rc;
+  if ((rc = check_settings(settings, "raster_forward")) || (rc = check_camera(camera, "raster_forward"))) return rc;
+  if (!tile_ranges || !rgb || !alpha || !depth || !normals || !distortion_l1 || !distortion_l2 || !median_depth ||
+      !ray_color || !ambiguity || !pixel_state || n < 0 || (n > 0 && !records))
+    return fail(SF_ERR_ARGUMENT, "raster_forward: NULL buffer");
+  int tx;
+  const int n_tiles = tiles_of(camera, &tx);
+  if (settings->distortions & SF_DIST_L1) {
+    if (!l1_samples) return fail(SF_ERR_ARGUMENT, "raster_forward: L1 requested without sample storage");
+    if (!l1_offsets && (l1_cap <= 0 || l1_slots < (int64_t)n_tiles * l1_cap * 256))
+      return fail(SF_ERR_CAPACITY, "raster_forward: L1 storage of %lld slots is smaller than tiles*cap*256",
+                  (long long)l1_slots);
+  }
+  if (!aligned(records, 16)) return fail(SF_ERR_ARGUMENT, "raster_forward: records need 16-byte alignment");
+  sf::RasterFwdArgs a;
+  a.records = records; a.ids = isect_ids; a.ranges = reinterpret_cast<const int2*>(tile_ranges);
+  a.cam = *camera; a.st = *settings; a.tiles_x = tx;
+  a.rgb = rgb; a.alpha = alpha; a.depth = depth; a.normals = normals; a.l1 = distortion_l1; a.l2 = distortion_l2;
+  a.median = median_depth; a.ray_color = ray_color; a.amb = ambiguity; a.state = pixel_state;
+  a.l1s = l1_samples; a.l1_slots = l1_slots; a.l1_off = l1_offsets; a.l1_cap = l1_cap; a.l1_needed = l1_needed;
+  return cuda_status(sf::launch_raster_forward(a, n_tiles, as_stream(stream)), "raster_forward");
+}
+
+int sf_b200_l1_offsets(const sf_camera* camera, const float* pixel_state, int64_t* offsets, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = check_camera(camera, "l1_offsets"))) return rc;
+  if (!pixel_state || !offsets || !workspace) return fail(SF_ERR_ARGUMENT, "l1_offsets: NULL buffer");
+  const int64_t npix = (int64_t)camera->width * camera->height;
+  const size_t need = sf::scan_workspace_bytes(npix);
+  if (workspace_bytes < need) return fail(SF_ERR_CAPACITY, "l1_offsets: workspace of %zu bytes, %zu needed",
+                                          workspace_bytes, need);
+  char* ws = reinterpret_cast<char*>(workspace);
+  const size_t part = need - ((size_t)npix * sizeof(int32_t) + 255) / 256 * 256;
+  int32_t* counts = reinterpret_cast<int32_t*>(ws + part);
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e = sf::launch_pixel_counts(pixel_state, npix, counts, s);
+  if (e == cudaSuccess) e = sf::scan_counts(counts, npix, offsets, ws, part, s);
+  return cuda_status(e, "l1_offsets");
+}
+
+int sf_b200_l1_resolve(const sf_camera* camera, const sf_settings* settings, float* pixel_state, float* l1_samples,
+                       int64_t l1_slots, const int64_t* l1_offsets, int32_t l1_cap, float* distortion_l1,
+                       void* stream) {
+  int rc;
+  if ((rc = check_settings(settings, "l1_resolve")) || (rc = check_camera(camera, "l1_resolve"))) return rc;
+  if (!pixel_state || !l1_samples || !distortion_l1) return fail(SF_ERR_ARGUMENT, "l1_resolve: NULL buffer");
+  return cuda_status(sf::launch_l1_resolve(*camera, *settings, pixel_state, l1_samples, l1_slots, l1_offsets, l1_cap,
+                                           distortion_l1, as_stream(stream)),
+                     "l1_resolve");
+}
+
+int sf_b200_raster_backward(const float* records, int64_t n, const int32_t* isect_ids, const int32_t* tile_ranges,
+                            const sf_camera* camera, const sf_settings* settings, const float* pixel_state,
+                            const float* l1_samples, int64_t l1_slots, const int64_t* l1_offsets, int32_t l1_cap,
+                            const float* grad_rgb, const float* grad_alpha, const float* grad_depth,
+                            const float* grad_normals, const float* grad_l1, const float* grad_l2,
+                            const float* grad_median, const float* grad_ray_color, const float* grad_ambiguity,
+                            float* grad_records, float* grad_means2d, float* absgrad, void* stream) {
+  int rc;
+  if ((rc = check_settings(settings, "raster_backward")) || (rc = check_camera(camera, "raster_backward"))) return rc;
+  if (!tile_ranges || !pixel_state || n < 0 || (n > 0 && (!records || !grad_records || !grad_means2d || !absgrad)))
+    return fail(SF_ERR_ARGUMENT, "raster_backward: NULL buffer");
+  if ((settings->distortions & SF_DIST_L1) && !l1_samples)
+    return fail(SF_ERR_ARGUMENT, "raster_backward: L1 requested without sample storage");
+  if (!aligned(records, 16) || !aligned(grad_records, 16) || !aligned(absgrad, 8) || !aligned(grad_means2d, 8))
+    return fail(SF_ERR_ARGUMENT, "raster_backward: alignment");
+  int tx;
+  const int n_tiles = tiles_of(camera, &tx);
+  sf::RasterBwdArgs a;
+  a.records = records; a.ids = isect_ids; a.ranges = reinterpret_cast<const int2*>(tile_ranges);
+  a.cam = *camera; a.st = *settings; a.tiles_x = tx; a.state = pixel_state;
+  a.l1s = l1_samples; a.l1_slots = l1_slots; a.l1_off = l1_offsets; a.l1_cap = l1_cap;
+  a.g_rgb = grad_rgb; a.g_alpha = grad_alpha; a.g_depth = grad_depth; a.g_normals = grad_normals;
+  a.g_l1 = grad_l1; a.g_l2 = grad_l2; a.g_median = grad_median; a.g_var = grad_ray_color; a.g_amb = grad_ambiguity;
+  a.grad_records = grad_records; a.absgrad = absgrad;
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e = sf::launch_raster_backward(a, n_tiles, s);
+  if (e == cudaSuccess) e = sf::launch_raster_finalize(records, n, *camera, settings->mode, grad_records, grad_means2d, s);
+  return cuda_status(e, "raster_backward");
+}
+
+}  // extern "C"

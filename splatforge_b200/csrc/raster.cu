@@ -1,0 +1,503 @@
+// Tile rasterizer: forward compositing, L1 resolve, reverse-order backward.
+//
+// One CTA per 16x16 tile, one thread per pixel.  Gaussian records of the tile's
+// depth-ordered list are gathered in batches of 256 into shared memory (five 128-bit
+// loads per 80-byte record) and evaluated by every pixel of the tile against the
+// Torch provider's per-tile equations (src/splatforge/studio/batched_renderer.py:
+// 240-338) with front-to-back alpha compositing (splat.alpha_composite@3,
+// src/splatforge/providers/torch/gaussian/reference.py:151-186).
+//
+// There is no alpha threshold: every sample whose Mahalanobis distance passes
+// squared <= extent^2 and near < depth < far contributes, exactly as in the
+// reference.  A pixel stops once its transmittance is below settings.t_stop; the
+// remaining samples could add at most t_stop to any weight sum.
+#include <cuda_runtime.h>
+
+#include "sf_device.cuh"
+#include "sf_grad.cuh"
+#include "sf_kernels.h"
+
+namespace sf {
+
+namespace {
+
+constexpr int REC4 = SF_RECORD_FLOATS / 4;  // float4 per record
+constexpr int ACC = 24;                      // accumulator floats per batch slot (20 + absgrad 2 + pad)
+
+__device__ __forceinline__ int64_t l1_index(int tile, int k, int tid, int cap, const int64_t* off,
+                                            int64_t pix) {
+  return off ? off[pix] + k : ((int64_t)tile * cap + k) * TILE_PIXELS + tid;
+}
+
+// ------------------------------------------------------------------ forward
+template <int MODE, int DIST>
+__global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const RasterFwdArgs a) {
+  __shared__ float4 s_rec[TILE_PIXELS * REC4];
+  __shared__ int s_max;
+  const int tile = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int tx = tile % a.tiles_x, ty = tile / a.tiles_x;
+  const int u = tx * TILE + (tid & 15), v = ty * TILE + (tid >> 4);
+  const int W = a.cam.width, H = a.cam.height;
+  const bool inside = u < W && v < H;
+  PixelRay pr;
+  pixel_ray(a.cam, u, v, pr);
+  const int2 rg = a.ranges[tile];
+  const float ext2 = a.st.extent_sq, nearp = a.st.near_plane, farp = a.st.far_plane;
+  const double t_stop = (double)a.st.t_stop;
+  double Td = 1.0, Wd = 0.0;
+  float C0 = 0.f, C1 = 0.f, C2 = 0.f, D = 0.f, D2 = 0.f, N0 = 0.f, N1 = 0.f, N2 = 0.f;
+  float Dn = 0.f, A = 0.f, Scc = 0.f, med_depth = 0.f;
+  int last = rg.x, med = -1, cnt = 0;
+  bool done = !inside;
+  const int64_t pix = (int64_t)v * W + u;
+  if (tid == 0) s_max = 0;
+  __syncthreads();
+
+  for (int base = rg.x; base < rg.y; base += TILE_PIXELS) {
+    if (__syncthreads_count(done) == TILE_PIXELS) break;
+    const int n_in = min(TILE_PIXELS, rg.y - base);
+    for (int k = tid; k < n_in * REC4; k += TILE_PIXELS) {
+      const int slot = k / REC4, comp = k - slot * REC4;
+      const int id = __ldg(a.ids + base + slot);
+      s_rec[k] = __ldg(reinterpret_cast<const float4*>(a.records) + (int64_t)id * REC4 + comp);
+    }
+    __syncthreads();
+    if (!done) {
+      for (int j = 0; j < n_in; ++j) {
+        const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
+        Sample s;
+        if (!eval_sample<MODE>(rec, pr, ext2, nearp, farp, s)) continue;
+        const int pos = base + j;
+        const float w = s.alpha * (float)Td;
+        const float c0 = rec[R_RGB], c1 = rec[R_RGB + 1], c2 = rec[R_RGB + 2];
+        C0 += w * c0; C1 += w * c1; C2 += w * c2;
+        D += w * s.depth;
+        if (DIST & SF_DIST_L2) D2 += w * s.depth * s.depth;
+        N0 += w * s.n[0]; N1 += w * s.n[1]; N2 += w * s.n[2];
+        A += w * rec[R_SEL];
+        if (MODE == SF_MODE_AMBISUR) {
+          Dn += w * rec[R_PLANE];
+          Scc += w * (c0 * c0 + c1 * c1 + c2 * c2);
+        }
+        Wd += (double)w;
+        if (med < 0 && (float)Wd >= 0.5f) { med = pos; med_depth = s.depth; }
+        if (DIST & SF_DIST_L1) {
+          if (cnt < a.l1_cap || a.l1_off) {
+            const int64_t idx = l1_index(tile, cnt, tid, a.l1_cap, a.l1_off, pix);
+            a.l1s[idx] = s.depth;
+            a.l1s[a.l1_slots + idx] = w;
+            a.l1s[2 * a.l1_slots + idx] = i2f(pos);
+          }
+        }
+        ++cnt;
+        last = pos + 1;
+        Td *= (double)(1.f - s.alpha);
+        if (Td < t_stop) { done = true; break; }
+      }
+    }
+  }
+
+  if (inside) {
+    const float Wf = (float)Wd;
+    const float* bg = a.st.background;
+    const int64_t p3 = pix * 3;
+    a.rgb[p3 + 0] = C0 + (1.f - Wf) * bg[0];
+    a.rgb[p3 + 1] = C1 + (1.f - Wf) * bg[1];
+    a.rgb[p3 + 2] = C2 + (1.f - Wf) * bg[2];
+    a.alpha[pix] = Wf;
+    float expected = D / fmaxr(Wf, 1e-8f);
+    if (MODE == SF_MODE_AMBISUR) {
+      const float den = N0 * pr.r[0] + N1 * pr.r[1] + N2 * pr.r[2];
+      expected = fabsf(den) > 1e-8f ? Dn / den : 0.f;
+    }
+    a.depth[pix] = Wf > 1e-8f ? expected : 0.f;
+    const float nn = fmaxr(sqrtf(N0 * N0 + N1 * N1 + N2 * N2), 1e-12f);
+    a.normals[p3 + 0] = N0 / nn;
+    a.normals[p3 + 1] = N1 / nn;
+    a.normals[p3 + 2] = N2 / nn;
+    const float raw_l2 = (DIST & SF_DIST_L2) ? 2.f * (Wf * D2 - D * D) : 0.f;
+    a.l2[pix] = fmaxr(raw_l2, 0.f);
+    if (!(DIST & SF_DIST_L1)) a.l1[pix] = 0.f;
+    a.median[pix] = med >= 0 ? med_depth : 0.f;
+    a.ray_color[pix] =
+        MODE == SF_MODE_AMBISUR ? Scc - 2.f * (C0 * C0 + C1 * C1 + C2 * C2) + (C0 * C0 + C1 * C1 + C2 * C2) * Wf : 0.f;
+    a.amb[pix] = A;
+    float* st = a.state + pix * SF_PIXEL_STATE_FLOATS;
+    st[PS_T] = (float)Td;
+    st[PS_W] = Wf;
+    st[PS_D] = D;
+    st[PS_D2] = D2;
+    st[PS_C] = C0; st[PS_C + 1] = C1; st[PS_C + 2] = C2;
+    st[PS_N] = N0; st[PS_N + 1] = N1; st[PS_N + 2] = N2;
+    st[PS_DNUM] = Dn;
+    st[PS_L1] = 0.f;
+    st[PS_L2] = raw_l2;
+    st[PS_LAST] = i2f(last);
+    st[PS_MEDIAN] = i2f(med);
+    st[PS_COUNT] = i2f(cnt);
+  }
+  if ((DIST & SF_DIST_L1) && a.l1_needed) {
+    const int m = warp_max(cnt);
+    if ((tid & 31) == 0) atomicMax(&s_max, m);
+    __syncthreads();
+    if (tid == 0) atomicMax(a.l1_needed, s_max);
+  }
+}
+
+// ------------------------------------------------------------------ L1 resolve
+// One warp per pixel: bitonic sort of the stored (depth, sample) pairs in shared
+// memory, warp prefix sums of w and w*d in depth order, then
+//   L1     = sum_i 2 w_i (d_i W_<i - D_<i)
+//   auxw_i = 2 (2 d_i W_<i - d_i W + D - 2 D_<i)     (dL1/dw_i)
+//   auxd_i = 2 w_i (2 W_<i + w_i - W)                 (dL1/dd_i)
+// (composite_cuda.cu:54-65 computes the same factors from torch's sort order).
+// Columns of l1s: 0 depth, 1 weight, 2 list position, 3 auxw, 4 auxd.
+constexpr int L1_WARPS = 4;
+constexpr int L1_SMEM_K = 1024;  // per-warp capacity of the in-shared-memory sort
+
+__global__ void __launch_bounds__(L1_WARPS * 32) l1_resolve_kernel(
+    sf_camera cam, float* state, float* l1s, int64_t slots, const int64_t* off, int cap,
+    float* out_l1) {
+  __shared__ float s_key[L1_WARPS][L1_SMEM_K];
+  __shared__ int s_val[L1_WARPS][L1_SMEM_K];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int64_t npix = (int64_t)cam.width * cam.height;
+  const int tiles_x = (cam.width + TILE - 1) / TILE;
+  const float* col_d = l1s;
+  const float* col_w = l1s + slots;
+  float* col_aw = l1s + 3 * slots;
+  float* col_ad = l1s + 4 * slots;
+  for (int64_t pix = (int64_t)blockIdx.x * L1_WARPS + wid; pix < npix;
+       pix += (int64_t)gridDim.x * L1_WARPS) {
+    float* st = state + pix * SF_PIXEL_STATE_FLOATS;
+    int n = f2i(st[PS_COUNT]);
+    if (!off && n > cap) n = cap;  // over capacity: reported through l1_needed, rerun by the caller
+    const int u = (int)(pix % cam.width), v = (int)(pix / cam.width);
+    const int tile = (v / TILE) * tiles_x + (u / TILE);
+    const int tid = (v % TILE) * TILE + (u % TILE);
+    auto index = [&](int k) { return l1_index(tile, k, tid, cap, off, pix); };
+    float Wt = 0.f, Dt = 0.f;
+    for (int k = lane; k < n; k += 32) {
+      const int64_t i = index(k);
+      Wt += col_w[i]; Dt += col_w[i] * col_d[i];
+    }
+    Wt = warp_sum(Wt); Dt = warp_sum(Dt);
+    float raw = 0.f;
+    if (n <= L1_SMEM_K) {
+      int np = 32;
+      while (np < n) np <<= 1;
+      for (int k = lane; k < np; k += 32) {
+        s_key[wid][k] = k < n ? col_d[index(k)] : __int_as_float(0x7f800000);
+        s_val[wid][k] = k < n ? k : 0x7fffffff;
+      }
+      __syncwarp();
+      for (int size = 2; size <= np; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+          for (int k = lane; k < np; k += 32) {
+            const int partner = k ^ stride;
+            if (partner > k) {
+              const bool asc = (k & size) == 0;
+              const float ka = s_key[wid][k], kb = s_key[wid][partner];
+              const int va = s_val[wid][k], vb = s_val[wid][partner];
+              // order by (depth, compositing index)
+              const bool greater = ka > kb || (ka == kb && va > vb);
+              if (greater == asc) {
+                s_key[wid][k] = kb; s_key[wid][partner] = ka;
+                s_val[wid][k] = vb; s_val[wid][partner] = va;
+              }
+            }
+          }
+          __syncwarp();
+        }
+      }
+      float carry_w = 0.f, carry_wd = 0.f;
+      for (int k0 = 0; k0 < n; k0 += 32) {
+        const int k = k0 + lane;
+        float d = 0.f, w = 0.f;
+        int64_t i = 0;
+        if (k < n) {
+          i = index(s_val[wid][k]);
+          d = s_key[wid][k];
+          w = col_w[i];
+        }
+        float sw = w, swd = w * d;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float a1 = __shfl_up_sync(FULL, sw, o), a2 = __shfl_up_sync(FULL, swd, o);
+          if (lane >= o) { sw += a1; swd += a2; }
+        }
+        const float pw = carry_w + sw - w, pwd = carry_wd + swd - w * d;
+        carry_w += __shfl_sync(FULL, sw, 31);
+        carry_wd += __shfl_sync(FULL, swd, 31);
+        if (k < n) {
+          raw += 2.f * w * (d * pw - pwd);
+          col_aw[i] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
+          col_ad[i] = 2.f * w * (2.f * pw + w - Wt);
+        }
+      }
+      __syncwarp();
+    } else {
+      // rare long lists: ranks straight from global memory, O(n^2) per pixel
+      for (int k = lane; k < n; k += 32) {
+        const int64_t i = index(k);
+        const float d = col_d[i], w = col_w[i];
+        float pw = 0.f, pwd = 0.f;
+        for (int m = 0; m < n; ++m) {
+          const int64_t jm = index(m);
+          const float dm = col_d[jm];
+          if (dm < d || (dm == d && m < k)) { const float wm = col_w[jm]; pw += wm; pwd += wm * dm; }
+        }
+        raw += 2.f * w * (d * pw - pwd);
+        col_aw[i] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
+        col_ad[i] = 2.f * w * (2.f * pw + w - Wt);
+      }
+    }
+    raw = warp_sum(raw);
+    if (lane == 0) {
+      st[PS_L1] = raw;
+      out_l1[pix] = fmaxr(raw, 0.f);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ backward
+template <int MODE, int DIST>
+__global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const RasterBwdArgs a) {
+  __shared__ float4 s_rec[TILE_PIXELS * REC4];
+  __shared__ int s_id[TILE_PIXELS];
+  __shared__ float s_acc[TILE_PIXELS * ACC];
+  __shared__ int s_max;
+  constexpr int NV = SampleLayout<MODE>::NV;
+  const int tile = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int tx = tile % a.tiles_x, ty = tile / a.tiles_x;
+  const int u = tx * TILE + (tid & 15), v = ty * TILE + (tid >> 4);
+  const int W = a.cam.width, H = a.cam.height;
+  const bool inside = u < W && v < H;
+  const int64_t pix = (int64_t)v * W + u;
+  PixelRay pr;
+  pixel_ray(a.cam, u, v, pr);
+  const int2 rg = a.ranges[tile];
+  const float ext2 = a.st.extent_sq, nearp = a.st.near_plane, farp = a.st.far_plane;
+  const float fx = a.cam.K[0], fy = a.cam.K[4];
+
+  PixelGrads pg;
+  float T = 1.f;
+  int last = rg.x, k = -1;
+  if (inside) {
+    const float* st = a.state + pix * SF_PIXEL_STATE_FLOATS;
+    PixelUpstream up;
+    const int64_t p3 = pix * 3;
+    for (int c = 0; c < 3; ++c) {
+      up.rgb[c] = a.g_rgb ? a.g_rgb[p3 + c] : 0.f;
+      up.normal[c] = a.g_normals ? a.g_normals[p3 + c] : 0.f;
+    }
+    up.alpha = a.g_alpha ? a.g_alpha[pix] : 0.f;
+    up.depth = a.g_depth ? a.g_depth[pix] : 0.f;
+    up.l1 = a.g_l1 ? a.g_l1[pix] : 0.f;
+    up.l2 = a.g_l2 ? a.g_l2[pix] : 0.f;
+    up.median = a.g_median ? a.g_median[pix] : 0.f;
+    up.var = a.g_var ? a.g_var[pix] : 0.f;
+    up.amb = a.g_amb ? a.g_amb[pix] : 0.f;
+    pixel_grads(MODE, DIST, st, pr, a.st.background, up, pg);
+    T = st[PS_T];
+    last = f2i(st[PS_LAST]);
+    k = f2i(st[PS_COUNT]) - 1;
+    if (!a.l1_off && k >= a.l1_cap) k = a.l1_cap - 1;  // never read past the pixel's slots
+  } else {
+    pg.gW = pg.gD = pg.gDnum = pg.gA = pg.gL1 = pg.gL2 = pg.gMed = pg.gVar = 0.f;
+    for (int c = 0; c < 3; ++c) pg.gC[c] = pg.gN[c] = pg.C[c] = 0.f;
+    pg.W = pg.D = 0.f;
+    pg.med_pos = -1;
+  }
+  if (tid == 0) s_max = rg.x;
+  __syncthreads();
+  {
+    const int m = warp_max(last);
+    if (lane == 0) atomicMax(&s_max, m);
+  }
+  __syncthreads();
+  const int maxlast = s_max;
+  float S = 0.f;
+
+  for (int hi = maxlast; hi > rg.x; hi -= TILE_PIXELS) {
+    const int lo = max(rg.x, hi - TILE_PIXELS);
+    const int n_in = hi - lo;
+    __syncthreads();
+    for (int q = tid; q < n_in * REC4; q += TILE_PIXELS) {
+      const int slot = q / REC4, comp = q - slot * REC4;
+      const int id = __ldg(a.ids + lo + slot);
+      if (comp == 0) s_id[slot] = id;
+      s_rec[q] = __ldg(reinterpret_cast<const float4*>(a.records) + (int64_t)id * REC4 + comp);
+    }
+    for (int q = tid; q < n_in * ACC; q += TILE_PIXELS) s_acc[q] = 0.f;
+    __syncthreads();
+    for (int j = n_in - 1; j >= 0; --j) {
+      const int pos = lo + j;
+      float vals[NV];
+#pragma unroll
+      for (int q = 0; q < NV; ++q) vals[q] = 0.f;
+      bool act = false;
+      if (pos < last) {
+        const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
+        Sample s;
+        bool contrib;
+        float auxw = 0.f, auxd = 0.f;
+        if (DIST & SF_DIST_L1) {
+          // membership was recorded by the forward pass: the stored list position of
+          // this pixel's k-th contributing sample
+          contrib = false;
+          if (k >= 0) {
+            const int64_t idx = l1_index(tile, k, tid, a.l1_cap, a.l1_off, pix);
+            if (f2i(a.l1s[2 * a.l1_slots + idx]) == pos) {
+              contrib = true;
+              auxw = a.l1s[3 * a.l1_slots + idx];
+              auxd = a.l1s[4 * a.l1_slots + idx];
+              --k;
+              eval_sample<MODE, false>(rec, pr, ext2, nearp, farp, s);
+            }
+          }
+        } else {
+          contrib = eval_sample<MODE>(rec, pr, ext2, nearp, farp, s);
+        }
+        if (contrib && s.alpha > 0.f) {
+          act = true;
+          const float al = s.alpha;
+          const float om = 1.f - al;
+          const float Ti = T / om;
+          const float w = al * Ti;
+          const float adj = sample_adj<MODE>(rec, s, pg, auxw);
+          const float g_alpha = Ti * adj - S / om;
+          S += w * adj;
+          T = Ti;
+          float g_depth = w * pg.gD + (pos == pg.med_pos ? pg.gMed : 0.f) + pg.gL1 * auxd;
+          if (DIST & SF_DIST_L2) g_depth += pg.gL2 * 4.f * w * (pg.W * s.depth - pg.D);
+          sample_backward<MODE>(rec, pr, s, pg, w, g_alpha, g_depth, fx, fy, vals);
+        }
+      }
+      if (__any_sync(FULL, act)) {
+        float v16[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) v16[q] = q < NV ? vals[q] : 0.f;
+        const float r = reduce16_transposed(v16, lane);
+        const int qi = lane >> 1;
+        if ((lane & 1) == 0 && qi < NV && qi < 16 && r != 0.f)
+          atomicAdd(&s_acc[j * ACC + SampleLayout<MODE>::slot(qi)], r);
+#pragma unroll
+        for (int q = 16; q < NV; ++q) {
+          const float t = warp_sum(vals[q]);
+          if (lane == 2 * (q - 16) + 1 && t != 0.f) atomicAdd(&s_acc[j * ACC + SampleLayout<MODE>::slot(q)], t);
+        }
+      }
+    }
+    __syncthreads();
+    for (int q = tid; q < n_in * (ACC / 4); q += TILE_PIXELS) {
+      const int slot = q / (ACC / 4), c4 = q - slot * (ACC / 4);
+      const float4 val = reinterpret_cast<const float4*>(s_acc)[q];
+      if (val.x == 0.f && val.y == 0.f && val.z == 0.f && val.w == 0.f) continue;
+      const int id = s_id[slot];
+      if (c4 < REC4) {
+        atomicAdd(reinterpret_cast<float4*>(a.grad_records + (int64_t)id * SF_RECORD_FLOATS) + c4, val);
+      } else {
+        atomicAdd(reinterpret_cast<float2*>(a.absgrad + (int64_t)id * 2), make_float2(val.x, val.y));
+      }
+    }
+  }
+}
+
+// GOF: proxy_xy = (xy - c) z / f  -> adjoint of the projected means and of camera z;
+// RaDe-GS / AmbiSuR: the delta adjoint already is the projected-mean adjoint.
+__global__ void raster_finalize_kernel(const float* records, int64_t n, sf_camera cam, int mode,
+                                       float* grec, float* gxy) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float* g = grec + i * SF_RECORD_FLOATS;
+  if (mode == SF_MODE_GOF) {
+    const float* r = records + i * SF_RECORD_FLOATS;
+    const float fx = cam.K[0], fy = cam.K[4], cx = cam.K[2], cy = cam.K[5];
+    const float z = r[R_Z];
+    const float gp0 = g[R_PROXY], gp1 = g[R_PROXY + 1], gp2 = g[R_PROXY + 2];
+    gxy[i * 2 + 0] = gp0 * z / fx;
+    gxy[i * 2 + 1] = gp1 * z / fy;
+    g[R_Z] = gp0 * (r[R_X] - cx) / fx + gp1 * (r[R_Y] - cy) / fy + gp2;
+  } else {
+    gxy[i * 2 + 0] = g[R_X];
+    gxy[i * 2 + 1] = g[R_Y];
+  }
+}
+
+__global__ void pixel_counts_kernel(const float* state, int64_t npix, int32_t* counts) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < npix) counts[i] = f2i(state[i * SF_PIXEL_STATE_FLOATS + PS_COUNT]);
+}
+
+template <int MODE>
+cudaError_t fwd_dispatch(const RasterFwdArgs& a, int n_tiles, cudaStream_t s) {
+  switch (a.st.distortions & 3) {
+    case 0: raster_forward_kernel<MODE, 0><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
+    case 1: raster_forward_kernel<MODE, 1><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
+    case 2: raster_forward_kernel<MODE, 2><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
+    default: raster_forward_kernel<MODE, 3><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
+  }
+  return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t bwd_dispatch(const RasterBwdArgs& a, int n_tiles, cudaStream_t s) {
+  switch (a.st.distortions & 3) {
+    case 0: raster_backward_kernel<MODE, 0><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
+    case 1: raster_backward_kernel<MODE, 1><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
+    case 2: raster_backward_kernel<MODE, 2><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
+    default: raster_backward_kernel<MODE, 3><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_raster_forward(const RasterFwdArgs& a, int n_tiles, cudaStream_t s) {
+  if (n_tiles <= 0) return cudaSuccess;
+  switch (a.st.mode) {
+    case SF_MODE_RADEGS: return fwd_dispatch<SF_MODE_RADEGS>(a, n_tiles, s);
+    case SF_MODE_GOF: return fwd_dispatch<SF_MODE_GOF>(a, n_tiles, s);
+    default: return fwd_dispatch<SF_MODE_AMBISUR>(a, n_tiles, s);
+  }
+}
+
+cudaError_t launch_raster_backward(const RasterBwdArgs& a, int n_tiles, cudaStream_t s) {
+  if (n_tiles <= 0) return cudaSuccess;
+  switch (a.st.mode) {
+    case SF_MODE_RADEGS: return bwd_dispatch<SF_MODE_RADEGS>(a, n_tiles, s);
+    case SF_MODE_GOF: return bwd_dispatch<SF_MODE_GOF>(a, n_tiles, s);
+    default: return bwd_dispatch<SF_MODE_AMBISUR>(a, n_tiles, s);
+  }
+}
+
+cudaError_t launch_l1_resolve(const sf_camera& cam, const sf_settings& st, float* state,
+                              float* l1s, int64_t slots, const int64_t* off, int cap,
+                              float* out_l1, cudaStream_t s) {
+  (void)st;
+  const int64_t npix = (int64_t)cam.width * cam.height;
+  if (npix == 0) return cudaSuccess;
+  int64_t blocks = (npix + L1_WARPS - 1) / L1_WARPS;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  l1_resolve_kernel<<<(unsigned)blocks, L1_WARPS * 32, 0, s>>>(cam, state, l1s, slots, off, cap, out_l1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_raster_finalize(const float* records, int64_t n, const sf_camera& cam,
+                                   int mode, float* grad_records, float* grad_means2d,
+                                   cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  raster_finalize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(records, n, cam, mode, grad_records, grad_means2d);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pixel_counts(const float* state, int64_t npix, int32_t* counts, cudaStream_t s) {
+  if (npix == 0) return cudaSuccess;
+  pixel_counts_kernel<<<(unsigned)((npix + 255) / 256), 256, 0, s>>>(state, npix, counts);
+  return cudaGetLastError();
+}
+
+}  // namespace sf

@@ -1,0 +1,92 @@
+// Host-side launchers of the kernels (C++), called by the C ABI layer in capi.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/splatforge_b200.h"
+
+namespace sf {
+
+struct RasterFwdArgs {
+  const float* records;
+  const int32_t* ids;
+  const int2* ranges;
+  sf_camera cam;
+  sf_settings st;
+  int tiles_x;
+  float* rgb; float* alpha; float* depth; float* normals; float* l1; float* l2;
+  float* median; float* ray_color; float* amb;
+  float* state;
+  float* l1s; int64_t l1_slots; const int64_t* l1_off; int l1_cap; int32_t* l1_needed;
+};
+
+struct RasterBwdArgs {
+  const float* records;
+  const int32_t* ids;
+  const int2* ranges;
+  sf_camera cam;
+  sf_settings st;
+  int tiles_x;
+  const float* state;
+  const float* l1s; int64_t l1_slots; const int64_t* l1_off; int l1_cap;
+  const float* g_rgb; const float* g_alpha; const float* g_depth; const float* g_normals;
+  const float* g_l1; const float* g_l2; const float* g_median; const float* g_var;
+  const float* g_amb;
+  float* grad_records;
+  float* absgrad;
+};
+
+cudaError_t launch_raster_forward(const RasterFwdArgs& a, int n_tiles, cudaStream_t s);
+cudaError_t launch_l1_resolve(const sf_camera& cam, const sf_settings& st, float* state,
+                              float* l1s, int64_t l1_slots, const int64_t* l1_off, int l1_cap,
+                              float* out_l1, cudaStream_t s);
+cudaError_t launch_raster_backward(const RasterBwdArgs& a, int n_tiles, cudaStream_t s);
+cudaError_t launch_raster_finalize(const float* records, int64_t n, const sf_camera& cam,
+                                   int mode, float* grad_records, float* grad_means2d,
+                                   cudaStream_t s);
+cudaError_t launch_pixel_counts(const float* state, int64_t npix, int32_t* counts,
+                                cudaStream_t s);
+
+cudaError_t launch_project_forward(const float* means, const float* quats, const float* scales,
+                                   const float* opacities, const float* sh,
+                                   const uint8_t* selected, int64_t n, const sf_camera& cam,
+                                   const sf_settings& st, float* means2d, float* radii,
+                                   float* records, int32_t* rect, int32_t* count,
+                                   uint32_t* depth_key, int32_t* nonfinite, cudaStream_t s);
+cudaError_t launch_project_backward(const float* means, const float* quats, const float* scales,
+                                    const float* opacities, const float* sh, int64_t n,
+                                    const sf_camera& cam, const sf_settings& st,
+                                    const float* gxy, const float* grec, float* g_means,
+                                    float* g_quats, float* g_scales, float* g_opacities,
+                                    float* g_sh, cudaStream_t s);
+cudaError_t launch_covariance_forward(const float* q, const float* s_, int64_t n, float* cov,
+                                      cudaStream_t s);
+cudaError_t launch_covariance_backward(const float* q, const float* s_, int64_t n,
+                                       const float* gcov, float* gq, float* gs, cudaStream_t s);
+cudaError_t launch_sh_forward(const float* coeffs, int K, const float* dirs, int64_t n,
+                              int degree, float* rgb, cudaStream_t s);
+cudaError_t launch_sh_backward(const float* coeffs, int K, const float* dirs, int64_t n,
+                               int degree, const float* grgb, float* gcoeffs, float* gdirs,
+                               cudaStream_t s);
+
+// binning / sorting
+cudaError_t launch_bin_rects(const float* bounds, int64_t n, int width, int height, int tile,
+                             float near_plane, float far_plane, int32_t* rect, int32_t* count,
+                             uint32_t* depth_key, int32_t* nonfinite, cudaStream_t s);
+size_t bin_workspace_bytes(int64_t n, int64_t n_isect, int n_tiles);
+cudaError_t bin_order(const int32_t* count, const uint32_t* depth_key, int64_t n,
+                      int32_t* order, int64_t* offsets, void* ws, size_t ws_bytes,
+                      cudaStream_t s);
+cudaError_t bin_emit(const int32_t* order, const int64_t* offsets, const int32_t* rect,
+                     int64_t n, int64_t n_isect, int tiles_x, int n_tiles, int32_t* ids,
+                     int32_t* ranges, void* ws, size_t ws_bytes, cudaStream_t s);
+cudaError_t bin_keys(const int32_t* ids, const int32_t* ranges, const uint32_t* depth_key,
+                     int n_tiles, int64_t n_isect, uint64_t* keys, cudaStream_t s);
+// exclusive scan int32 -> int64 of n values; out has n+1 entries (out[n] = total)
+cudaError_t scan_counts(const int32_t* in, int64_t n, int64_t* out, void* ws, size_t ws_bytes,
+                        cudaStream_t s);
+size_t scan_workspace_bytes(int64_t n);
+
+}  // namespace sf

@@ -1,0 +1,334 @@
+"""Host orchestration of the B200 rasterizer: autograd functions over the C ABI.
+
+The differentiable path mirrors the Torch provider's composition
+(src/splatforge/studio/batched_renderer.py:45-410):
+
+    (means, quats, scales, opacities, sh)
+        --_Project-->  projected means [N,2] (a real autograd intermediate, so
+                       ``retain_grad()`` works), radii [N], Gaussian records [N,20]
+        --binning-->   per-tile Gaussian lists (device radix sort, one host read of
+                       the intersection count)
+        --_Raster-->   the nine RenderOutput images
+
+The records tensor carries the per-Gaussian values the tile kernels read (projected
+mean, conic, opacity, colour, mode extras); its adjoint is produced by the raster
+backward kernel and consumed by the projection backward kernel.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib
+from ._lib import L1_SAMPLE_FLOATS, PIXEL_STATE_FLOATS, RECORD_FLOATS, Camera, Settings, call
+
+TILE = 16
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def camera_struct(camera):
+    """``Camera`` (src/splatforge/studio/cameras.py:8-22) -> the C ``sf_camera``.
+
+    ``inv(K)`` and the camera centre ``inv(world_to_camera)[:3, 3]`` are evaluated on the
+    host in float32, as the reference's CPU path does.
+    """
+    K = camera.K.detach().to("cpu", torch.float32)
+    W = camera.world_to_camera.detach().to("cpu", torch.float32)
+    Kinv = torch.linalg.inv(K)
+    origin = torch.linalg.inv(W)[:3, 3]
+    c = Camera()
+    c.R[:] = W[:3, :3].reshape(-1).tolist()
+    c.t[:] = W[:3, 3].tolist()
+    c.K[:] = K.reshape(-1).tolist()
+    c.Kinv[:] = Kinv.reshape(-1).tolist()
+    c.origin[:] = origin.tolist()
+    c.width = int(camera.width)
+    c.height = int(camera.height)
+    return c
+
+
+@dataclass
+class RasterSettings:
+    """Render-time configuration (RenderConfig fields of src/splatforge/studio/config.py:29-40)."""
+
+    mode: str = "gof"
+    distortions: str = "both"
+    sigma_extent: float = 3.0
+    trunc_sigma: float = 2.0
+    eps2d: float = 0.3
+    near: float = 0.01
+    far: float = 10000.0
+    background: tuple = (1.0, 1.0, 1.0)
+    antialiased: bool = False
+    tile_size: int = 16
+    transmittance_floor: float = 1e-6
+    l1_capacity: int = 48
+
+    def extent(self):
+        return self.trunc_sigma if self.mode == "ambisur" else self.sigma_extent
+
+    def struct(self, sh_degree, sh_coeffs):
+        if self.mode not in _lib.MODE:
+            raise ValueError(f"unsupported rendering mode: {self.mode}")
+        if self.distortions not in _lib.DISTORTIONS:
+            raise ValueError("distortions must explicitly be none, l1, l2 or both")
+        if self.tile_size != TILE:
+            raise ValueError("the B200 rasterizer uses 16x16 tiles")
+        s = Settings()
+        s.mode = _lib.MODE[self.mode]
+        s.distortions = _lib.DISTORTIONS[self.distortions]
+        s.tile_size = TILE
+        s.sh_degree = int(sh_degree)
+        s.sh_coeffs = int(sh_coeffs)
+        s.antialiased = int(bool(self.antialiased))
+        ext = float(self.extent())
+        s.extent = ext
+        s.extent_sq = float(torch.tensor(ext**2, dtype=torch.float32))
+        s.eps2d = float(self.eps2d)
+        s.near_plane = float(self.near)
+        s.far_plane = float(self.far)
+        s.background[:] = [float(v) for v in self.background]
+        s.t_stop = float(self.transmittance_floor)
+        return s
+
+
+@dataclass
+class _Plan:
+    cam: Camera
+    settings: Settings
+    n: int
+    device: torch.device
+    selected: torch.Tensor | None = None
+    rect: torch.Tensor | None = None
+    count: torch.Tensor | None = None
+    depth_key: torch.Tensor | None = None
+    nonfinite: torch.Tensor | None = None
+    ids: torch.Tensor | None = None
+    ranges: torch.Tensor | None = None
+    n_isect: int = 0
+    absgrad: torch.Tensor | None = None
+    l1_capacity: int = 48
+    stats: dict = field(default_factory=dict)
+
+    @property
+    def tiles_x(self):
+        return (self.cam.width + TILE - 1) // TILE
+
+    @property
+    def n_tiles(self):
+        return self.tiles_x * ((self.cam.height + TILE - 1) // TILE)
+
+
+def _check_inputs(tensors, names):
+    dev = tensors[0].device
+    if dev.type != "cuda":
+        raise ValueError("the B200 rasterizer requires CUDA tensors; there is no CPU fallback")
+    for t, name in zip(tensors, names):
+        if t.dtype != torch.float32:
+            raise ValueError(f"{name}: the B200 rasterizer requires float32 (got {t.dtype})")
+        if t.device != dev:
+            raise ValueError("tensor dtype/device must match explicitly")
+    return dev
+
+
+class _Project(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means, quats, scales, opacities, sh, plan):
+        n = plan.n
+        dev = plan.device
+        means, quats, scales, opacities, sh = (
+            t.contiguous() for t in (means, quats, scales, opacities, sh)
+        )
+        means2d = torch.empty((n, 2), device=dev, dtype=torch.float32)
+        radii = torch.empty((n,), device=dev, dtype=torch.float32)
+        records = torch.empty((n, RECORD_FLOATS), device=dev, dtype=torch.float32)
+        plan.rect = torch.empty((n, 4), device=dev, dtype=torch.int32)
+        plan.count = torch.empty((n,), device=dev, dtype=torch.int32)
+        plan.depth_key = torch.empty((n,), device=dev, dtype=torch.int32)
+        plan.nonfinite = torch.zeros((1,), device=dev, dtype=torch.int32)
+        call(
+            "sf_b200_project_forward",
+            _ptr(means), _ptr(quats), _ptr(scales), _ptr(opacities), _ptr(sh), _ptr(plan.selected),
+            n, ctypes.byref(plan.cam), ctypes.byref(plan.settings),
+            _ptr(means2d), _ptr(radii), _ptr(records), _ptr(plan.rect), _ptr(plan.count),
+            _ptr(plan.depth_key), _ptr(plan.nonfinite), _stream(dev),
+        )
+        ctx.save_for_backward(means, quats, scales, opacities, sh)
+        ctx.plan = plan
+        ctx.mark_non_differentiable(radii)
+        return means2d, radii, records
+
+    @staticmethod
+    def backward(ctx, g_means2d, g_radii, g_records):
+        means, quats, scales, opacities, sh = ctx.saved_tensors
+        plan = ctx.plan
+        n, dev = plan.n, plan.device
+        g_means2d = (
+            torch.zeros((n, 2), device=dev) if g_means2d is None else g_means2d.contiguous()
+        )
+        g_records = (
+            torch.zeros((n, RECORD_FLOATS), device=dev)
+            if g_records is None
+            else g_records.contiguous()
+        )
+        need = ctx.needs_input_grad
+        outs = [
+            torch.empty_like(t) if need[i] else None
+            for i, t in enumerate((means, quats, scales, opacities, sh))
+        ]
+        call(
+            "sf_b200_project_backward",
+            _ptr(means), _ptr(quats), _ptr(scales), _ptr(opacities), _ptr(sh), n,
+            ctypes.byref(plan.cam), ctypes.byref(plan.settings), _ptr(g_means2d), _ptr(g_records),
+            *(_ptr(o) for o in outs), _stream(dev),
+        )
+        return (*outs, None)
+
+
+def bin_gaussians(plan):
+    """Device tile binning; one host read (intersection count + non-finite flag)."""
+    n, dev = plan.n, plan.device
+    size = ctypes.c_size_t()
+    call("sf_b200_bin_workspace_bytes", n, 0, plan.n_tiles, ctypes.byref(size))
+    ws = torch.empty((max(size.value, 1),), device=dev, dtype=torch.uint8)
+    order = torch.empty((n,), device=dev, dtype=torch.int32)
+    offsets = torch.empty((n + 1,), device=dev, dtype=torch.int64)
+    call(
+        "sf_b200_bin_order", _ptr(plan.count), _ptr(plan.depth_key), n, _ptr(order), _ptr(offsets),
+        _ptr(ws), size.value, _stream(dev),
+    )
+    total, bad = torch.stack((offsets[n], plan.nonfinite[0].to(torch.int64))).tolist()
+    if bad:
+        raise FloatingPointError("non-finite projected bounds")
+    plan.n_isect = int(total)
+    call("sf_b200_bin_workspace_bytes", n, plan.n_isect, plan.n_tiles, ctypes.byref(size))
+    if size.value > ws.numel():
+        ws = torch.empty((size.value,), device=dev, dtype=torch.uint8)
+    plan.ids = torch.empty((max(plan.n_isect, 1),), device=dev, dtype=torch.int32)
+    plan.ranges = torch.empty((plan.n_tiles, 2), device=dev, dtype=torch.int32)
+    call(
+        "sf_b200_bin_emit", _ptr(order), _ptr(offsets), _ptr(plan.rect), n, plan.n_isect,
+        plan.tiles_x, plan.n_tiles, _ptr(plan.ids), _ptr(plan.ranges), _ptr(ws), size.value,
+        _stream(dev),
+    )
+    return plan
+
+
+class _Raster(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means2d, records, plan):
+        dev = plan.device
+        H, W = plan.cam.height, plan.cam.width
+        f = dict(device=dev, dtype=torch.float32)
+        rgb = torch.empty((H, W, 3), **f)
+        alpha = torch.empty((H, W, 1), **f)
+        depth = torch.empty((H, W, 1), **f)
+        normals = torch.empty((H, W, 3), **f)
+        l1 = torch.empty((H, W, 1), **f)
+        l2 = torch.empty((H, W, 1), **f)
+        median = torch.empty((H, W, 1), **f)
+        ray_color = torch.empty((H, W, 1), **f)
+        amb = torch.empty((H, W, 1), **f)
+        state = torch.empty((H * W, PIXEL_STATE_FLOATS), **f)
+        records = records.contiguous()
+        use_l1 = bool(plan.settings.distortions & 1)
+        l1s, l1_off, cap, slots = None, None, 0, 0
+        needed = None
+        if use_l1:
+            cap = int(plan.l1_capacity)
+            slots = plan.n_tiles * cap * TILE * TILE
+            l1s = torch.empty((L1_SAMPLE_FLOATS, slots), **f)
+            needed = torch.zeros((1,), device=dev, dtype=torch.int32)
+
+        def run():
+            call(
+                "sf_b200_raster_forward", _ptr(records), plan.n, _ptr(plan.ids), _ptr(plan.ranges),
+                ctypes.byref(plan.cam), ctypes.byref(plan.settings),
+                _ptr(rgb), _ptr(alpha), _ptr(depth), _ptr(normals), _ptr(l1), _ptr(l2), _ptr(median),
+                _ptr(ray_color), _ptr(amb), _ptr(state), _ptr(l1s), slots, _ptr(l1_off), cap,
+                _ptr(needed), _stream(dev),
+            )
+
+        run()
+        if use_l1:
+            most = int(needed.item())
+            plan.stats["l1_max_samples"] = most
+            if most > cap:
+                # capacity exceeded somewhere: exact per-pixel (CSR) storage and a rerun
+                ws_bytes = (H * W + 2048) * 8 + H * W * 4 + 4096
+                ws = torch.empty((ws_bytes,), device=dev, dtype=torch.uint8)
+                l1_off = torch.empty((H * W + 1,), device=dev, dtype=torch.int64)
+                call("sf_b200_l1_offsets", ctypes.byref(plan.cam), _ptr(state), _ptr(l1_off),
+                     _ptr(ws), ws_bytes, _stream(dev))
+                slots = int(l1_off[H * W].item())
+                l1s = torch.empty((L1_SAMPLE_FLOATS, max(slots, 1)), **f)
+                run()
+            call(
+                "sf_b200_l1_resolve", ctypes.byref(plan.cam), ctypes.byref(plan.settings), _ptr(state),
+                _ptr(l1s), slots, _ptr(l1_off), cap, _ptr(l1), _stream(dev),
+            )
+        ctx.save_for_backward(records)
+        ctx.plan = plan
+        ctx.state = state
+        ctx.l1 = (l1s, slots, l1_off, cap)
+        return rgb, alpha, depth, normals, l1, l2, median, ray_color, amb
+
+    @staticmethod
+    def backward(ctx, g_rgb, g_alpha, g_depth, g_normals, g_l1, g_l2, g_median, g_var, g_amb):
+        (records,) = ctx.saved_tensors
+        plan = ctx.plan
+        dev, n = plan.device, plan.n
+        grads = [
+            None if g is None else g.contiguous()
+            for g in (g_rgb, g_alpha, g_depth, g_normals, g_l1, g_l2, g_median, g_var, g_amb)
+        ]
+        grad_records = torch.zeros((n, RECORD_FLOATS), device=dev, dtype=torch.float32)
+        grad_means2d = torch.empty((n, 2), device=dev, dtype=torch.float32)
+        absgrad = plan.absgrad if plan.absgrad is not None else torch.zeros((n, 2), device=dev)
+        l1s, slots, l1_off, cap = ctx.l1
+        call(
+            "sf_b200_raster_backward", _ptr(records), n, _ptr(plan.ids), _ptr(plan.ranges),
+            ctypes.byref(plan.cam), ctypes.byref(plan.settings), _ptr(ctx.state), _ptr(l1s), slots,
+            _ptr(l1_off), cap, *(_ptr(g) for g in grads), _ptr(grad_records), _ptr(grad_means2d),
+            _ptr(absgrad), _stream(dev),
+        )
+        return grad_means2d, grad_records, None
+
+
+def rasterize(means, quats, scales, opacities, sh, sh_degree, camera, settings, *, selected=None):
+    """One differentiable render.  Returns a dict of the nine images plus
+    ``projected_means`` (with ``.absgrad`` when it requires grad) and ``projected_radii``."""
+    dev = _check_inputs((means, quats, scales, opacities, sh), ("means", "quats", "scales", "opacities", "sh"))
+    n = means.shape[0]
+    if sh.ndim != 3 or sh.shape[0] != n or sh.shape[2] != 3:
+        raise ValueError("sh must be [N, K, 3]")
+    with torch.cuda.device(dev):
+        plan = _Plan(camera_struct(camera), settings.struct(sh_degree, sh.shape[1]), n, dev)
+        plan.l1_capacity = settings.l1_capacity
+        if selected is not None:
+            plan.selected = selected.to(device=dev, dtype=torch.uint8).contiguous()
+        means2d, radii, records = _Project.apply(means, quats, scales, opacities, sh, plan)
+        if means2d.requires_grad:
+            means2d.retain_grad()
+            means2d.absgrad = torch.zeros_like(means2d)
+            plan.absgrad = means2d.absgrad
+        bin_gaussians(plan)
+        images = _Raster.apply(means2d, records, plan)
+    names = ("rgb", "alpha", "depth", "normals", "distortion_l1", "distortion_l2",
+             "median_depth", "ray_color", "ambiguity_mask")
+    out = dict(zip(names, images))
+    out["projected_means"] = means2d
+    out["projected_radii"] = radii
+    out["n_isect"] = plan.n_isect
+    out["stats"] = plan.stats
+    return out
