@@ -86,6 +86,8 @@ typedef struct sf_settings {
 
 const char* sf_b200_last_error(void);
 int sf_b200_abi_version(void);
+/* Running total of kernels this library has launched in the process (diagnostics). */
+int64_t sf_b200_kernel_launches(void);
 
 /* ---- gaussian.covariance@1 (reference.py:33-35): cov[N,3,3] = R diag(s^2) R^T ---- */
 int sf_b200_covariance_forward(const float* quats, const float* scales, int64_t n,
@@ -171,7 +173,8 @@ int sf_b200_bin_keys(const int32_t* isect_ids, const int32_t* tile_ranges,
  * [l1_offsets[p], l1_offsets[p+1]) and l1_slots = l1_offsets[H*W].  l1_needed (device
  * int, may be NULL) receives the largest per-pixel sample count; when it exceeds the
  * capacity the caller reruns the forward with CSR offsets (the L1 result of this
- * call is then incomplete). */
+ * call is then incomplete).  counters (device int64[2], may be NULL) accumulate the
+ * (pixel, Gaussian) pairs evaluated and the pairs that contributed. */
 int sf_b200_raster_forward(const float* records, int64_t n, const int32_t* isect_ids,
                            const int32_t* tile_ranges, const sf_camera* camera,
                            const sf_settings* settings, float* rgb, float* alpha,
@@ -179,7 +182,7 @@ int sf_b200_raster_forward(const float* records, int64_t n, const int32_t* isect
                            float* distortion_l2, float* median_depth, float* ray_color,
                            float* ambiguity, float* pixel_state, float* l1_samples,
                            int64_t l1_slots, const int64_t* l1_offsets, int32_t l1_cap,
-                           int32_t* l1_needed, void* stream);
+                           int32_t* l1_needed, int64_t* counters, void* stream);
 
 /* Per-pixel sample counts (pixel_state column) -> CSR offsets[H*W+1] (int64) for the
  * rerun of an L1 forward whose capacity was exceeded.  workspace as for binning with

@@ -55,6 +55,7 @@ P = c_void_p  # every device pointer travels as an untyped address
 _SIGNATURES = {
     "sf_b200_last_error": (ctypes.c_char_p, []),
     "sf_b200_abi_version": (ctypes.c_int, []),
+    "sf_b200_kernel_launches": (ctypes.c_int64, []),
     "sf_b200_covariance_forward": (ctypes.c_int, [P, P, c_int64, P, P]),
     "sf_b200_covariance_backward": (ctypes.c_int, [P, P, c_int64, P, P, P, P]),
     "sf_b200_sh_color_forward": (ctypes.c_int, [P, c_int32, P, c_int64, c_int32, P, P]),
@@ -82,7 +83,7 @@ _SIGNATURES = {
         ctypes.c_int,
         [P, c_int64, P, P, POINTER(Camera), POINTER(Settings)]
         + [P] * 10
-        + [P, c_int64, P, c_int32, P, P],
+        + [P, c_int64, P, c_int32, P, P, P],
     ),
     "sf_b200_l1_offsets": (ctypes.c_int, [POINTER(Camera), P, P, P, c_size_t, P]),
     "sf_b200_l1_resolve": (

@@ -117,6 +117,7 @@ cudaError_t exclusive_scan(const TI* in, int64_t n, TO* out, TO* partial, TO* gr
   }
   if (n > SC_MAX) return cudaErrorInvalidValue;
   const int64_t nb = scan_blocks(n);
+  count_launches(3);
   scan_reduce_kernel<TI, TO><<<(unsigned)nb, SC_THREADS, 0, s>>>(in, n, partial);
   scan_top_kernel<TO><<<1, SC_TOP_THREADS, 0, s>>>(partial, nb, grand);
   scan_down_kernel<TI, TO><<<(unsigned)nb, SC_THREADS, 0, s>>>(in, n, partial, out);
@@ -222,6 +223,7 @@ cudaError_t radix_sort(uint32_t* k0, int32_t* v0, uint32_t* k1, int32_t* v1, int
   for (int p = 0; p < passes && n > 0; ++p) {
     const int shift = 8 * p;
     int32_t* vdst = (p == passes - 1 && v_out) ? v_out : vo;
+    count_launches(2);
     radix_upsweep_kernel<<<(unsigned)nb, RS_THREADS, 0, s>>>(ki, n, shift, (int)nb, sc.hist);
     cudaError_t e = exclusive_scan<uint32_t, uint32_t>(sc.hist, RADIX * nb, sc.hist, sc.partial, nullptr, s);
     if (e != cudaSuccess) return e;
@@ -360,10 +362,12 @@ cudaError_t bin_order(const int32_t* count, const uint32_t* depth_key, int64_t n
   sc.hist = c.take<uint32_t>(RADIX * radix_blocks(n));
   sc.partial = c.take<uint32_t>(scan_blocks(RADIX * radix_blocks(n)) + 1);
   int64_t* spart = c.take<int64_t>(scan_blocks(n) + 1);
+  count_launches(1);
   iota_copy_kernel<<<grid_for(n, 256), 256, 0, s>>>(depth_key, n, kA, vA);
   uint32_t* kf; int32_t* vf;
   cudaError_t e = radix_sort(kA, vA, kB, vB, n, 32, sc, &kf, &vf, nullptr, s);
   if (e != cudaSuccess) return e;
+  count_launches(1);
   gather_counts_kernel<<<grid_for(n, 256), 256, 0, s>>>(vf, count, n, order, cs);
   return exclusive_scan<int32_t, int64_t>(cs, n, offsets, spart, offsets + n, s);
 }
@@ -382,12 +386,14 @@ cudaError_t bin_emit(const int32_t* order, const int64_t* offsets, const int32_t
   RadixScratch sc;
   sc.hist = c.take<uint32_t>(RADIX * radix_blocks(m));
   sc.partial = c.take<uint32_t>(scan_blocks(RADIX * radix_blocks(m)) + 1);
+  count_launches(1);
   emit_kernel<<<grid_for(n, 256), 256, 0, s>>>(order, offsets, rect, n, tiles_x, tA, vA);
   int bits = 1;
   while ((1 << bits) < n_tiles) ++bits;
   uint32_t* kf; int32_t* vf;
   e = radix_sort(tA, vA, tB, vB, m, bits, sc, &kf, &vf, ids, s);
   if (e != cudaSuccess) return e;
+  count_launches(1);
   ranges_kernel<<<grid_for(m, 256), 256, 0, s>>>(kf, m, reinterpret_cast<int2*>(ranges));
   return cudaGetLastError();
 }
@@ -396,6 +402,7 @@ cudaError_t bin_keys(const int32_t* ids, const int32_t* ranges, const uint32_t* 
                      int n_tiles, int64_t m, uint64_t* keys, cudaStream_t s) {
   (void)m;
   if (n_tiles == 0) return cudaSuccess;
+  count_launches(1);
   keys_kernel<<<n_tiles, 128, 0, s>>>(ids, reinterpret_cast<const int2*>(ranges), depth_key, n_tiles, keys);
   return cudaGetLastError();
 }

@@ -6,7 +6,17 @@
 #include <cstdio>
 #include <cstring>
 
+#include <atomic>
+
 #include "sf_kernels.h"
+
+namespace sf {
+namespace {
+std::atomic<int64_t> g_launches{0};
+}
+void count_launches(int k) { g_launches.fetch_add(k, std::memory_order_relaxed); }
+int64_t launches_total() { return g_launches.load(std::memory_order_relaxed); }
+}  // namespace sf
 
 namespace {
 
@@ -63,6 +73,7 @@ extern "C" {
 
 const char* sf_b200_last_error(void) { return g_error; }
 int sf_b200_abi_version(void) { return SF_B200_ABI_VERSION; }
+int64_t sf_b200_kernel_launches(void) { return sf::launches_total(); }
 
 int sf_b200_covariance_forward(const float* quats, const float* scales, int64_t n, float* cov, void* stream) {
   if (n < 0 || (n > 0 && (!quats || !scales || !cov))) return fail(SF_ERR_ARGUMENT, "covariance_forward: bad arguments");
@@ -194,7 +205,7 @@ int sf_b200_raster_forward(const float* records, int64_t n, const int32_t* isect
                            float* depth, float* normals, float* distortion_l1, float* distortion_l2,
                            float* median_depth, float* ray_color, float* ambiguity, float* pixel_state,
                            float* l1_samples, int64_t l1_slots, const int64_t* l1_offsets, int32_t l1_cap,
-                           int32_t* l1_needed, void* stream) {
+                           int32_t* l1_needed, int64_t* counters, void* stream) {
   int rc;
   if ((rc = check_settings(settings, "raster_forward")) || (rc = check_camera(camera, "raster_forward"))) return rc;
   if (!tile_ranges || !rgb || !alpha || !depth || !normals || !distortion_l1 || !distortion_l2 || !median_depth ||
@@ -215,6 +226,8 @@ int sf_b200_raster_forward(const float* records, int64_t n, const int32_t* isect
   a.rgb = rgb; a.alpha = alpha; a.depth = depth; a.normals = normals; a.l1 = distortion_l1; a.l2 = distortion_l2;
   a.median = median_depth; a.ray_color = ray_color; a.amb = ambiguity; a.state = pixel_state;
   a.l1s = l1_samples; a.l1_slots = l1_slots; a.l1_off = l1_offsets; a.l1_cap = l1_cap; a.l1_needed = l1_needed;
+  a.counters = reinterpret_cast<unsigned long long*>(counters);
+  if (counters && !aligned(counters, 8)) return fail(SF_ERR_ARGUMENT, "raster_forward: counters alignment");
   return cuda_status(sf::launch_raster_forward(a, n_tiles, as_stream(stream)), "raster_forward");
 }
 

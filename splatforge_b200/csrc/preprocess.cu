@@ -224,6 +224,7 @@ cudaError_t launch_project_forward(const float* means, const float* quats, const
                                    uint32_t* depth_key, int32_t* nonfinite, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
   const size_t smem = (size_t)PB * st.sh_coeffs * 3 * sizeof(float);
+  count_launches(1);
   project_forward_kernel<<<blocks_for(n, PB), PB, smem, s>>>(
       means, quats, scales, opacities, sh, selected, n, cam, st, means2d, radii, records, rect,
       count, depth_key, nonfinite);
@@ -238,6 +239,7 @@ cudaError_t launch_project_backward(const float* means, const float* quats, cons
                                     float* g_sh, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
   const size_t smem = (size_t)PB * st.sh_coeffs * 3 * sizeof(float);
+  count_launches(1);
   project_backward_kernel<<<blocks_for(n, PB), PB, smem, s>>>(
       means, quats, scales, opacities, sh, n, cam, st, gxy, grec, g_means, g_quats, g_scales,
       g_opacities, g_sh);
@@ -247,6 +249,7 @@ cudaError_t launch_project_backward(const float* means, const float* quats, cons
 cudaError_t launch_covariance_forward(const float* q, const float* s_, int64_t n, float* cov,
                                       cudaStream_t s) {
   if (n == 0) return cudaSuccess;
+  count_launches(1);
   covariance_forward_kernel<<<blocks_for(n, 256), 256, 0, s>>>(q, s_, n, cov);
   return cudaGetLastError();
 }
@@ -254,6 +257,7 @@ cudaError_t launch_covariance_forward(const float* q, const float* s_, int64_t n
 cudaError_t launch_covariance_backward(const float* q, const float* s_, int64_t n,
                                        const float* gcov, float* gq, float* gs, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
+  count_launches(1);
   covariance_backward_kernel<<<blocks_for(n, 256), 256, 0, s>>>(q, s_, n, gcov, gq, gs);
   return cudaGetLastError();
 }
@@ -261,6 +265,7 @@ cudaError_t launch_covariance_backward(const float* q, const float* s_, int64_t 
 cudaError_t launch_sh_forward(const float* coeffs, int K, const float* dirs, int64_t n,
                               int degree, float* rgb, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
+  count_launches(1);
   sh_forward_kernel<<<blocks_for(n, 256), 256, 0, s>>>(coeffs, K, dirs, n, degree, rgb);
   return cudaGetLastError();
 }
@@ -269,6 +274,7 @@ cudaError_t launch_sh_backward(const float* coeffs, int K, const float* dirs, in
                                int degree, const float* grgb, float* gcoeffs, float* gdirs,
                                cudaStream_t s) {
   if (n == 0) return cudaSuccess;
+  count_launches(1);
   sh_backward_kernel<<<blocks_for(n, 256), 256, 0, s>>>(coeffs, K, dirs, n, degree, grgb, gcoeffs, gdirs);
   return cudaGetLastError();
 }
@@ -278,6 +284,7 @@ cudaError_t launch_bin_rects(const float* bounds, int64_t n, int width, int heig
                              uint32_t* depth_key, int32_t* nonfinite, cudaStream_t s) {
   (void)tile;
   if (n == 0) return cudaSuccess;
+  count_launches(1);
   bin_rects_kernel<<<blocks_for(n, 256), 256, 0, s>>>(bounds, n, width, height, near_plane,
                                                       far_plane, rect, count, depth_key, nonfinite);
   return cudaGetLastError();

@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
   double Td = 1.0, Wd = 0.0;
   float C0 = 0.f, C1 = 0.f, C2 = 0.f, D = 0.f, D2 = 0.f, N0 = 0.f, N1 = 0.f, N2 = 0.f;
   float Dn = 0.f, A = 0.f, Scc = 0.f, med_depth = 0.f;
-  int last = rg.x, med = -1, cnt = 0;
+  int last = rg.x, med = -1, cnt = 0, evaluated = 0;
   bool done = !inside;
   const int64_t pix = (int64_t)v * W + u;
   if (tid == 0) s_max = 0;
@@ -67,6 +67,7 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
       for (int j = 0; j < n_in; ++j) {
         const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
         Sample s;
+        ++evaluated;
         if (!eval_sample<MODE>(rec, pr, ext2, nearp, farp, s)) continue;
         const int pos = base + j;
         const float w = s.alpha * (float)Td;
@@ -83,7 +84,7 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
         Wd += (double)w;
         if (med < 0 && (float)Wd >= 0.5f) { med = pos; med_depth = s.depth; }
         if (DIST & SF_DIST_L1) {
-          if (cnt < a.l1_cap || a.l1_off) {
+          if (a.l1_off ? (a.l1_off[pix] + cnt < a.l1_off[pix + 1]) : (cnt < a.l1_cap)) {
             const int64_t idx = l1_index(tile, cnt, tid, a.l1_cap, a.l1_off, pix);
             a.l1s[idx] = s.depth;
             a.l1s[a.l1_slots + idx] = w;
@@ -143,6 +144,18 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
     __syncthreads();
     if (tid == 0) atomicMax(a.l1_needed, s_max);
   }
+  if (a.counters) {
+    unsigned long long e = (unsigned long long)evaluated, c = (unsigned long long)cnt;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      e += __shfl_xor_sync(FULL, e, o);
+      c += __shfl_xor_sync(FULL, c, o);
+    }
+    if ((tid & 31) == 0) {
+      atomicAdd(a.counters, e);
+      atomicAdd(a.counters + 1, c);
+    }
+  }
 }
 
 // ------------------------------------------------------------------ L1 resolve
@@ -173,6 +186,7 @@ __global__ void __launch_bounds__(L1_WARPS * 32) l1_resolve_kernel(
     float* st = state + pix * SF_PIXEL_STATE_FLOATS;
     int n = f2i(st[PS_COUNT]);
     if (!off && n > cap) n = cap;  // over capacity: reported through l1_needed, rerun by the caller
+    if (off && n > off[pix + 1] - off[pix]) n = (int)(off[pix + 1] - off[pix]);
     const int u = (int)(pix % cam.width), v = (int)(pix / cam.width);
     const int tile = (v / TILE) * tiles_x + (u / TILE);
     const int tid = (v % TILE) * TILE + (u % TILE);
@@ -304,7 +318,9 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
     T = st[PS_T];
     last = f2i(st[PS_LAST]);
     k = f2i(st[PS_COUNT]) - 1;
-    if (!a.l1_off && k >= a.l1_cap) k = a.l1_cap - 1;  // never read past the pixel's slots
+    // never read past the pixel's slots
+    if (!a.l1_off && k >= a.l1_cap) k = a.l1_cap - 1;
+    if (a.l1_off && k >= a.l1_off[pix + 1] - a.l1_off[pix]) k = (int)(a.l1_off[pix + 1] - a.l1_off[pix]) - 1;
   } else {
     pg.gW = pg.gD = pg.gDnum = pg.gA = pg.gL1 = pg.gL2 = pg.gMed = pg.gVar = 0.f;
     for (int c = 0; c < 3; ++c) pg.gC[c] = pg.gN[c] = pg.C[c] = 0.f;
@@ -434,6 +450,7 @@ __global__ void pixel_counts_kernel(const float* state, int64_t npix, int32_t* c
 
 template <int MODE>
 cudaError_t fwd_dispatch(const RasterFwdArgs& a, int n_tiles, cudaStream_t s) {
+  count_launches(1);
   switch (a.st.distortions & 3) {
     case 0: raster_forward_kernel<MODE, 0><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
     case 1: raster_forward_kernel<MODE, 1><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
@@ -445,6 +462,7 @@ cudaError_t fwd_dispatch(const RasterFwdArgs& a, int n_tiles, cudaStream_t s) {
 
 template <int MODE>
 cudaError_t bwd_dispatch(const RasterBwdArgs& a, int n_tiles, cudaStream_t s) {
+  count_launches(1);
   switch (a.st.distortions & 3) {
     case 0: raster_backward_kernel<MODE, 0><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
     case 1: raster_backward_kernel<MODE, 1><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
@@ -482,6 +500,7 @@ cudaError_t launch_l1_resolve(const sf_camera& cam, const sf_settings& st, float
   if (npix == 0) return cudaSuccess;
   int64_t blocks = (npix + L1_WARPS - 1) / L1_WARPS;
   if (blocks > 148 * 64) blocks = 148 * 64;
+  count_launches(1);
   l1_resolve_kernel<<<(unsigned)blocks, L1_WARPS * 32, 0, s>>>(cam, state, l1s, slots, off, cap, out_l1);
   return cudaGetLastError();
 }
@@ -490,12 +509,14 @@ cudaError_t launch_raster_finalize(const float* records, int64_t n, const sf_cam
                                    int mode, float* grad_records, float* grad_means2d,
                                    cudaStream_t s) {
   if (n == 0) return cudaSuccess;
+  count_launches(1);
   raster_finalize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(records, n, cam, mode, grad_records, grad_means2d);
   return cudaGetLastError();
 }
 
 cudaError_t launch_pixel_counts(const float* state, int64_t npix, int32_t* counts, cudaStream_t s) {
   if (npix == 0) return cudaSuccess;
+  count_launches(1);
   pixel_counts_kernel<<<(unsigned)((npix + 255) / 256), 256, 0, s>>>(state, npix, counts);
   return cudaGetLastError();
 }

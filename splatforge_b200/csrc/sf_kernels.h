@@ -9,6 +9,10 @@
 
 namespace sf {
 
+// kernels launched by this library (sf_b200_kernel_launches)
+void count_launches(int k);
+int64_t launches_total();
+
 struct RasterFwdArgs {
   const float* records;
   const int32_t* ids;
@@ -20,6 +24,7 @@ struct RasterFwdArgs {
   float* median; float* ray_color; float* amb;
   float* state;
   float* l1s; int64_t l1_slots; const int64_t* l1_off; int l1_cap; int32_t* l1_needed;
+  unsigned long long* counters;
 };
 
 struct RasterBwdArgs {

@@ -27,6 +27,13 @@ from ._lib import L1_SAMPLE_FLOATS, PIXEL_STATE_FLOATS, RECORD_FLOATS, Camera, S
 
 TILE = 16
 
+# Optional instrumentation used by bench.py: when PROFILE is a dict, CUDA events are
+# recorded on the launching stream around the raster forward / backward calls and
+# the (start, end) pairs appended to PROFILE["fwd"] / PROFILE["bwd"].
+PROFILE = None
+# evaluated / contributing (pixel, Gaussian) pairs of the last forward raster
+LAST_PAIRS = {}
+
 
 def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
@@ -250,16 +257,26 @@ class _Raster(torch.autograd.Function):
             l1s = torch.empty((L1_SAMPLE_FLOATS, slots), **f)
             needed = torch.zeros((1,), device=dev, dtype=torch.int32)
 
+        counters = torch.zeros((2,), device=dev, dtype=torch.int64) if PROFILE is not None else None
+
         def run():
             call(
                 "sf_b200_raster_forward", _ptr(records), plan.n, _ptr(plan.ids), _ptr(plan.ranges),
                 ctypes.byref(plan.cam), ctypes.byref(plan.settings),
                 _ptr(rgb), _ptr(alpha), _ptr(depth), _ptr(normals), _ptr(l1), _ptr(l2), _ptr(median),
                 _ptr(ray_color), _ptr(amb), _ptr(state), _ptr(l1s), slots, _ptr(l1_off), cap,
-                _ptr(needed), _stream(dev),
+                _ptr(needed), _ptr(counters), _stream(dev),
             )
 
-        run()
+        if PROFILE is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+            run()
+            ev[1].record()
+            PROFILE["fwd"].append(ev)
+            PROFILE.setdefault("counters", []).append(counters)
+        else:
+            run()
         if use_l1:
             most = int(needed.item())
             plan.stats["l1_max_samples"] = most
@@ -296,13 +313,25 @@ class _Raster(torch.autograd.Function):
         grad_means2d = torch.empty((n, 2), device=dev, dtype=torch.float32)
         absgrad = plan.absgrad if plan.absgrad is not None else torch.zeros((n, 2), device=dev)
         l1s, slots, l1_off, cap = ctx.l1
+        ev = None
+        if PROFILE is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
         call(
             "sf_b200_raster_backward", _ptr(records), n, _ptr(plan.ids), _ptr(plan.ranges),
             ctypes.byref(plan.cam), ctypes.byref(plan.settings), _ptr(ctx.state), _ptr(l1s), slots,
             _ptr(l1_off), cap, *(_ptr(g) for g in grads), _ptr(grad_records), _ptr(grad_means2d),
             _ptr(absgrad), _stream(dev),
         )
+        if ev is not None:
+            ev[1].record()
+            PROFILE["bwd"].append(ev)
         return grad_means2d, grad_records, None
+
+
+def kernel_launches():
+    """Kernels launched so far by libsf_b200.so in this process."""
+    return int(_lib.lib().sf_b200_kernel_launches())
 
 
 def rasterize(means, quats, scales, opacities, sh, sh_degree, camera, settings, *, selected=None):
