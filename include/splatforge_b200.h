@@ -51,9 +51,9 @@ enum {
 #define SF_RECORD_FLOATS 20
 /* floats per pixel of the forward state kept for the backward pass */
 #define SF_PIXEL_STATE_FLOATS 16
-/* floats per stored L1 sample: depth, weight, list position, and the two adjoint
- * factors written by sf_b200_l1_resolve (stored column-wise, see raster_forward) */
-#define SF_L1_SAMPLE_FLOATS 5
+/* floats per stored L1 sample: depth and weight, which sf_b200_l1_resolve replaces by
+ * the two adjoint factors the backward pass reads (stored column-wise) */
+#define SF_L1_SAMPLE_FLOATS 2
 
 /* Pinhole camera, OpenCV convention (src/splatforge/studio/cameras.py:8-22). */
 typedef struct sf_camera {
@@ -167,14 +167,14 @@ int sf_b200_bin_keys(const int32_t* isect_ids, const int32_t* tile_ranges,
  * One CTA per 16x16 tile.  Images are HWC float32: rgb/normals [H,W,3], the rest
  * [H,W].  pixel_state [H*W, SF_PIXEL_STATE_FLOATS] is kept for the backward pass.
  * L1 (settings->distortions & SF_DIST_L1) stores each pixel's contributing samples in
- * l1_samples, laid out [SF_L1_SAMPLE_FLOATS, l1_slots]: with l1_offsets == NULL the
- * 256 pixels of tile t own slots [(t*l1_cap + k)*256 + pixel-in-tile] for k < l1_cap
- * (l1_slots = n_tiles*l1_cap*256); otherwise pixel p (row-major) owns slots
- * [l1_offsets[p], l1_offsets[p+1]) and l1_slots = l1_offsets[H*W].  l1_needed (device
- * int, may be NULL) receives the largest per-pixel sample count; when it exceeds the
- * capacity the caller reruns the forward with CSR offsets (the L1 result of this
- * call is then incomplete).  counters (device int64[2], may be NULL) accumulate the
- * (pixel, Gaussian) pairs evaluated and the pairs that contributed. */
+ * l1_samples, laid out [SF_L1_SAMPLE_FLOATS, l1_slots], each pixel's samples
+ * contiguous: with l1_offsets == NULL pixel t*256+i (tile t, pixel i of the tile) owns
+ * slots [(t*256+i)*l1_cap, +l1_cap) and l1_slots = n_tiles*256*l1_cap; otherwise pixel
+ * p (row-major) owns [l1_offsets[p], l1_offsets[p+1]) and l1_slots = l1_offsets[H*W].
+ * l1_needed (device int, may be NULL) receives the largest per-pixel sample count;
+ * when it exceeds the capacity the caller reruns the forward with CSR offsets (the L1
+ * result of this call is then incomplete).  counters (device int64[2], may be NULL)
+ * accumulate the (pixel, Gaussian) pairs evaluated and the pairs that contributed. */
 int sf_b200_raster_forward(const float* records, int64_t n, const int32_t* isect_ids,
                            const int32_t* tile_ranges, const sf_camera* camera,
                            const sf_settings* settings, float* rgb, float* alpha,
@@ -190,17 +190,21 @@ int sf_b200_raster_forward(const float* records, int64_t n, const int32_t* isect
 int sf_b200_l1_offsets(const sf_camera* camera, const float* pixel_state, int64_t* offsets,
                        void* workspace, size_t workspace_bytes, void* stream);
 
-/* Sorts every pixel's stored samples by depth, writes distortion_l1 and replaces
- * each sample by the two factors the backward pass needs. */
+/* Sorts every pixel's stored samples by depth (a warp-level LSD radix sort in shared
+ * memory), writes distortion_l1 and replaces each sample by the two factors the
+ * backward pass needs.  max_samples bounds the per-pixel count (the l1_needed value of
+ * the forward call); it sizes the shared-memory staging. */
 int sf_b200_l1_resolve(const sf_camera* camera, const sf_settings* settings,
                        float* pixel_state, float* l1_samples, int64_t l1_slots,
-                       const int64_t* l1_offsets, int32_t l1_cap, float* distortion_l1,
-                       void* stream);
+                       const int64_t* l1_offsets, int32_t l1_cap, int32_t max_samples,
+                       float* distortion_l1, void* stream);
 
 /* ---- raster backward ---------------------------------------------------------------
  * Upstream image adjoints may each be NULL (zero).  grad_records [N,SF_RECORD_FLOATS]
  * and absgrad [N,2] are ACCUMULATED into (the caller zeroes them); grad_means2d [N,2]
- * is overwritten with the adjoint of the projected means. */
+ * is overwritten with the adjoint of the projected means.  error_word (device int,
+ * may be NULL) is OR-ed with 1 when a pixel's recomputed contributing samples do not
+ * match the count the forward pass stored (an internal consistency check). */
 int sf_b200_raster_backward(const float* records, int64_t n, const int32_t* isect_ids,
                             const int32_t* tile_ranges, const sf_camera* camera,
                             const sf_settings* settings, const float* pixel_state,
@@ -211,7 +215,8 @@ int sf_b200_raster_backward(const float* records, int64_t n, const int32_t* isec
                             const float* grad_l1, const float* grad_l2,
                             const float* grad_median, const float* grad_ray_color,
                             const float* grad_ambiguity, float* grad_records,
-                            float* grad_means2d, float* absgrad, void* stream);
+                            float* grad_means2d, float* absgrad, int32_t* error_word,
+                            void* stream);
 
 #ifdef __cplusplus
 }

@@ -18,7 +18,7 @@ MODE = {"radegs": 0, "gof": 1, "ambisur": 2}
 DISTORTIONS = {"none": 0, "l1": 1, "l2": 2, "both": 3}
 RECORD_FLOATS = 20
 PIXEL_STATE_FLOATS = 16
-L1_SAMPLE_FLOATS = 5
+L1_SAMPLE_FLOATS = 2
 
 
 class Camera(ctypes.Structure):
@@ -88,13 +88,13 @@ _SIGNATURES = {
     "sf_b200_l1_offsets": (ctypes.c_int, [POINTER(Camera), P, P, P, c_size_t, P]),
     "sf_b200_l1_resolve": (
         ctypes.c_int,
-        [POINTER(Camera), POINTER(Settings), P, P, c_int64, P, c_int32, P, P],
+        [POINTER(Camera), POINTER(Settings), P, P, c_int64, P, c_int32, c_int32, P, P],
     ),
     "sf_b200_raster_backward": (
         ctypes.c_int,
         [P, c_int64, P, P, POINTER(Camera), POINTER(Settings), P, P, c_int64, P, c_int32]
         + [P] * 9
-        + [P, P, P, P],
+        + [P, P, P, P, P],
     ),
 }
 

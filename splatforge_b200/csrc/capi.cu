@@ -215,8 +215,8 @@ int sf_b200_raster_forward(const float* records, int64_t n, const int32_t* isect
   const int n_tiles = tiles_of(camera, &tx);
   if (settings->distortions & SF_DIST_L1) {
     if (!l1_samples) return fail(SF_ERR_ARGUMENT, "raster_forward: L1 requested without sample storage");
-    if (!l1_offsets && (l1_cap <= 0 || l1_slots < (int64_t)n_tiles * l1_cap * 256))
-      return fail(SF_ERR_CAPACITY, "raster_forward: L1 storage of %lld slots is smaller than tiles*cap*256",
+    if (!l1_offsets && (l1_cap <= 0 || l1_slots < (int64_t)n_tiles * 256 * l1_cap))
+      return fail(SF_ERR_CAPACITY, "raster_forward: L1 storage of %lld slots is smaller than tiles*256*cap",
                   (long long)l1_slots);
   }
   if (!aligned(records, 16)) return fail(SF_ERR_ARGUMENT, "raster_forward: records need 16-byte alignment");
@@ -250,13 +250,20 @@ int sf_b200_l1_offsets(const sf_camera* camera, const float* pixel_state, int64_
 }
 
 int sf_b200_l1_resolve(const sf_camera* camera, const sf_settings* settings, float* pixel_state, float* l1_samples,
-                       int64_t l1_slots, const int64_t* l1_offsets, int32_t l1_cap, float* distortion_l1,
-                       void* stream) {
+                       int64_t l1_slots, const int64_t* l1_offsets, int32_t l1_cap, int32_t max_samples,
+                       float* distortion_l1, void* stream) {
   int rc;
   if ((rc = check_settings(settings, "l1_resolve")) || (rc = check_camera(camera, "l1_resolve"))) return rc;
   if (!pixel_state || !l1_samples || !distortion_l1) return fail(SF_ERR_ARGUMENT, "l1_resolve: NULL buffer");
+  if (max_samples < 0) return fail(SF_ERR_ARGUMENT, "l1_resolve: negative max_samples");
+  const int smem_k = ((max_samples > 0 ? max_samples : 1) + 31) / 32 * 32;
+  if (sf::l1_resolve_smem_per_warp(smem_k) > 200 * 1024)
+    return fail(SF_ERR_CAPACITY,
+                "l1_resolve: a pixel has %d contributing samples, more than the %d the shared-memory sort "
+                "stages; raise transmittance_floor",
+                max_samples, (int)((200 * 1024 / 4 - 256) / 5));
   return cuda_status(sf::launch_l1_resolve(*camera, *settings, pixel_state, l1_samples, l1_slots, l1_offsets, l1_cap,
-                                           distortion_l1, as_stream(stream)),
+                                           max_samples, distortion_l1, as_stream(stream)),
                      "l1_resolve");
 }
 
@@ -266,7 +273,8 @@ int sf_b200_raster_backward(const float* records, int64_t n, const int32_t* isec
                             const float* grad_rgb, const float* grad_alpha, const float* grad_depth,
                             const float* grad_normals, const float* grad_l1, const float* grad_l2,
                             const float* grad_median, const float* grad_ray_color, const float* grad_ambiguity,
-                            float* grad_records, float* grad_means2d, float* absgrad, void* stream) {
+                            float* grad_records, float* grad_means2d, float* absgrad, int32_t* error_word,
+                            void* stream) {
   int rc;
   if ((rc = check_settings(settings, "raster_backward")) || (rc = check_camera(camera, "raster_backward"))) return rc;
   if (!tile_ranges || !pixel_state || n < 0 || (n > 0 && (!records || !grad_records || !grad_means2d || !absgrad)))
@@ -283,7 +291,7 @@ int sf_b200_raster_backward(const float* records, int64_t n, const int32_t* isec
   a.l1s = l1_samples; a.l1_slots = l1_slots; a.l1_off = l1_offsets; a.l1_cap = l1_cap;
   a.g_rgb = grad_rgb; a.g_alpha = grad_alpha; a.g_depth = grad_depth; a.g_normals = grad_normals;
   a.g_l1 = grad_l1; a.g_l2 = grad_l2; a.g_median = grad_median; a.g_var = grad_ray_color; a.g_amb = grad_ambiguity;
-  a.grad_records = grad_records; a.absgrad = absgrad;
+  a.grad_records = grad_records; a.absgrad = absgrad; a.error_word = error_word;
   cudaStream_t s = as_stream(stream);
   cudaError_t e = sf::launch_raster_backward(a, n_tiles, s);
   if (e == cudaSuccess) e = sf::launch_raster_finalize(records, n, *camera, settings->mode, grad_records, grad_means2d, s);

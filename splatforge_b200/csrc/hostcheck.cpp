@@ -30,7 +30,7 @@ void rect_bounds(int64_t i, float x, float y, float r, float z, const sf_camera&
   depth_key[i] = c > 0 ? bits : 0xffffffffu;
 }
 
-int64_t l1_index(int tile, int k, int tid, int cap) { return ((int64_t)tile * cap + k) * 256 + tid; }
+int64_t l1_index(int tile, int k, int tid, int cap) { return ((int64_t)tile * 256 + tid) * cap + k; }
 
 }  // namespace
 
@@ -145,7 +145,6 @@ int hc_raster_forward(const float* records, const int32_t* ids, const int32_t* r
           const int64_t idx = l1_index(tile, cnt, tid, cap);
           l1s[idx] = s.depth;
           l1s[slots + idx] = w;
-          l1s[2 * slots + idx] = i2f(pos);
         }
         ++cnt;
         last = pos + 1;
@@ -186,14 +185,19 @@ int hc_raster_forward(const float* records, const int32_t* ids, const int32_t* r
         float Wt = 0, Dt = 0;
         for (int k = 0; k < n; ++k) { Wt += wk(k); Dt += wk(k) * dk(k); }
         float pw = 0, pwd = 0;
+        std::vector<float> aw(n), ad(n);
         for (int r = 0; r < n; ++r) {
           const int k = order[r];
           const float d = dk(k), w = wk(k);
           raw += 2.f * w * (d * pw - pwd);
-          const int64_t idx = l1_index(tile, k, tid, cap);
-          l1s[3 * slots + idx] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
-          l1s[4 * slots + idx] = 2.f * w * (2.f * pw + w - Wt);
+          aw[k] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
+          ad[k] = 2.f * w * (2.f * pw + w - Wt);
           pw += w; pwd += w * d;
+        }
+        for (int k = 0; k < n; ++k) {
+          const int64_t idx = l1_index(tile, k, tid, cap);
+          l1s[idx] = aw[k];
+          l1s[slots + idx] = ad[k];
         }
       }
       stt[PS_L1] = raw;
@@ -245,26 +249,20 @@ int hc_raster_backward(const float* records, int64_t n, const int32_t* ids, cons
         Sample s;
         bool contrib;
         float auxw = 0.f, auxd = 0.f;
-        if (dist & SF_DIST_L1) {
-          contrib = false;
-          if (k >= 0) {
-            const int64_t idx = l1_index(tile, k, tid, cap);
-            if (f2i(l1s[2 * slots + idx]) == pos) {
-              contrib = true;
-              auxw = l1s[3 * slots + idx];
-              auxd = l1s[4 * slots + idx];
-              --k;
-              if (mode == SF_MODE_GOF) eval_sample<SF_MODE_GOF, false>(rec, pr, 0, 0, 0, s);
-              else if (mode == SF_MODE_RADEGS) eval_sample<SF_MODE_RADEGS, false>(rec, pr, 0, 0, 0, s);
-              else eval_sample<SF_MODE_AMBISUR, false>(rec, pr, 0, 0, 0, s);
-            }
-          }
-        } else if (mode == SF_MODE_GOF) {
+        if (mode == SF_MODE_GOF) {
           contrib = eval_sample<SF_MODE_GOF>(rec, pr, st->extent_sq, st->near_plane, st->far_plane, s);
         } else if (mode == SF_MODE_RADEGS) {
           contrib = eval_sample<SF_MODE_RADEGS>(rec, pr, st->extent_sq, st->near_plane, st->far_plane, s);
         } else {
           contrib = eval_sample<SF_MODE_AMBISUR>(rec, pr, st->extent_sq, st->near_plane, st->far_plane, s);
+        }
+        if ((dist & SF_DIST_L1) && contrib) {
+          if (k >= 0) {
+            const int64_t idx = l1_index(tile, k, tid, cap);
+            auxw = l1s[idx];
+            auxd = l1s[slots + idx];
+          }
+          --k;
         }
         if (!contrib || !(s.alpha > 0.f)) continue;
         const float al = s.alpha, om = 1.f - al;

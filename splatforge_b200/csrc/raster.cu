@@ -24,9 +24,48 @@ namespace {
 constexpr int REC4 = SF_RECORD_FLOATS / 4;  // float4 per record
 constexpr int ACC = 24;                      // accumulator floats per batch slot (20 + absgrad 2 + pad)
 
-__device__ __forceinline__ int64_t l1_index(int tile, int k, int tid, int cap, const int64_t* off,
-                                            int64_t pix) {
-  return off ? off[pix] + k : ((int64_t)tile * cap + k) * TILE_PIXELS + tid;
+// first slot of a pixel's contiguous L1 sample run (fixed capacity or CSR)
+__device__ __forceinline__ int64_t l1_base(int tile, int tid, int cap, const int64_t* off, int64_t pix) {
+  return off ? off[pix] : ((int64_t)tile * TILE_PIXELS + tid) * cap;
+}
+
+// Warp-level culling of a batch: bit j of mask[j / 32] is set when Gaussian j may reach
+// a pixel of this warp's 16x2 pixel block.  Conservative: the axis-aligned box of the
+// ellipse squared <= extent^2 (half-widths sqrt(extent^2 * inv(Q)_xx), ...) widened by
+// a margin, tested against the box spanned by the warp's own pixel coordinates.
+__device__ __forceinline__ void warp_cull(const float4* s_rec, int n_in, int lane, float x0, float x1,
+                                          float y0, float y1, float ext2, unsigned (&mask)[TILE_PIXELS / 32]) {
+#pragma unroll
+  for (int g = 0; g < TILE_PIXELS / 32; ++g) {
+    const int j = g * 32 + lane;
+    bool hit = false;
+    if (j < n_in) {
+      const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
+      const float qa = rec[R_QA], qb = rec[R_QB], qc = rec[R_QC];
+      const float det = qa * qc - qb * qb;
+      if (det > 0.f) {
+        const float hx = sqrtf(fmaxf(ext2 * qc / det, 0.f)) * 1.001f + 1e-2f;
+        const float hy = sqrtf(fmaxf(ext2 * qa / det, 0.f)) * 1.001f + 1e-2f;
+        const float X = rec[R_X], Y = rec[R_Y];
+        hit = (X + hx >= x0) && (X - hx <= x1) && (Y + hy >= y0) && (Y - hy <= y1);
+      } else {
+        hit = true;  // degenerate conic: never cull
+      }
+      if (!(hit == hit)) hit = true;
+    }
+    mask[g] = __ballot_sync(FULL, hit);
+  }
+}
+
+__device__ __forceinline__ float warp_minf(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(FULL, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_maxf(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, o));
+  return v;
 }
 
 // ------------------------------------------------------------------ forward
@@ -42,6 +81,8 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
   const bool inside = u < W && v < H;
   PixelRay pr;
   pixel_ray(a.cam, u, v, pr);
+  const float wx0 = warp_minf(pr.px), wx1 = warp_maxf(pr.px);
+  const float wy0 = warp_minf(pr.py), wy1 = warp_maxf(pr.py);
   const int2 rg = a.ranges[tile];
   const float ext2 = a.st.extent_sq, nearp = a.st.near_plane, farp = a.st.far_plane;
   const double t_stop = (double)a.st.t_stop;
@@ -51,6 +92,12 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
   int last = rg.x, med = -1, cnt = 0, evaluated = 0;
   bool done = !inside;
   const int64_t pix = (int64_t)v * W + u;
+  int64_t l1_at = 0;
+  int l1_room = 0;
+  if ((DIST & SF_DIST_L1) && inside) {
+    l1_at = l1_base(tile, tid, a.l1_cap, a.l1_off, pix);
+    l1_room = a.l1_off ? (int)(a.l1_off[pix + 1] - a.l1_off[pix]) : a.l1_cap;
+  }
   if (tid == 0) s_max = 0;
   __syncthreads();
 
@@ -63,8 +110,15 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
       s_rec[k] = __ldg(reinterpret_cast<const float4*>(a.records) + (int64_t)id * REC4 + comp);
     }
     __syncthreads();
-    if (!done) {
-      for (int j = 0; j < n_in; ++j) {
+    unsigned mask[TILE_PIXELS / 32];
+    warp_cull(s_rec, n_in, tid & 31, wx0, wx1, wy0, wy1, ext2, mask);
+    for (int g = 0; g < TILE_PIXELS / 32; ++g) {
+      if (__all_sync(FULL, done)) break;
+      unsigned m = mask[g];
+      while (m) {
+        const int j = g * 32 + __ffs(m) - 1;
+        m &= m - 1;
+        if (done) continue;
         const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
         Sample s;
         ++evaluated;
@@ -84,17 +138,15 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
         Wd += (double)w;
         if (med < 0 && (float)Wd >= 0.5f) { med = pos; med_depth = s.depth; }
         if (DIST & SF_DIST_L1) {
-          if (a.l1_off ? (a.l1_off[pix] + cnt < a.l1_off[pix + 1]) : (cnt < a.l1_cap)) {
-            const int64_t idx = l1_index(tile, cnt, tid, a.l1_cap, a.l1_off, pix);
-            a.l1s[idx] = s.depth;
-            a.l1s[a.l1_slots + idx] = w;
-            a.l1s[2 * a.l1_slots + idx] = i2f(pos);
+          if (cnt < l1_room) {
+            a.l1s[l1_at + cnt] = s.depth;
+            a.l1s[a.l1_slots + l1_at + cnt] = w;
           }
         }
         ++cnt;
         last = pos + 1;
         Td *= (double)(1.f - s.alpha);
-        if (Td < t_stop) { done = true; break; }
+        if (Td < t_stop) done = true;
       }
     }
   }
@@ -159,82 +211,132 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
 }
 
 // ------------------------------------------------------------------ L1 resolve
-// One warp per pixel: bitonic sort of the stored (depth, sample) pairs in shared
-// memory, warp prefix sums of w and w*d in depth order, then
+// One warp per pixel.  The pixel's samples (depth, weight; compositing order) are
+// staged in shared memory and sorted by depth with a stable warp-level LSD radix sort
+// on the float bits (positive depths order like their bit patterns; bytes that are
+// equal for every sample are skipped), then prefix sums of w and w*d in depth order
+// give
 //   L1     = sum_i 2 w_i (d_i W_<i - D_<i)
 //   auxw_i = 2 (2 d_i W_<i - d_i W + D - 2 D_<i)     (dL1/dw_i)
 //   auxd_i = 2 w_i (2 W_<i + w_i - W)                 (dL1/dd_i)
-// (composite_cuda.cu:54-65 computes the same factors from torch's sort order).
-// Columns of l1s: 0 depth, 1 weight, 2 list position, 3 auxw, 4 auxd.
-constexpr int L1_WARPS = 4;
-constexpr int L1_SMEM_K = 1024;  // per-warp capacity of the in-shared-memory sort
+// (composite_cuda.cu:54-65 computes the same factors from torch's sort order).  The
+// two factors replace (d_i, w_i) in place, written back contiguously.
+__device__ __forceinline__ void warp_radix_sort(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1,
+                                                uint32_t* hist, int n, int lane, uint32_t** kout,
+                                                uint32_t** vout) {
+  uint32_t orv = 0u, andv = 0xffffffffu;
+  for (int i = lane; i < n; i += 32) { orv |= k0[i]; andv &= k0[i]; }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    orv |= __shfl_xor_sync(FULL, orv, o);
+    andv &= __shfl_xor_sync(FULL, andv, o);
+  }
+  const uint32_t vary = orv ^ andv;
+  const unsigned lt = (1u << lane) - 1u;
+  uint32_t *ki = k0, *vi = v0, *ko = k1, *vo = v1;
+  for (int shift = 0; shift < 32; shift += 8) {
+    if (((vary >> shift) & 0xffu) == 0u) continue;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) hist[lane * 8 + b] = 0u;
+    __syncwarp();
+    for (int c = 0; c < n; c += 32) {
+      const int i = c + lane;
+      const bool valid = i < n;
+      const uint32_t d = valid ? (ki[i] >> shift) & 0xffu : 0u;
+      const unsigned peers = __match_any_sync(FULL, valid ? d : 0x100u + lane);
+      if (valid && lane == __ffs(peers) - 1) hist[d] += __popc(peers);
+      __syncwarp();
+    }
+    // exclusive scan of the 256 counts: 8 per lane
+    uint32_t loc[8], sum = 0u;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) { loc[b] = hist[lane * 8 + b]; sum += loc[b]; }
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(FULL, incl, o);
+      if (lane >= o) incl += y;
+    }
+    uint32_t run = incl - sum;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) { hist[lane * 8 + b] = run; run += loc[b]; }
+    __syncwarp();
+    for (int c = 0; c < n; c += 32) {
+      const int i = c + lane;
+      const bool valid = i < n;
+      const uint32_t key = valid ? ki[i] : 0u;
+      const uint32_t d = (key >> shift) & 0xffu;
+      const unsigned peers = __match_any_sync(FULL, valid ? d : 0x100u + lane);
+      const uint32_t base = valid ? hist[d] : 0u;
+      __syncwarp();
+      if (valid) {
+        const uint32_t pos = base + __popc(peers & lt);
+        ko[pos] = key;
+        vo[pos] = vi[i];
+        if (lane == 31 - __clz(peers)) hist[d] = base + __popc(peers);
+      }
+      __syncwarp();
+    }
+    uint32_t* t = ki; ki = ko; ko = t;
+    t = vi; vi = vo; vo = t;
+  }
+  *kout = ki;
+  *vout = vi;
+}
 
-__global__ void __launch_bounds__(L1_WARPS * 32) l1_resolve_kernel(
-    sf_camera cam, float* state, float* l1s, int64_t slots, const int64_t* off, int cap,
+__global__ void __launch_bounds__(128) l1_resolve_kernel(
+    sf_camera cam, float* state, float* l1s, int64_t slots, const int64_t* off, int cap, int smem_k,
     float* out_l1) {
-  __shared__ float s_key[L1_WARPS][L1_SMEM_K];
-  __shared__ int s_val[L1_WARPS][L1_SMEM_K];
+  extern __shared__ uint32_t s_l1[];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int warps = blockDim.x >> 5;
+  uint32_t* k0 = s_l1 + (size_t)wid * (5 * smem_k + 256);
+  uint32_t* v0 = k0 + smem_k;
+  uint32_t* k1 = v0 + smem_k;
+  uint32_t* v1 = k1 + smem_k;
+  float* ws = reinterpret_cast<float*>(v1 + smem_k);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(ws + smem_k);
   const int64_t npix = (int64_t)cam.width * cam.height;
   const int tiles_x = (cam.width + TILE - 1) / TILE;
-  const float* col_d = l1s;
-  const float* col_w = l1s + slots;
-  float* col_aw = l1s + 3 * slots;
-  float* col_ad = l1s + 4 * slots;
-  for (int64_t pix = (int64_t)blockIdx.x * L1_WARPS + wid; pix < npix;
-       pix += (int64_t)gridDim.x * L1_WARPS) {
+  float* col_d = l1s;
+  float* col_w = l1s + slots;
+  for (int64_t pix = (int64_t)blockIdx.x * warps + wid; pix < npix;
+       pix += (int64_t)gridDim.x * warps) {
     float* st = state + pix * SF_PIXEL_STATE_FLOATS;
     int n = f2i(st[PS_COUNT]);
-    if (!off && n > cap) n = cap;  // over capacity: reported through l1_needed, rerun by the caller
-    if (off && n > off[pix + 1] - off[pix]) n = (int)(off[pix + 1] - off[pix]);
     const int u = (int)(pix % cam.width), v = (int)(pix / cam.width);
     const int tile = (v / TILE) * tiles_x + (u / TILE);
     const int tid = (v % TILE) * TILE + (u % TILE);
-    auto index = [&](int k) { return l1_index(tile, k, tid, cap, off, pix); };
+    const int64_t base = l1_base(tile, tid, cap, off, pix);
+    // never read past the pixel's run (a capacity overflow is rerun by the caller)
+    const int room = off ? (int)(off[pix + 1] - off[pix]) : cap;
+    if (n > room) n = room;
     float Wt = 0.f, Dt = 0.f;
     for (int k = lane; k < n; k += 32) {
-      const int64_t i = index(k);
-      Wt += col_w[i]; Dt += col_w[i] * col_d[i];
+      const float d = col_d[base + k], w = col_w[base + k];
+      Wt += w; Dt += w * d;
     }
     Wt = warp_sum(Wt); Dt = warp_sum(Dt);
     float raw = 0.f;
-    if (n <= L1_SMEM_K) {
-      int np = 32;
-      while (np < n) np <<= 1;
-      for (int k = lane; k < np; k += 32) {
-        s_key[wid][k] = k < n ? col_d[index(k)] : __int_as_float(0x7f800000);
-        s_val[wid][k] = k < n ? k : 0x7fffffff;
+    if (n > smem_k) n = smem_k;  // the launcher sizes smem_k >= the largest count
+    {
+      for (int k = lane; k < n; k += 32) {
+        k0[k] = __float_as_uint(col_d[base + k]);
+        v0[k] = (uint32_t)k;
+        ws[k] = col_w[base + k];
       }
       __syncwarp();
-      for (int size = 2; size <= np; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-          for (int k = lane; k < np; k += 32) {
-            const int partner = k ^ stride;
-            if (partner > k) {
-              const bool asc = (k & size) == 0;
-              const float ka = s_key[wid][k], kb = s_key[wid][partner];
-              const int va = s_val[wid][k], vb = s_val[wid][partner];
-              // order by (depth, compositing index)
-              const bool greater = ka > kb || (ka == kb && va > vb);
-              if (greater == asc) {
-                s_key[wid][k] = kb; s_key[wid][partner] = ka;
-                s_val[wid][k] = vb; s_val[wid][partner] = va;
-              }
-            }
-          }
-          __syncwarp();
-        }
-      }
+      uint32_t *ks, *vs;
+      warp_radix_sort(k0, v0, k1, v1, hist, n, lane, &ks, &vs);
+      // the buffers not holding the sorted result receive the factors, by sample index
+      float* aw = reinterpret_cast<float*>(ks == k0 ? k1 : k0);
+      float* ad = reinterpret_cast<float*>(vs == v0 ? v1 : v0);
       float carry_w = 0.f, carry_wd = 0.f;
-      for (int k0 = 0; k0 < n; k0 += 32) {
-        const int k = k0 + lane;
+      for (int c = 0; c < n; c += 32) {
+        const int r = c + lane;
         float d = 0.f, w = 0.f;
-        int64_t i = 0;
-        if (k < n) {
-          i = index(s_val[wid][k]);
-          d = s_key[wid][k];
-          w = col_w[i];
-        }
+        uint32_t k = 0;
+        if (r < n) { k = vs[r]; d = __uint_as_float(ks[r]); w = ws[k]; }
         float sw = w, swd = w * d;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -244,28 +346,18 @@ __global__ void __launch_bounds__(L1_WARPS * 32) l1_resolve_kernel(
         const float pw = carry_w + sw - w, pwd = carry_wd + swd - w * d;
         carry_w += __shfl_sync(FULL, sw, 31);
         carry_wd += __shfl_sync(FULL, swd, 31);
-        if (k < n) {
+        if (r < n) {
           raw += 2.f * w * (d * pw - pwd);
-          col_aw[i] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
-          col_ad[i] = 2.f * w * (2.f * pw + w - Wt);
+          aw[k] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
+          ad[k] = 2.f * w * (2.f * pw + w - Wt);
         }
       }
       __syncwarp();
-    } else {
-      // rare long lists: ranks straight from global memory, O(n^2) per pixel
       for (int k = lane; k < n; k += 32) {
-        const int64_t i = index(k);
-        const float d = col_d[i], w = col_w[i];
-        float pw = 0.f, pwd = 0.f;
-        for (int m = 0; m < n; ++m) {
-          const int64_t jm = index(m);
-          const float dm = col_d[jm];
-          if (dm < d || (dm == d && m < k)) { const float wm = col_w[jm]; pw += wm; pwd += wm * dm; }
-        }
-        raw += 2.f * w * (d * pw - pwd);
-        col_aw[i] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
-        col_ad[i] = 2.f * w * (2.f * pw + w - Wt);
+        col_d[base + k] = aw[k];
+        col_w[base + k] = ad[k];
       }
+      __syncwarp();
     }
     raw = warp_sum(raw);
     if (lane == 0) {
@@ -292,6 +384,8 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
   const int64_t pix = (int64_t)v * W + u;
   PixelRay pr;
   pixel_ray(a.cam, u, v, pr);
+  const float wx0 = warp_minf(pr.px), wx1 = warp_maxf(pr.px);
+  const float wy0 = warp_minf(pr.py), wy1 = warp_maxf(pr.py);
   const int2 rg = a.ranges[tile];
   const float ext2 = a.st.extent_sq, nearp = a.st.near_plane, farp = a.st.far_plane;
   const float fx = a.cam.K[0], fy = a.cam.K[4];
@@ -299,6 +393,7 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
   PixelGrads pg;
   float T = 1.f;
   int last = rg.x, k = -1;
+  int64_t l1_at = 0;
   if (inside) {
     const float* st = a.state + pix * SF_PIXEL_STATE_FLOATS;
     PixelUpstream up;
@@ -318,9 +413,12 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
     T = st[PS_T];
     last = f2i(st[PS_LAST]);
     k = f2i(st[PS_COUNT]) - 1;
-    // never read past the pixel's slots
-    if (!a.l1_off && k >= a.l1_cap) k = a.l1_cap - 1;
-    if (a.l1_off && k >= a.l1_off[pix + 1] - a.l1_off[pix]) k = (int)(a.l1_off[pix + 1] - a.l1_off[pix]) - 1;
+    if (DIST & SF_DIST_L1) {
+      l1_at = l1_base(tile, tid, a.l1_cap, a.l1_off, pix);
+      // never read past the pixel's run
+      const int room = a.l1_off ? (int)(a.l1_off[pix + 1] - a.l1_off[pix]) : a.l1_cap;
+      if (k >= room) k = room - 1;
+    }
   } else {
     pg.gW = pg.gD = pg.gDnum = pg.gA = pg.gL1 = pg.gL2 = pg.gMed = pg.gVar = 0.f;
     for (int c = 0; c < 3; ++c) pg.gC[c] = pg.gN[c] = pg.C[c] = 0.f;
@@ -349,7 +447,14 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
     }
     for (int q = tid; q < n_in * ACC; q += TILE_PIXELS) s_acc[q] = 0.f;
     __syncthreads();
-    for (int j = n_in - 1; j >= 0; --j) {
+    unsigned mask[TILE_PIXELS / 32];
+    warp_cull(s_rec, n_in, lane, wx0, wx1, wy0, wy1, ext2, mask);
+    for (int g = TILE_PIXELS / 32 - 1; g >= 0; --g) {
+     unsigned m = mask[g];
+     while (m) {
+      const int jb = 31 - __clz(m);
+      m &= ~(1u << jb);
+      const int j = g * 32 + jb;
       const int pos = lo + j;
       float vals[NV];
 #pragma unroll
@@ -358,26 +463,19 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
       if (pos < last) {
         const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
         Sample s;
-        bool contrib;
         float auxw = 0.f, auxd = 0.f;
-        if (DIST & SF_DIST_L1) {
-          // membership was recorded by the forward pass: the stored list position of
-          // this pixel's k-th contributing sample
-          contrib = false;
+        // the sample evaluation is a fixed function of its inputs (explicit rounding
+        // everywhere), so membership matches the forward pass exactly and this pixel's
+        // k-th contributing sample (counted from the end) is its k-th stored sample
+        const bool contrib = eval_sample<MODE>(rec, pr, ext2, nearp, farp, s);
+        if ((DIST & SF_DIST_L1) && contrib) {
           if (k >= 0) {
-            const int64_t idx = l1_index(tile, k, tid, a.l1_cap, a.l1_off, pix);
-            if (f2i(a.l1s[2 * a.l1_slots + idx]) == pos) {
-              contrib = true;
-              auxw = a.l1s[3 * a.l1_slots + idx];
-              auxd = a.l1s[4 * a.l1_slots + idx];
-              --k;
-              eval_sample<MODE, false>(rec, pr, ext2, nearp, farp, s);
-            }
+            auxw = a.l1s[l1_at + k];
+            auxd = a.l1s[a.l1_slots + l1_at + k];
           }
-        } else {
-          contrib = eval_sample<MODE>(rec, pr, ext2, nearp, farp, s);
+          --k;
         }
-        if (contrib && s.alpha > 0.f) {
+        if (contrib) {
           act = true;
           const float al = s.alpha;
           const float om = 1.f - al;
@@ -406,6 +504,7 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
           if (lane == 2 * (q - 16) + 1 && t != 0.f) atomicAdd(&s_acc[j * ACC + SampleLayout<MODE>::slot(q)], t);
         }
       }
+     }
     }
     __syncthreads();
     for (int q = tid; q < n_in * (ACC / 4); q += TILE_PIXELS) {
@@ -420,6 +519,7 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
       }
     }
   }
+  if ((DIST & SF_DIST_L1) && inside && k != -1 && a.error_word) atomicOr(a.error_word, 1);
 }
 
 // GOF: proxy_xy = (xy - c) z / f  -> adjoint of the projected means and of camera z;
@@ -492,16 +592,26 @@ cudaError_t launch_raster_backward(const RasterBwdArgs& a, int n_tiles, cudaStre
   }
 }
 
+size_t l1_resolve_smem_per_warp(int smem_k) { return ((size_t)5 * smem_k + 256) * sizeof(uint32_t); }
+
 cudaError_t launch_l1_resolve(const sf_camera& cam, const sf_settings& st, float* state,
-                              float* l1s, int64_t slots, const int64_t* off, int cap,
+                              float* l1s, int64_t slots, const int64_t* off, int cap, int max_samples,
                               float* out_l1, cudaStream_t s) {
   (void)st;
   const int64_t npix = (int64_t)cam.width * cam.height;
   if (npix == 0) return cudaSuccess;
-  int64_t blocks = (npix + L1_WARPS - 1) / L1_WARPS;
-  if (blocks > 148 * 64) blocks = 148 * 64;
+  const int smem_k = ((max(max_samples, 1) + 31) / 32) * 32;
+  const size_t per_warp = l1_resolve_smem_per_warp(smem_k);
+  const size_t budget = 200 * 1024;
+  if (per_warp > budget) return cudaErrorInvalidValue;
+  int warps = (int)min((size_t)4, budget / per_warp);
+  const size_t smem = per_warp * warps;
+  cudaError_t e = cudaFuncSetAttribute(l1_resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  int64_t blocks = (npix + warps - 1) / warps;
+  if (blocks > 148 * 32) blocks = 148 * 32;
   count_launches(1);
-  l1_resolve_kernel<<<(unsigned)blocks, L1_WARPS * 32, 0, s>>>(cam, state, l1s, slots, off, cap, out_l1);
+  l1_resolve_kernel<<<(unsigned)blocks, warps * 32, smem, s>>>(cam, state, l1s, slots, off, cap, smem_k, out_l1);
   return cudaGetLastError();
 }
 

@@ -41,12 +41,14 @@ struct RasterBwdArgs {
   const float* g_amb;
   float* grad_records;
   float* absgrad;
+  int32_t* error_word;
 };
 
 cudaError_t launch_raster_forward(const RasterFwdArgs& a, int n_tiles, cudaStream_t s);
 cudaError_t launch_l1_resolve(const sf_camera& cam, const sf_settings& st, float* state,
                               float* l1s, int64_t l1_slots, const int64_t* l1_off, int l1_cap,
-                              float* out_l1, cudaStream_t s);
+                              int max_samples, float* out_l1, cudaStream_t s);
+size_t l1_resolve_smem_per_warp(int smem_k);
 cudaError_t launch_raster_backward(const RasterBwdArgs& a, int n_tiles, cudaStream_t s);
 cudaError_t launch_raster_finalize(const float* records, int64_t n, const sf_camera& cam,
                                    int mode, float* grad_records, float* grad_means2d,

@@ -58,6 +58,20 @@ SF_HD float rsqrt_rn(float a) {
   return sqrtf(a);
 #endif
 }
+// Explicitly fused multiply-add (never re-associated): together with rmul/radd it
+// makes a sample's depth, response and alpha a fixed function of its inputs, so the
+// forward and backward kernels reach bit-identical membership decisions.
+SF_HD float ffma(float a, float b, float c) {
+#if defined(__CUDA_ARCH__)
+  return __fmaf_rn(a, b, c);
+#else
+  return fmaf(a, b, c);
+#endif
+}
+SF_HD float dot3(float a0, float a1, float a2, float b0, float b1, float b2) {
+  return ffma(a2, b2, ffma(a1, b1, rmul(a0, b0)));
+}
+
 SF_HD float fmaxr(float a, float b) { return a > b ? a : b; }
 SF_HD int f2i(float f) {
 #if defined(__CUDA_ARCH__)
@@ -492,7 +506,7 @@ SF_HD void pixel_ray(const sf_camera& cam, int u, int v, PixelRay& pr) {
     pr.r[i] = radd(radd(rmul(uf, Ki[i * 3 + 0]), rmul(vf, Ki[i * 3 + 1])), Ki[i * 3 + 2]);
   pr.px = radd(radd(rmul(pr.r[0], K[0]), rmul(pr.r[1], K[1])), rmul(pr.r[2], K[2]));
   pr.py = radd(radd(rmul(pr.r[0], K[3]), rmul(pr.r[1], K[4])), rmul(pr.r[2], K[5]));
-  pr.rnorm = norm3(pr.r);
+  pr.rnorm = rsqrt_rn(dot3(pr.r[0], pr.r[1], pr.r[2], pr.r[0], pr.r[1], pr.r[2]));
 }
 
 // delta^T Q delta as dx (Q delta)_x + dy (Q delta)_y, exact sequence
@@ -515,8 +529,8 @@ struct Sample {
   bool aok;
 };
 
-// CHECK = false evaluates the values of a sample already known to contribute (its
-// membership was recorded by the forward pass) without re-testing the masks.
+// CHECK = false evaluates the values of a sample already known to contribute
+// without re-testing the masks.
 template <int MODE, bool CHECK = true>
 SF_HD bool eval_sample(const float* rec, const PixelRay& pr, float ext2, float near_plane,
                        float far_plane, Sample& s) {
@@ -528,40 +542,40 @@ SF_HD bool eval_sample(const float* rec, const PixelRay& pr, float ext2, float n
   if (MODE == SF_MODE_GOF) {
     const float* q = rec + R_Q3;  // q00 q01 q02 q11 q12 q22
     const float* r = pr.r;
-    s.qd[0] = q[0] * r[0] + q[1] * r[1] + q[2] * r[2];
-    s.qd[1] = q[1] * r[0] + q[3] * r[1] + q[4] * r[2];
-    s.qd[2] = q[2] * r[0] + q[4] * r[1] + q[5] * r[2];
-    s.den_raw = s.qd[0] * r[0] + s.qd[1] * r[1] + s.qd[2] * r[2];
+    s.qd[0] = dot3(q[0], q[1], q[2], r[0], r[1], r[2]);
+    s.qd[1] = dot3(q[1], q[3], q[4], r[0], r[1], r[2]);
+    s.qd[2] = dot3(q[2], q[4], q[5], r[0], r[1], r[2]);
+    s.den_raw = dot3(s.qd[0], s.qd[1], s.qd[2], r[0], r[1], r[2]);
     s.den = fmaxr(s.den_raw, 1e-12f);
     const float* pm = rec + R_PROXY;
-    s.t = (pm[0] * s.qd[0] + pm[1] * s.qd[1] + pm[2] * s.qd[2]) / s.den;
-    s.off[0] = s.t * r[0] - pm[0];
-    s.off[1] = s.t * r[1] - pm[1];
-    s.off[2] = s.t * r[2] - pm[2];
-    float o0 = q[0] * s.off[0] + q[1] * s.off[1] + q[2] * s.off[2];
-    float o1 = q[1] * s.off[0] + q[3] * s.off[1] + q[4] * s.off[2];
-    float o2 = q[2] * s.off[0] + q[4] * s.off[1] + q[5] * s.off[2];
-    s.e = s.off[0] * o0 + s.off[1] * o1 + s.off[2] * o2;
-    resp = expf(-0.5f * fmaxr(s.e, 0.f));
+    s.t = rdiv(dot3(pm[0], pm[1], pm[2], s.qd[0], s.qd[1], s.qd[2]), s.den);
+    s.off[0] = ffma(s.t, r[0], -pm[0]);
+    s.off[1] = ffma(s.t, r[1], -pm[1]);
+    s.off[2] = ffma(s.t, r[2], -pm[2]);
+    const float o0 = dot3(q[0], q[1], q[2], s.off[0], s.off[1], s.off[2]);
+    const float o1 = dot3(q[1], q[3], q[4], s.off[0], s.off[1], s.off[2]);
+    const float o2 = dot3(q[2], q[4], q[5], s.off[0], s.off[1], s.off[2]);
+    s.e = dot3(s.off[0], s.off[1], s.off[2], o0, o1, o2);
+    resp = expf(rmul(-0.5f, fmaxr(s.e, 0.f)));
     s.depth = s.t;
     float mq[3] = {-s.qd[0], -s.qd[1], -s.qd[2]};
     unit3(mq, s.n);
   } else {
-    resp = expf(-0.5f * s.sq);
+    resp = expf(rmul(-0.5f, s.sq));
     if (MODE == SF_MODE_RADEGS) {
-      s.depth = (rec[R_RADIAL] + (rec[R_GAIN] * s.dx + rec[R_GAIN + 1] * s.dy)) / pr.rnorm;
+      s.depth = rdiv(radd(rec[R_RADIAL], ffma(rec[R_GAIN + 1], s.dy, rmul(rec[R_GAIN], s.dx))), pr.rnorm);
       s.n[0] = rec[R_NRM]; s.n[1] = rec[R_NRM + 1]; s.n[2] = rec[R_NRM + 2];
     } else {
       s.n[0] = rec[R_ANRM]; s.n[1] = rec[R_ANRM + 1]; s.n[2] = rec[R_ANRM + 2];
-      s.aden = s.n[0] * pr.r[0] + s.n[1] * pr.r[1] + s.n[2] * pr.r[2];
+      s.aden = dot3(s.n[0], s.n[1], s.n[2], pr.r[0], pr.r[1], pr.r[2]);
       s.aok = fabsf(s.aden) > 1e-8f;
-      s.depth = rec[R_PLANE] / (s.aok ? s.aden : 1.f);
+      s.depth = rdiv(rec[R_PLANE], s.aok ? s.aden : 1.f);
       if (!s.aok) resp = 0.f;
     }
   }
   if (CHECK && !(s.depth > near_plane && s.depth < far_plane)) return false;
   s.resp = resp;
-  s.a_raw = rec[R_OPA] * resp;
+  s.a_raw = rmul(rec[R_OPA], resp);
   s.alpha = fminr(fmaxr(s.a_raw, 0.f), 0.999f);
   return s.alpha > 0.f;
 }

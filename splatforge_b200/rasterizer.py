@@ -31,8 +31,8 @@ TILE = 16
 # recorded on the launching stream around the raster forward / backward calls and
 # the (start, end) pairs appended to PROFILE["fwd"] / PROFILE["bwd"].
 PROFILE = None
-# evaluated / contributing (pixel, Gaussian) pairs of the last forward raster
-LAST_PAIRS = {}
+# largest per-pixel L1 sample count seen, per image size (capacity of the next render)
+_L1_SEEN = {}
 
 
 def _ptr(t):
@@ -79,7 +79,10 @@ class RasterSettings:
     antialiased: bool = False
     tile_size: int = 16
     transmittance_floor: float = 1e-6
-    l1_capacity: int = 48
+    # per-pixel L1 sample capacity of the first forward attempt; None adapts to the
+    # largest count seen for this image size (a pixel over capacity triggers an exact
+    # per-pixel-offset rerun, so the value only affects speed and memory)
+    l1_capacity: int | None = None
 
     def extent(self):
         return self.trunc_sigma if self.mode == "ambisur" else self.sigma_extent
@@ -124,7 +127,8 @@ class _Plan:
     ranges: torch.Tensor | None = None
     n_isect: int = 0
     absgrad: torch.Tensor | None = None
-    l1_capacity: int = 48
+    l1_capacity: int | None = None
+    error_word: torch.Tensor | None = None
     stats: dict = field(default_factory=dict)
 
     @property
@@ -251,12 +255,16 @@ class _Raster(torch.autograd.Function):
         use_l1 = bool(plan.settings.distortions & 1)
         l1s, l1_off, cap, slots = None, None, 0, 0
         needed = None
+        key = (W, H)
         if use_l1:
-            cap = int(plan.l1_capacity)
-            slots = plan.n_tiles * cap * TILE * TILE
+            if plan.l1_capacity is not None:
+                cap = int(plan.l1_capacity)
+            else:
+                cap = _L1_SEEN.get(key, 256)
+            cap = max(32, (cap + 31) // 32 * 32)
+            slots = plan.n_tiles * TILE * TILE * cap
             l1s = torch.empty((L1_SAMPLE_FLOATS, slots), **f)
             needed = torch.zeros((1,), device=dev, dtype=torch.int32)
-
         counters = torch.zeros((2,), device=dev, dtype=torch.int64) if PROFILE is not None else None
 
         def run():
@@ -280,8 +288,12 @@ class _Raster(torch.autograd.Function):
         if use_l1:
             most = int(needed.item())
             plan.stats["l1_max_samples"] = most
+            plan.stats["l1_capacity"] = cap
+            if plan.l1_capacity is None:
+                _L1_SEEN[key] = max(32, int(most * 1.2 + 31) // 32 * 32)
             if most > cap:
                 # capacity exceeded somewhere: exact per-pixel (CSR) storage and a rerun
+                plan.stats["l1_rerun"] = True
                 ws_bytes = (H * W + 2048) * 8 + H * W * 4 + 4096
                 ws = torch.empty((ws_bytes,), device=dev, dtype=torch.uint8)
                 l1_off = torch.empty((H * W + 1,), device=dev, dtype=torch.int64)
@@ -292,7 +304,7 @@ class _Raster(torch.autograd.Function):
                 run()
             call(
                 "sf_b200_l1_resolve", ctypes.byref(plan.cam), ctypes.byref(plan.settings), _ptr(state),
-                _ptr(l1s), slots, _ptr(l1_off), cap, _ptr(l1), _stream(dev),
+                _ptr(l1s), slots, _ptr(l1_off), cap, most, _ptr(l1), _stream(dev),
             )
         ctx.save_for_backward(records)
         ctx.plan = plan
@@ -317,11 +329,12 @@ class _Raster(torch.autograd.Function):
         if PROFILE is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
+        plan.error_word = torch.zeros((1,), device=dev, dtype=torch.int32)
         call(
             "sf_b200_raster_backward", _ptr(records), n, _ptr(plan.ids), _ptr(plan.ranges),
             ctypes.byref(plan.cam), ctypes.byref(plan.settings), _ptr(ctx.state), _ptr(l1s), slots,
             _ptr(l1_off), cap, *(_ptr(g) for g in grads), _ptr(grad_records), _ptr(grad_means2d),
-            _ptr(absgrad), _stream(dev),
+            _ptr(absgrad), _ptr(plan.error_word), _stream(dev),
         )
         if ev is not None:
             ev[1].record()
@@ -360,4 +373,5 @@ def rasterize(means, quats, scales, opacities, sh, sh_degree, camera, settings, 
     out["projected_radii"] = radii
     out["n_isect"] = plan.n_isect
     out["stats"] = plan.stats
+    out["plan"] = plan
     return out

@@ -82,7 +82,7 @@ def render(params, camera, settings, *, selected=None, ups=None, cap=None):
     l1s = torch.zeros(L1_SAMPLE_FLOATS, slots) if (st.distortions & 1) else torch.zeros(1)
     h.hc_raster_forward(_p(records), _p(ids_t), _p(ranges), ctypes.byref(cam), ctypes.byref(st),
                         *(_p(imgs[name]) for name, _ in CH), _p(state), _p(l1s), slots, cap)
-    extras = {"means2d": means2d, "radii": radii, "records": records, "state": state, "ids": ids_t,
+    extras = {"means2d": means2d, "radii": radii, "records": records, "state": state, "ids": ids_t, "l1s": l1s, "cap": cap,
               "ranges": ranges}
     if ups is None:
         return imgs, None, extras
