@@ -158,6 +158,19 @@ int sf_b200_bin_emit(const int32_t* order, const int64_t* offsets, const int32_t
                      int32_t* isect_ids, int32_t* tile_ranges, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* Same result as sf_b200_bin_order, for callers that cannot allocate device memory
+ * (for instance a host application that owns the whole device budget through its own
+ * pool and lets no plugin call cudaMalloc).  No counterpart in the reference: it has
+ * no device path at all.  The scratch is a static array inside the library (about 21
+ * MB, held on every GPU that loads the library until exit); n is limited to
+ * SF_B200_STATIC_MAX_GAUSSIANS and larger counts return SF_ERR_CAPACITY.  Calls share
+ * that array: calls whose kernels overlap on the GPU race and must be serialised by
+ * the caller.  The first call on a device resolves the array's device address; make
+ * it before any stream capture.  Nothing is allocated or freed. */
+#define SF_B200_STATIC_MAX_GAUSSIANS 1048576
+int sf_b200_bin_order_static(const int32_t* tile_count, const uint32_t* depth_key, int64_t n,
+                             int32_t* order, int64_t* offsets, void* stream);
+
 /* 64-bit keys tile<<32 | depth bits of the sorted intersections (diagnostics/tests). */
 int sf_b200_bin_keys(const int32_t* isect_ids, const int32_t* tile_ranges,
                      const uint32_t* depth_key, int32_t n_tiles, int64_t n_isect,

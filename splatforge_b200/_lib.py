@@ -79,6 +79,7 @@ _SIGNATURES = {
         [P, P, P, c_int64, c_int64, c_int32, c_int32, P, P, P, c_size_t, P],
     ),
     "sf_b200_bin_keys": (ctypes.c_int, [P, P, P, c_int32, c_int64, P, P]),
+    "sf_b200_bin_order_static": (ctypes.c_int, [P, P, c_int64, P, P, P]),
     "sf_b200_raster_forward": (
         ctypes.c_int,
         [P, c_int64, P, P, POINTER(Camera), POINTER(Settings)]

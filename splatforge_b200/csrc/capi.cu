@@ -69,6 +69,8 @@ int tiles_of(const sf_camera* c, int* tx) {
 
 }  // namespace
 
+void sf::set_last_error(const char* msg) { snprintf(g_error, sizeof(g_error), "%s", msg); }
+
 extern "C" {
 
 const char* sf_b200_last_error(void) { return g_error; }

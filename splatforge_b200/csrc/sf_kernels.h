@@ -12,6 +12,8 @@ namespace sf {
 // kernels launched by this library (sf_b200_kernel_launches)
 void count_launches(int k);
 int64_t launches_total();
+// message returned by sf_b200_last_error() on this thread
+void set_last_error(const char* msg);
 
 struct RasterFwdArgs {
   const float* records;
