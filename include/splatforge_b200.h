@@ -176,6 +176,42 @@ int sf_b200_bin_keys(const int32_t* isect_ids, const int32_t* tile_ranges,
                      const uint32_t* depth_key, int32_t n_tiles, int64_t n_isect,
                      uint64_t* keys, void* stream);
 
+/* ---- splat.alpha_composite@3 over dense [B,N,P] (reference.py:151-186; replaces
+ * composite_cuda.cu:26-98 at the operator seam) -------------------------------------
+ * Inputs alphas/depths [B,N,P], colors [B,N,3], normals [B,N,P,3]; outputs rgb
+ * [B,P,3], alpha/znum/l1/l2/median [B,P], nnum [B,P,3], weights [B,N,P].  The
+ * workspace (size from sf_b200_composite_workspace_bytes) carries the L1 factors and
+ * the raw distortions from the forward call to the backward call. */
+int sf_b200_composite_workspace_bytes(int64_t B, int64_t N, int64_t P, int32_t distortions,
+                                      size_t* bytes);
+int sf_b200_alpha_composite_forward(const float* alphas, const float* colors, const float* depths,
+                                    const float* normals, int64_t B, int64_t N, int64_t P,
+                                    int32_t distortions, float* rgb, float* alpha, float* znum,
+                                    float* nnum, float* l1, float* l2, float* median,
+                                    float* weights, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+/* Any upstream adjoint may be NULL.  d_* outputs are overwritten. */
+int sf_b200_alpha_composite_backward(const float* alphas, const float* colors, const float* depths,
+                                     const float* normals, int64_t B, int64_t N, int64_t P,
+                                     int32_t distortions, const float* weights,
+                                     const void* workspace, size_t workspace_bytes,
+                                     const float* grad_rgb, const float* grad_alpha,
+                                     const float* grad_znum, const float* grad_nnum,
+                                     const float* grad_l1, const float* grad_l2,
+                                     const float* grad_median, const float* grad_weights,
+                                     float* d_alphas, float* d_colors, float* d_depths,
+                                     float* d_normals, void* stream);
+
+/* ---- gaussian.opacity_field@1 (reference.py:194-222) -------------------------------
+ * points [P,3], means [N,3], inverse_covariances [N,3,3], opacities [N], origins
+ * [C,3] (C >= 1) -> field [P] (forward only).  Workspace from
+ * sf_b200_opacity_field_workspace_bytes(N). */
+int sf_b200_opacity_field_workspace_bytes(int64_t n_gaussians, size_t* bytes);
+int sf_b200_opacity_field(const float* points, int64_t n_points, const float* means,
+                          const float* inverse_covariances, const float* opacities,
+                          int64_t n_gaussians, const float* origins, int32_t n_origins,
+                          float* field, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- raster forward (batched_renderer.py:169-338 + alpha_composite@3) -----------
  * One CTA per 16x16 tile.  Images are HWC float32: rgb/normals [H,W,3], the rest
  * [H,W].  pixel_state [H*W, SF_PIXEL_STATE_FLOATS] is kept for the backward pass.

@@ -80,6 +80,17 @@ _SIGNATURES = {
     ),
     "sf_b200_bin_keys": (ctypes.c_int, [P, P, P, c_int32, c_int64, P, P]),
     "sf_b200_bin_order_static": (ctypes.c_int, [P, P, c_int64, P, P, P]),
+    "sf_b200_opacity_field_workspace_bytes": (ctypes.c_int, [c_int64, POINTER(c_size_t)]),
+    "sf_b200_opacity_field": (ctypes.c_int, [P, c_int64, P, P, P, c_int64, P, c_int32, P, P, c_size_t, P]),
+    "sf_b200_composite_workspace_bytes": (ctypes.c_int, [c_int64, c_int64, c_int64, c_int32, POINTER(c_size_t)]),
+    "sf_b200_alpha_composite_forward": (
+        ctypes.c_int,
+        [P, P, P, P, c_int64, c_int64, c_int64, c_int32] + [P] * 8 + [P, c_size_t, P],
+    ),
+    "sf_b200_alpha_composite_backward": (
+        ctypes.c_int,
+        [P, P, P, P, c_int64, c_int64, c_int64, c_int32, P, P, c_size_t] + [P] * 8 + [P] * 4 + [P],
+    ),
     "sf_b200_raster_forward": (
         ctypes.c_int,
         [P, c_int64, P, P, POINTER(Camera), POINTER(Settings)]

@@ -255,8 +255,8 @@ __global__ void gather_counts_kernel(const int32_t* order, const int32_t* count,
   }
 }
 
-// One warp per 32 depth-ordered Gaussians; the warp walks their intersections
-// cooperatively so long and short rectangles share the lanes evenly.
+// One warp per 32 depth-ordered Gaussians: the warp writes each Gaussian's run of
+// intersections in turn, lanes covering consecutive entries (coalesced stores).
 __global__ void emit_kernel(const int32_t* order, const int64_t* offsets, const int32_t* rect,
                             int64_t n, int tiles_x, uint32_t* tiles, int32_t* ids) {
   const int lane = threadIdx.x & 31;
@@ -265,7 +265,7 @@ __global__ void emit_kernel(const int32_t* order, const int64_t* offsets, const 
   if (first >= n) return;
   const int64_t i = first + lane;
   int g = 0, x0 = 0, y0 = 0, w = 1;
-  int64_t o = 0, c = 0;
+  long long o = 0, c = 0;
   if (i < n) {
     g = order[i];
     o = offsets[i];
@@ -273,12 +273,19 @@ __global__ void emit_kernel(const int32_t* order, const int64_t* offsets, const 
     const int4 r = reinterpret_cast<const int4*>(rect)[g];
     x0 = r.x; y0 = r.y; w = r.z - r.x + 1;
   }
-  // each lane emits its own Gaussian's run; lanes with short runs then help none --
-  // rectangles are small (tens of tiles), so the simple form keeps writes contiguous
-  for (int64_t k = 0; k < c; ++k) {
-    const int ty = y0 + (int)(k / w), tx = x0 + (int)(k % w);
-    tiles[o + k] = (uint32_t)(ty * tiles_x + tx);
-    ids[o + k] = g;
+  for (int src = 0; src < 32; ++src) {
+    const long long cs = __shfl_sync(FULL, c, src);
+    if (cs == 0) continue;
+    const long long os = __shfl_sync(FULL, o, src);
+    const int gs = __shfl_sync(FULL, g, src);
+    const int xs = __shfl_sync(FULL, x0, src), ys = __shfl_sync(FULL, y0, src), ws = __shfl_sync(FULL, w, src);
+    for (long long k = lane; k < cs; k += 32) {
+      const int kk = (int)k;
+      const int row = kk / ws;
+      const int col = kk - row * ws;
+      tiles[os + k] = (uint32_t)((ys + row) * tiles_x + xs + col);
+      ids[os + k] = gs;
+    }
   }
 }
 

@@ -300,4 +300,86 @@ int sf_b200_raster_backward(const float* records, int64_t n, const int32_t* isec
   return cuda_status(e, "raster_backward");
 }
 
+int sf_b200_opacity_field_workspace_bytes(int64_t n_gaussians, size_t* bytes) {
+  if (n_gaussians < 0 || !bytes) return fail(SF_ERR_ARGUMENT, "opacity_field_workspace_bytes: bad arguments");
+  *bytes = sf::field_workspace_bytes(n_gaussians);
+  return SF_OK;
+}
+
+int sf_b200_opacity_field(const float* points, int64_t n_points, const float* means, const float* inverse_covariances,
+                          const float* opacities, int64_t n_gaussians, const float* origins, int32_t n_origins,
+                          float* field, void* workspace, size_t workspace_bytes, void* stream) {
+  if (n_points < 0 || n_gaussians < 0) return fail(SF_ERR_ARGUMENT, "opacity_field: negative size");
+  if (n_origins < 1 || n_origins > 65535) return fail(SF_ERR_ARGUMENT, "opacity_field: requires 1..65535 origins");
+  if (n_points > 0 && (!points || !field || !origins)) return fail(SF_ERR_ARGUMENT, "opacity_field: NULL buffer");
+  if (n_gaussians > 0 && (!means || !inverse_covariances || !opacities || !workspace))
+    return fail(SF_ERR_ARGUMENT, "opacity_field: NULL buffer");
+  if (workspace_bytes < sf::field_workspace_bytes(n_gaussians))
+    return fail(SF_ERR_CAPACITY, "opacity_field: workspace too small");
+  return cuda_status(sf::launch_opacity_field(points, n_points, means, inverse_covariances, opacities, n_gaussians,
+                                              origins, n_origins, field, workspace, as_stream(stream)),
+                     "opacity_field");
+}
+
+int sf_b200_composite_workspace_bytes(int64_t B, int64_t N, int64_t P, int32_t distortions, size_t* bytes) {
+  if (B < 0 || N < 0 || P < 0 || !bytes) return fail(SF_ERR_ARGUMENT, "composite_workspace_bytes: bad arguments");
+  const size_t aux = (distortions & SF_DIST_L1) ? (size_t)2 * B * N * P * sizeof(float) : 0;
+  *bytes = aux + (size_t)2 * B * P * sizeof(float) + 256;
+  return SF_OK;
+}
+
+namespace {
+int composite_checks(int64_t B, int64_t N, int64_t P, int32_t dist, size_t ws_bytes, const char* where) {
+  if (B < 0 || N < 0 || P < 0) return fail(SF_ERR_ARGUMENT, "%s: negative size", where);
+  if (dist < 0 || dist > 3) return fail(SF_ERR_ARGUMENT, "%s: distortions must be none/l1/l2/both", where);
+  if (B * N * P >= (int64_t)1 << 40 || B * P > 0x7fffffffLL * 128 || N > 0x7fffffffLL)
+    return fail(SF_ERR_ARGUMENT, "%s: sizes too large", where);
+  size_t need = 0;
+  sf_b200_composite_workspace_bytes(B, N, P, dist, &need);
+  if (ws_bytes < need) return fail(SF_ERR_CAPACITY, "%s: workspace of %zu bytes, %zu needed", where, ws_bytes, need);
+  if ((dist & SF_DIST_L1) && sf::composite_l1_smem_per_warp((int)N) > 200 * 1024)
+    return fail(SF_ERR_CAPACITY, "%s: L1 over %lld samples exceeds the shared-memory sort", where, (long long)N);
+  return SF_OK;
+}
+}  // namespace
+
+int sf_b200_alpha_composite_forward(const float* alphas, const float* colors, const float* depths, const float* normals,
+                                    int64_t B, int64_t N, int64_t P, int32_t distortions, float* rgb, float* alpha,
+                                    float* znum, float* nnum, float* l1, float* l2, float* median, float* weights,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = composite_checks(B, N, P, distortions, workspace_bytes, "alpha_composite_forward"))) return rc;
+  if (B * P > 0 && (!rgb || !alpha || !znum || !nnum || !l1 || !l2 || !median || !workspace))
+    return fail(SF_ERR_ARGUMENT, "alpha_composite_forward: NULL output");
+  if (B * N * P > 0 && (!alphas || !colors || !depths || !normals || !weights))
+    return fail(SF_ERR_ARGUMENT, "alpha_composite_forward: NULL input");
+  float* raw = reinterpret_cast<float*>(workspace);
+  float* aux = (distortions & SF_DIST_L1) ? raw + 2 * B * P : nullptr;
+  return cuda_status(sf::launch_composite_forward(alphas, colors, depths, normals, (int)B, (int)N, (int)P, distortions,
+                                                  rgb, alpha, znum, nnum, l1, l2, median, weights, aux, raw,
+                                                  as_stream(stream)),
+                     "alpha_composite_forward");
+}
+
+int sf_b200_alpha_composite_backward(const float* alphas, const float* colors, const float* depths,
+                                     const float* normals, int64_t B, int64_t N, int64_t P, int32_t distortions,
+                                     const float* weights, const void* workspace, size_t workspace_bytes,
+                                     const float* grad_rgb, const float* grad_alpha, const float* grad_znum,
+                                     const float* grad_nnum, const float* grad_l1, const float* grad_l2,
+                                     const float* grad_median, const float* grad_weights, float* d_alphas,
+                                     float* d_colors, float* d_depths, float* d_normals, void* stream) {
+  int rc;
+  if ((rc = composite_checks(B, N, P, distortions, workspace_bytes, "alpha_composite_backward"))) return rc;
+  if (B * N * P > 0 && (!alphas || !colors || !depths || !normals || !weights || !workspace || !d_alphas ||
+                        !d_colors || !d_depths || !d_normals))
+    return fail(SF_ERR_ARGUMENT, "alpha_composite_backward: NULL buffer");
+  const float* raw = reinterpret_cast<const float*>(workspace);
+  const float* aux = (distortions & SF_DIST_L1) ? raw + 2 * B * P : nullptr;
+  return cuda_status(sf::launch_composite_backward(alphas, colors, depths, normals, (int)B, (int)N, (int)P,
+                                                   distortions, weights, aux, raw, grad_rgb, grad_alpha, grad_znum,
+                                                   grad_nnum, grad_l1, grad_l2, grad_median, grad_weights, d_alphas,
+                                                   d_colors, d_depths, d_normals, as_stream(stream)),
+                     "alpha_composite_backward");
+}
+
 }  // extern "C"

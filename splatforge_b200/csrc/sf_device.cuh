@@ -70,4 +70,70 @@ __device__ __forceinline__ float reduce16_transposed(float (&v)[16], int lane) {
   return v[0];
 }
 
+// Stable LSD radix sort of n <= capacity (key, value) pairs held in shared memory by
+// one warp: 8-bit digits, bytes that are equal in every key skipped, ranks from
+// __match_any_sync.  The result lands in (*kout, *vout), one of the two buffers.
+__device__ __forceinline__ void warp_radix_sort_u32(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1,
+                                                uint32_t* hist, int n, int lane, uint32_t** kout,
+                                                uint32_t** vout) {
+  uint32_t orv = 0u, andv = 0xffffffffu;
+  for (int i = lane; i < n; i += 32) { orv |= k0[i]; andv &= k0[i]; }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    orv |= __shfl_xor_sync(FULL, orv, o);
+    andv &= __shfl_xor_sync(FULL, andv, o);
+  }
+  const uint32_t vary = orv ^ andv;
+  const unsigned lt = (1u << lane) - 1u;
+  uint32_t *ki = k0, *vi = v0, *ko = k1, *vo = v1;
+  for (int shift = 0; shift < 32; shift += 8) {
+    if (((vary >> shift) & 0xffu) == 0u) continue;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) hist[lane * 8 + b] = 0u;
+    __syncwarp();
+    for (int c = 0; c < n; c += 32) {
+      const int i = c + lane;
+      const bool valid = i < n;
+      const uint32_t d = valid ? (ki[i] >> shift) & 0xffu : 0u;
+      const unsigned peers = __match_any_sync(FULL, valid ? d : 0x100u + lane);
+      if (valid && lane == __ffs(peers) - 1) hist[d] += __popc(peers);
+      __syncwarp();
+    }
+    // exclusive scan of the 256 counts: 8 per lane
+    uint32_t loc[8], sum = 0u;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) { loc[b] = hist[lane * 8 + b]; sum += loc[b]; }
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(FULL, incl, o);
+      if (lane >= o) incl += y;
+    }
+    uint32_t run = incl - sum;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) { hist[lane * 8 + b] = run; run += loc[b]; }
+    __syncwarp();
+    for (int c = 0; c < n; c += 32) {
+      const int i = c + lane;
+      const bool valid = i < n;
+      const uint32_t key = valid ? ki[i] : 0u;
+      const uint32_t d = (key >> shift) & 0xffu;
+      const unsigned peers = __match_any_sync(FULL, valid ? d : 0x100u + lane);
+      const uint32_t base = valid ? hist[d] : 0u;
+      __syncwarp();
+      if (valid) {
+        const uint32_t pos = base + __popc(peers & lt);
+        ko[pos] = key;
+        vo[pos] = vi[i];
+        if (lane == 31 - __clz(peers)) hist[d] = base + __popc(peers);
+      }
+      __syncwarp();
+    }
+    uint32_t* t = ki; ki = ko; ko = t;
+    t = vi; vi = vo; vo = t;
+  }
+  *kout = ki;
+  *vout = vi;
+}
+
 }  // namespace sf

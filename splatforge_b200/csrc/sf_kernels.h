@@ -80,6 +80,25 @@ cudaError_t launch_sh_backward(const float* coeffs, int K, const float* dirs, in
                                int degree, const float* grgb, float* gcoeffs, float* gdirs,
                                cudaStream_t s);
 
+// splat.alpha_composite@3 over dense [B, N, P]
+size_t composite_l1_smem_per_warp(int n);
+cudaError_t launch_composite_forward(const float* al, const float* col, const float* dep, const float* nrm, int B,
+                                     int N, int P, int dist, float* rgb, float* alpha, float* znum, float* nnum,
+                                     float* l1, float* l2, float* median, float* w, float* aux, float* raw,
+                                     cudaStream_t s);
+cudaError_t launch_composite_backward(const float* al, const float* col, const float* dep, const float* nrm, int B,
+                                      int N, int P, int dist, const float* w, const float* aux, const float* raw,
+                                      const float* g_rgb, const float* g_alpha, const float* g_znum,
+                                      const float* g_nnum, const float* g_l1, const float* g_l2,
+                                      const float* g_median, const float* g_w, float* da, float* dc, float* dd,
+                                      float* dn, cudaStream_t s);
+
+// gaussian.opacity_field@1
+size_t field_workspace_bytes(int64_t n);
+cudaError_t launch_opacity_field(const float* pts, int64_t np, const float* means, const float* invcov,
+                                 const float* op, int64_t ng, const float* origins, int nc, float* out, void* ws,
+                                 cudaStream_t s);
+
 // binning / sorting
 cudaError_t launch_bin_rects(const float* bounds, int64_t n, int width, int height, int tile,
                              float near_plane, float far_plane, int32_t* rect, int32_t* count,

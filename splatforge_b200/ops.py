@@ -1,0 +1,160 @@
+"""Operator runners with the Torch provider's signatures, backed by libsf_b200.so.
+
+Each runner takes exactly the positional tensors and keyword attributes SplatForge's
+operator validator passes (src/splatforge/gaussian/ops.py:23-51, 54-172) and returns
+what the Torch provider's function returns:
+
+* ``covariance(quats, scales)``                      gaussian.covariance@1 (reference.py:33-35)
+* ``sh_color(coefficients, directions, *, degree)``  gaussian.sh_color@1   (reference.py:85-113)
+* ``alpha_composite_selected(alphas, colors, depths, normals, *, distortions)``
+                                                     splat.alpha_composite@3 (reference.py:182-186)
+* ``opacity_field(points, means, inverse_covariances, opacities, origins, *, gaussian_chunk)``
+                                                     gaussian.opacity_field@1 (reference.py:194-222)
+
+They accept CUDA float32 tensors only and raise ``ValueError`` otherwise, like the
+reference's CUDA composite provider (cuda_composite.py:79-85); nothing falls back
+to Torch.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import call
+from .rasterizer import _ptr, _stream
+
+
+def _require_cuda_f32(name, *tensors):
+    for t in tensors:
+        if not isinstance(t, torch.Tensor) or t.device.type != "cuda" or t.dtype != torch.float32:
+            raise ValueError(f"{name} requires explicit CUDA float32 tensors (no fallback)")
+    dev = tensors[0].device
+    if any(t.device != dev for t in tensors):
+        raise ValueError(f"{name}: tensors must share one device")
+    return dev
+
+
+# ---------------------------------------------------------------- gaussian.covariance@1
+class _Covariance(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, quats, scales):
+        dev = quats.device
+        q, s = quats.contiguous(), scales.contiguous()
+        n = q.shape[0]
+        cov = torch.empty((n, 3, 3), device=dev, dtype=torch.float32)
+        call("sf_b200_covariance_forward", _ptr(q), _ptr(s), n, _ptr(cov), _stream(dev))
+        ctx.save_for_backward(q, s)
+        return cov
+
+    @staticmethod
+    def backward(ctx, g):
+        q, s = ctx.saved_tensors
+        dev = q.device
+        gq = torch.empty_like(q) if ctx.needs_input_grad[0] else None
+        gs = torch.empty_like(s) if ctx.needs_input_grad[1] else None
+        call("sf_b200_covariance_backward", _ptr(q), _ptr(s), q.shape[0], _ptr(g.contiguous()), _ptr(gq), _ptr(gs),
+             _stream(dev))
+        return gq, gs
+
+
+def covariance(quats, scales):
+    with torch.cuda.device(_require_cuda_f32("gaussian.covariance@1", quats, scales)):
+        return _Covariance.apply(quats, scales)
+
+
+# ---------------------------------------------------------------- gaussian.sh_color@1
+class _ShColor(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, coeffs, dirs, degree):
+        dev = coeffs.device
+        c, d = coeffs.contiguous(), dirs.contiguous()
+        n, K = c.shape[0], c.shape[1]
+        out = torch.empty((n, 3), device=dev, dtype=torch.float32)
+        call("sf_b200_sh_color_forward", _ptr(c), K, _ptr(d), n, degree, _ptr(out), _stream(dev))
+        ctx.save_for_backward(c, d)
+        ctx.degree = degree
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        c, d = ctx.saved_tensors
+        dev = c.device
+        gc = torch.empty_like(c) if ctx.needs_input_grad[0] else None
+        gd = torch.empty_like(d) if ctx.needs_input_grad[1] else None
+        call("sf_b200_sh_color_backward", _ptr(c), c.shape[1], _ptr(d), c.shape[0], ctx.degree, _ptr(g.contiguous()),
+             _ptr(gc), _ptr(gd), _stream(dev))
+        return gc, gd, None
+
+
+def sh_color(coefficients, directions, *, degree):
+    with torch.cuda.device(_require_cuda_f32("gaussian.sh_color@1", coefficients, directions)):
+        return _ShColor.apply(coefficients, directions, int(degree))
+
+
+# ---------------------------------------------------------------- splat.alpha_composite@3
+class _Composite(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, c, d, n, dist):
+        dev = a.device
+        a, c, d, n = (t.contiguous() for t in (a, c, d, n))
+        B, N, P = a.shape
+        f = dict(device=dev, dtype=torch.float32)
+        rgb = torch.empty((B, P, 3), **f)
+        alpha = torch.empty((B, P), **f)
+        znum = torch.empty((B, P), **f)
+        nnum = torch.empty((B, P, 3), **f)
+        l1 = torch.empty((B, P), **f)
+        l2 = torch.empty((B, P), **f)
+        median = torch.empty((B, P), **f)
+        w = torch.empty((B, N, P), **f)
+        size = ctypes.c_size_t()
+        call("sf_b200_composite_workspace_bytes", B, N, P, dist, ctypes.byref(size))
+        ws = torch.empty((size.value,), device=dev, dtype=torch.uint8)
+        call("sf_b200_alpha_composite_forward", _ptr(a), _ptr(c), _ptr(d), _ptr(n), B, N, P, dist, _ptr(rgb),
+             _ptr(alpha), _ptr(znum), _ptr(nnum), _ptr(l1), _ptr(l2), _ptr(median), _ptr(w), _ptr(ws), size.value,
+             _stream(dev))
+        ctx.save_for_backward(a, c, d, n, w, ws)
+        ctx.dist = dist
+        ctx.set_materialize_grads(False)
+        return rgb, alpha, znum, nnum, l1, l2, median, w
+
+    @staticmethod
+    def backward(ctx, g_rgb, g_alpha, g_znum, g_nnum, g_l1, g_l2, g_median, g_w):
+        a, c, d, n, w, ws = ctx.saved_tensors
+        dev = a.device
+        B, N, P = a.shape
+        grads = [None if g is None else g.contiguous() for g in (g_rgb, g_alpha, g_znum, g_nnum, g_l1, g_l2, g_median, g_w)]
+        da, dc, dd, dn = (torch.empty_like(t) for t in (a, c, d, n))
+        call("sf_b200_alpha_composite_backward", _ptr(a), _ptr(c), _ptr(d), _ptr(n), B, N, P, ctx.dist, _ptr(w),
+             _ptr(ws), ws.numel(), *(_ptr(g) for g in grads), _ptr(da), _ptr(dc), _ptr(dd), _ptr(dn), _stream(dev))
+        return da, dc, dd, dn, None
+
+
+def alpha_composite_selected(alphas, colors, depths, normals, *, distortions):
+    if distortions not in _lib.DISTORTIONS:
+        raise ValueError("distortions must explicitly be none, l1, l2 or both")
+    dev = _require_cuda_f32("splat.alpha_composite@3", alphas, colors, depths, normals)
+    with torch.cuda.device(dev):
+        return _Composite.apply(alphas, colors, depths, normals, _lib.DISTORTIONS[distortions])
+
+
+# ---------------------------------------------------------------- gaussian.opacity_field@1
+def opacity_field(points, means, inverse_covariances, opacities, origins, *, gaussian_chunk=1024):
+    """Forward only (the manifest declares ``backward: false``).  ``gaussian_chunk``
+    only affects the reference's memory use; the field does not depend on it."""
+    dev = _require_cuda_f32("gaussian.opacity_field@1", points, means, inverse_covariances, opacities, origins)
+    del gaussian_chunk
+    if origins.shape[0] < 1:
+        raise ValueError("opacity field requires at least one origin")
+    with torch.cuda.device(dev), torch.no_grad():
+        p, m, q, o, org = (t.contiguous() for t in (points, means, inverse_covariances, opacities, origins))
+        out = torch.empty((p.shape[0],), device=dev, dtype=torch.float32)
+        size = ctypes.c_size_t()
+        call("sf_b200_opacity_field_workspace_bytes", m.shape[0], ctypes.byref(size))
+        ws = torch.empty((size.value,), device=dev, dtype=torch.uint8)
+        call("sf_b200_opacity_field", _ptr(p), p.shape[0], _ptr(m), _ptr(q), _ptr(o), m.shape[0], _ptr(org),
+             org.shape[0], _ptr(out), _ptr(ws), size.value, _stream(dev))
+    return out

@@ -1,0 +1,113 @@
+"""Operator runners (gaussian.covariance@1, gaussian.sh_color@1,
+splat.alpha_composite@3, gaussian.opacity_field@1) on the GPU against the reference's
+golden fixtures and the CPU oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops as oracle_ops
+from splatforge_b200 import ops
+from tests._util import rel_err
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def T(a, grad=False):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+    return t.requires_grad_() if grad else t
+
+
+def test_covariance_matches_reference_fixture_and_gradients(golden):
+    f = golden("ops")
+    q, s = T(f["cov/quats"], True), T(f["cov/scales"], True)
+    cov = ops.covariance(q, s)
+    np.testing.assert_allclose(cov.detach().cpu().numpy(), f["cov/out"], atol=1e-6)
+    g = torch.randn(cov.shape, generator=torch.Generator().manual_seed(3)).to(DEV)
+    gq, gs = torch.autograd.grad((cov * g).sum(), (q, s))
+    qc, sc = torch.from_numpy(f["cov/quats"]).requires_grad_(), torch.from_numpy(f["cov/scales"]).requires_grad_()
+    wq, ws = torch.autograd.grad((oracle_ops.covariance(qc, sc) * g.cpu()).sum(), (qc, sc))
+    assert rel_err(gq.cpu(), wq) < 1e-4 and rel_err(gs.cpu(), ws) < 1e-4
+
+
+@pytest.mark.parametrize("degree", [0, 1, 2, 3])
+def test_sh_color_matches_reference_fixture(golden, degree):
+    f = golden("ops")
+    sh, d = T(f["sh/coeffs"], True), T(f["sh/dirs"], True)
+    col = ops.sh_color(sh, d, degree=degree)
+    np.testing.assert_allclose(col.detach().cpu().numpy(), f[f"sh/deg{degree}/out"], atol=1e-6)
+    gs, gd = torch.autograd.grad((col * T(f[f"sh/deg{degree}/up"])).sum(), (sh, d))
+    np.testing.assert_allclose(gs.cpu().numpy(), f[f"sh/deg{degree}/gcoeffs"], atol=1e-6)
+    np.testing.assert_allclose(gd.cpu().numpy(), f[f"sh/deg{degree}/gdirs"], atol=2e-5)
+
+
+@pytest.mark.parametrize("profile", ["none", "l1", "l2", "both"])
+def test_alpha_composite_matches_reference_fixture(golden, profile):
+    """Includes alphas clamped at 0.999 and at 0 (no adjoint through the clamp)."""
+    f = golden("ops")
+    ins = [T(f[f"comp/{k}"], True) for k in "acdn"]
+    res = ops.alpha_composite_selected(*ins, distortions=profile)
+    for i, r in enumerate(res):
+        np.testing.assert_allclose(r.detach().cpu().numpy(), f[f"comp/{profile}/out{i}"], atol=2e-6, err_msg=f"out{i}")
+    loss = sum((r * T(f[f"comp/up{i}"])).sum() for i, r in enumerate(res))
+    grads = torch.autograd.grad(loss, ins)
+    for name, g in zip("acdn", grads):
+        np.testing.assert_allclose(g.cpu().numpy(), f[f"comp/{profile}/g{name}"], atol=5e-5, err_msg=name)
+
+
+@pytest.mark.parametrize("profile", ["l1", "both"])
+def test_alpha_composite_large_against_oracle(profile):
+    g = torch.Generator().manual_seed(11)
+    B, N, P = 4, 300, 256
+    a = (torch.rand(B, N, P, generator=g) * 0.3)
+    c = torch.rand(B, N, 3, generator=g)
+    d = torch.rand(B, N, P, generator=g) * 3 + 1
+    n = torch.randn(B, N, P, 3, generator=g)
+    ups = None
+    outs = {}
+    for side in ("gpu", "cpu"):
+        ins = [t.clone().to(DEV if side == "gpu" else "cpu").requires_grad_() for t in (a, c, d, n)]
+        fn = ops.alpha_composite_selected if side == "gpu" else oracle_ops.alpha_composite_batch
+        res = fn(*ins, distortions=profile)
+        if ups is None:
+            ups = [torch.randn(r.shape, generator=g) for r in res]
+        loss = sum((r * u.to(r.device)).sum() for r, u in zip(res, ups))
+        outs[side] = ([r.detach().cpu() for r in res], [x.cpu() for x in torch.autograd.grad(loss, ins)])
+    for i, (x, y) in enumerate(zip(outs["gpu"][0], outs["cpu"][0])):
+        np.testing.assert_allclose(x.numpy(), y.numpy(), atol=1e-4, rtol=1e-4, err_msg=f"out{i}")
+    for name, x, y in zip("acdn", outs["gpu"][1], outs["cpu"][1]):
+        assert rel_err(x, y) < 1e-3, name
+
+
+def test_composite_rejects_cpu_and_bad_profile():
+    x = torch.rand(1, 2, 3)
+    with pytest.raises(ValueError):
+        ops.alpha_composite_selected(x, torch.rand(1, 2, 3), x, torch.rand(1, 2, 3, 3), distortions="both")
+    with pytest.raises(ValueError):
+        y = x.to(DEV)
+        ops.alpha_composite_selected(y, torch.rand(1, 2, 3, device=DEV), y, torch.rand(1, 2, 3, 3, device=DEV),
+                                     distortions="l3")
+
+
+def test_opacity_field_matches_reference_fixture(golden):
+    f = golden("ops")
+    out = ops.opacity_field(*(T(f[f"field/{k}"]) for k in ("p", "m", "Q", "o", "origins")))
+    np.testing.assert_allclose(out.cpu().numpy(), f["field/out"], atol=1e-6)
+
+
+def test_opacity_field_larger_against_oracle():
+    g = torch.Generator().manual_seed(5)
+    P, N, C = 3000, 2000, 5
+    pts = torch.randn(P, 3, generator=g) * 0.7
+    m = torch.randn(N, 3, generator=g) * 0.6
+    L = torch.randn(N, 3, 3, generator=g) * 0.05
+    cov = L @ L.transpose(-1, -2) + 1e-3 * torch.eye(3)
+    Q = torch.linalg.inv(cov)
+    op = torch.rand(N, generator=g)
+    origins = torch.randn(C, 3, generator=g) * 3
+    want = oracle_ops.opacity_field(pts, m, Q, op, origins)
+    got = ops.opacity_field(*(t.to(DEV) for t in (pts, m, Q, op, origins)))
+    np.testing.assert_allclose(got.cpu().numpy(), want.numpy(), atol=2e-5)
