@@ -119,15 +119,13 @@ def algorithmic_flops(mode, n_pairs_fwd):
 def run_b200(args):
     import torch.distributed as dist
 
-    from splatforge_b200 import rasterizer, scenes
+    from splatforge_b200 import distributed, rasterizer, scenes
     from splatforge_b200.renderer import B200Renderer
     from splatforge_b200.rasterizer import RasterSettings
 
-    rank, world, local = dist_env()
+    rank, world, local = distributed.init_from_env(backend="nccl", timeout_s=300)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=300))
     params, _ = scenes.workload(args.workload, seed=0)
     base_cam = scenes.workload(args.workload, seed=0)[1][0]
     cams = scenes.orbit_cameras(max(8, world), base_cam.width, base_cam.height, 60.0 if "1080" in args.workload else 50.0,
@@ -139,7 +137,7 @@ def run_b200(args):
     ups = {ch: torch.randn(H, W, 3 if ch in ("rgb", "normals") else 1, generator=g).to(dev) for ch in CHANNELS}
     p = params.to(dev).requires_grad_()
     n = p.means.shape[0]
-    flat_grad = torch.empty((n, 59), device=dev)
+    reducer = distributed.GradientAllReduce(p.tensors())
 
     prof = {"fwd": [], "bwd": []}
 
@@ -150,9 +148,7 @@ def run_b200(args):
         out = rasterizer.rasterize(view.means, view.quats, view.scales, view.opacities, view.sh, 3, cam, settings)
         loss = sum((out[ch] * ups[ch]).sum() for ch in CHANNELS)
         loss.backward()
-        if world > 1:
-            torch.cat([t.grad.reshape(n, -1) for t in p.tensors()], 1, out=flat_grad)
-            dist.all_reduce(flat_grad)
+        reducer()
         return out
 
     for _ in range(args.warmup):
@@ -196,6 +192,7 @@ def run_b200(args):
         dev_params = [torch.empty_like(t, device=dev) for t in host]
         h2d = sum(t.numel() * t.element_size() for t in host)
         loss_host = torch.empty((), pin_memory=True)
+        e2e_reducer = distributed.GradientAllReduce(dev_params)
 
         def e2e_step():
             for d, h in zip(dev_params, host):
@@ -208,9 +205,7 @@ def run_b200(args):
             o = renderer.render(v, cam, distortions=args.distortions)
             loss = sum((getattr(o, ch) * ups[ch]).sum() for ch in CHANNELS)
             loss.backward()
-            if world > 1:
-                torch.cat([d.grad.reshape(n, -1) for d in dev_params], 1, out=flat_grad)
-                dist.all_reduce(flat_grad)
+            e2e_reducer()
             loss_host.copy_(loss.detach(), non_blocking=True)
             for d in dev_params:
                 d.requires_grad_(False)

@@ -1,0 +1,108 @@
+"""View-sharded data parallelism for training on a batch of views (one process per GPU).
+
+The reference trains one view per step on one device (src/splatforge/studio/trainer.py:
+218-248) and has no distributed code.  Here a step's batch of views is split across the
+ranks of one node; the Gaussians are replicated; every rank renders its views forward
+and backward through the B200 rasterizer, then the per-Gaussian parameter gradients are
+summed across ranks with ONE all-reduce of a contiguous [N, 11 + 3K] float32 buffer
+(means 3, log-scales 3, quaternion 4, opacity logit 1, SH 3K; 59 floats for SH degree
+3) over NCCL (NVLink / NVSwitch), so that identical optimiser steps keep the replicas
+in sync.
+
+The rendering itself is independent per view, so no collective sits inside the
+rasterizer; the all-reduce is ~2(n-1)/n * 236 MB per step for a million Gaussians.
+"""
+
+from __future__ import annotations
+
+import datetime
+import math
+import os
+
+import torch
+import torch.distributed as dist
+
+PARAM_ORDER = ("means", "log_scales", "quats", "opacity_logits", "sh")
+
+
+def shard(items, rank, world):
+    """Contiguous block partition of a batch of views: rank r gets items
+    [r*len/world, (r+1)*len/world)."""
+    n = len(items)
+    lo, hi = rank * n // world, (rank + 1) * n // world
+    return items[lo:hi]
+
+
+def init_from_env(backend=None, timeout_s=120):
+    """``torch.distributed`` from torchrun's RANK / WORLD_SIZE / LOCAL_RANK / MASTER_*.
+    NCCL on CUDA (device bound to LOCAL_RANK), gloo otherwise.  A short timeout makes
+    ranks that wait for a failed peer end with an error instead of hanging."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world == 1:
+        return rank, world, local
+    if backend is None:
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+    kwargs = {"timeout": datetime.timedelta(seconds=timeout_s)}
+    if backend == "nccl":
+        torch.cuda.set_device(local)
+        kwargs["device_id"] = torch.device("cuda", local)
+    dist.init_process_group(backend, **kwargs)
+    return rank, world, local
+
+
+class GradientAllReduce:
+    """Sums (or averages) the gradients of the Gaussian parameters across ranks with one
+    collective on a packed [N, 11 + 3K] buffer.
+
+    ``params`` is a sequence of the five parameter tensors in PARAM_ORDER (each [N, ...]).
+    The packed buffer is allocated once and reused every step.
+    """
+
+    def __init__(self, params, *, group=None, average=False):
+        self.params = list(params)
+        if len(self.params) != len(PARAM_ORDER):
+            raise ValueError("expected means, log_scales, quats, opacity_logits, sh")
+        n = self.params[0].shape[0]
+        if any(p.shape[0] != n for p in self.params):
+            raise ValueError("all parameters must have the Gaussian count as their first dimension")
+        self.widths = [math.prod(p.shape[1:]) for p in self.params]
+        self.n = n
+        self.group = group
+        self.average = average
+        self.buffer = torch.empty((n, sum(self.widths)), device=self.params[0].device, dtype=torch.float32)
+
+    @property
+    def floats_per_gaussian(self):
+        return sum(self.widths)
+
+    def pack(self):
+        col = 0
+        for p, w in zip(self.params, self.widths):
+            view = self.buffer[:, col : col + w]
+            if p.grad is None:
+                view.zero_()
+            else:
+                view.copy_(p.grad.reshape(self.n, w))
+            col += w
+        return self.buffer
+
+    def unpack(self):
+        col = 0
+        for p, w in zip(self.params, self.widths):
+            g = self.buffer[:, col : col + w].reshape(p.shape)
+            if p.grad is None:
+                p.grad = g.clone()
+            else:
+                p.grad.copy_(g)
+            col += w
+
+    def __call__(self):
+        if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(self.group) == 1:
+            return
+        self.pack()
+        dist.all_reduce(self.buffer, op=dist.ReduceOp.SUM, group=self.group)
+        if self.average:
+            self.buffer /= dist.get_world_size(self.group)
+        self.unpack()

@@ -1,0 +1,99 @@
+"""View-sharded data parallelism on CPU ranks (gloo, world size 2).
+
+The per-view renders are the CPU oracle's (these tests check the host-side
+plumbing: sharding, packing of the [N, 59] gradient buffer, the all-reduce and the
+failure behaviour), so no GPU is needed.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import render as oracle_render
+from splatforge_b200 import distributed, scenes
+
+CH = ("rgb", "depth", "distortion_l1")
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _grads_for(views, params):
+    p = params.detach_clone().requires_grad_()
+    for cam in views:
+        out = oracle_render.render(scenes.activated(p), cam, mode="gof", distortions="l1")
+        sum(out[c].sum() for c in CH).backward()
+    return p
+
+
+def _worker(rank, world, port, mode, queue):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                          LOCAL_RANK=str(rank))
+        torch.set_num_threads(1)
+        distributed.init_from_env(backend="gloo", timeout_s=10)
+        params, cams = scenes.workload("demo48", seed=0)
+        mine = distributed.shard(cams[:4], rank, world)
+        if mode == "fail" and rank == 1:
+            raise RuntimeError("rank 1 failed before the all-reduce")
+        p = _grads_for(mine, params)
+        reducer = distributed.GradientAllReduce(p.tensors())
+        assert reducer.floats_per_gaussian == 59
+        reducer()
+        queue.put((rank, "ok", [t.grad.clone() for t in p.tensors()]))
+    except Exception as exc:  # report to the parent instead of hanging
+        queue.put((rank, "error", f"{type(exc).__name__}: {exc}\n{traceback.format_exc()[-400:]}"))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _run(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    results = {}
+    for _ in procs:
+        rank, status, payload = q.get(timeout=120)
+        results[rank] = (status, payload)
+    for pr in procs:
+        pr.join(timeout=60)
+        if pr.is_alive():
+            pr.kill()
+    return results
+
+
+def test_allreduced_gradients_equal_full_batch_gradients():
+    res = _run("ok")
+    assert all(s == "ok" for s, _ in res.values()), res
+    params, cams = scenes.workload("demo48", seed=0)
+    full = _grads_for(cams[:4], params)
+    for rank in (0, 1):
+        for got, want in zip(res[rank][1], full.tensors()):
+            torch.testing.assert_close(got, want.grad, atol=2e-5, rtol=1e-4)
+
+
+def test_failed_rank_ends_its_peer_with_an_error_not_a_hang():
+    res = _run("fail")
+    assert res[1][0] == "error" and "rank 1 failed" in res[1][1]
+    assert res[0][0] == "error", "the surviving rank must see an error from the collective"
+
+
+def test_shard_partitions_views():
+    views = list(range(10))
+    parts = [distributed.shard(views, r, 4) for r in range(4)]
+    assert sum(parts, []) == views
+    assert max(map(len, parts)) - min(map(len, parts)) <= 1
