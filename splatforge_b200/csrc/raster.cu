@@ -221,6 +221,94 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
 //   auxd_i = 2 w_i (2 W_<i + w_i - W)                 (dL1/dd_i)
 // (composite_cuda.cu:54-65 computes the same factors from torch's sort order).  The
 // two factors replace (d_i, w_i) in place, written back contiguously.
+// Register bitonic sort of one pixel's n <= 32*I samples, I per lane in blocked layout
+// (lane l holds sorted positions l*I .. l*I+I-1); strides below I are compare-exchanges
+// inside a lane, larger strides exchange with lane ^ (stride / I) by shuffle.  Ties are
+// ordered by compositing index.  Then the sorted prefix sums, the L1 value and the two
+// factors per sample, written back in place (by compositing index) once every lane has
+// read its originals.  Returns this lane's share of the raw L1.
+template <int I>
+__device__ __forceinline__ float l1_sort_pixel(float* col_d, float* col_w, int64_t base, int n, int lane) {
+  constexpr int NN = 32 * I;
+  // key = depth bits (positive depths order like their bit patterns) : sample index;
+  // padding sorts last
+  unsigned long long key[I];
+#pragma unroll
+  for (int j = 0; j < I; ++j) {
+    const int e = lane * I + j;
+    key[j] = e < n ? ((unsigned long long)__float_as_uint(col_d[base + e]) << 32) | (unsigned)e : ~0ull;
+  }
+#pragma unroll
+  for (int size = 2; size <= NN; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride < I) {
+#pragma unroll
+        for (int j = 0; j < I; ++j) {
+          if ((j & stride) == 0) {
+            const bool up = ((lane * I + j) & size) == 0;
+            const unsigned long long a = key[j], b = key[j + stride];
+            const bool sw = up ? (b < a) : (a < b);
+            key[j] = sw ? b : a;
+            key[j + stride] = sw ? a : b;
+          }
+        }
+      } else {
+        const int lm = stride / I;
+#pragma unroll
+        for (int j = 0; j < I; ++j) {
+          const int e = lane * I + j;
+          const unsigned long long o = __shfl_xor_sync(FULL, key[j], lm);
+          const bool up = (e & size) == 0;
+          const bool lower = (e & stride) == 0;
+          const bool take_min = lower == up;
+          const bool mine_less = key[j] < o;
+          key[j] = (take_min == mine_less) ? key[j] : o;
+        }
+      }
+    }
+  }
+  float w[I];
+  float lw = 0.f, lwd = 0.f;
+#pragma unroll
+  for (int j = 0; j < I; ++j) {
+    const unsigned k = (unsigned)key[j];
+    const bool live = key[j] != ~0ull;
+    w[j] = live ? col_w[base + k] : 0.f;
+    lw += w[j];
+    lwd += w[j] * (live ? __uint_as_float((unsigned)(key[j] >> 32)) : 0.f);
+  }
+  // totals and exclusive lane offsets of w and w*d in depth order
+  float iw = lw, iwd = lwd;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float a1 = __shfl_up_sync(FULL, iw, o), a2 = __shfl_up_sync(FULL, iwd, o);
+    if (lane >= o) { iw += a1; iwd += a2; }
+  }
+  const float Wt = __shfl_sync(FULL, iw, 31), Dt = __shfl_sync(FULL, iwd, 31);
+  float pw = iw - lw, pwd = iwd - lwd;
+  float raw = 0.f;
+  __syncwarp();  // every lane has read its originals
+#pragma unroll
+  for (int j = 0; j < I; ++j) {
+    if (key[j] != ~0ull) {
+      const unsigned k = (unsigned)key[j];
+      const float d = __uint_as_float((unsigned)(key[j] >> 32));
+      raw += 2.f * w[j] * (d * pw - pwd);
+      col_d[base + k] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
+      col_w[base + k] = 2.f * w[j] * (2.f * pw + w[j] - Wt);
+      pw += w[j];
+      pwd += w[j] * d;
+    }
+  }
+  return raw;
+}
+
+// CLASS 0 resolves pixels with at most 256 samples (register sorts), CLASS 1 those
+// with 257..512 (16 per lane), CLASS 2 longer runs (shared-memory radix sort); each
+// launch skips the pixels of the other classes, so the register budget of the rare
+// long runs does not limit the occupancy of the common case.
+template <int CLASS>
 __global__ void __launch_bounds__(128) l1_resolve_kernel(
     sf_camera cam, float* state, float* l1s, int64_t slots, const int64_t* off, int cap, int smem_k,
     float* out_l1) {
@@ -248,24 +336,34 @@ __global__ void __launch_bounds__(128) l1_resolve_kernel(
     // never read past the pixel's run (a capacity overflow is rerun by the caller)
     const int room = off ? (int)(off[pix + 1] - off[pix]) : cap;
     if (n > room) n = room;
-    float Wt = 0.f, Dt = 0.f;
-    for (int k = lane; k < n; k += 32) {
-      const float d = col_d[base + k], w = col_w[base + k];
-      Wt += w; Dt += w * d;
-    }
-    Wt = warp_sum(Wt); Dt = warp_sum(Dt);
+    const int cls = n <= 256 ? 0 : (n <= 512 ? 1 : 2);
+    if (cls != CLASS) continue;
     float raw = 0.f;
-    if (n > smem_k) n = smem_k;  // the launcher sizes smem_k >= the largest count
-    {
-      for (int k = lane; k < n; k += 32) {
-        k0[k] = __float_as_uint(col_d[base + k]);
-        v0[k] = (uint32_t)k;
-        ws[k] = col_w[base + k];
+    if (CLASS == 0) {
+      if (n <= 1) {
+        if (n == 1 && lane == 0) { col_d[base] = 0.f; col_w[base] = 0.f; }
+      } else if (n <= 128) {
+        raw = l1_sort_pixel<4>(col_d, col_w, base, n, lane);
+      } else {
+        raw = l1_sort_pixel<8>(col_d, col_w, base, n, lane);
       }
+    } else if (CLASS == 1) {
+      raw = l1_sort_pixel<16>(col_d, col_w, base, n, lane);
+    } else {
+      // long runs: stable warp radix sort staged in shared memory
+      float Wt = 0.f, Dt = 0.f;
+      if (n > smem_k) n = smem_k;  // the launcher sizes smem_k >= the largest count
+      for (int k = lane; k < n; k += 32) {
+        const float d = col_d[base + k], w = col_w[base + k];
+        k0[k] = __float_as_uint(d);
+        v0[k] = (uint32_t)k;
+        ws[k] = w;
+        Wt += w; Dt += w * d;
+      }
+      Wt = warp_sum(Wt); Dt = warp_sum(Dt);
       __syncwarp();
       uint32_t *ks, *vs;
       warp_radix_sort_u32(k0, v0, k1, v1, hist, n, lane, &ks, &vs);
-      // the buffers not holding the sorted result receive the factors, by sample index
       float* aw = reinterpret_cast<float*>(ks == k0 ? k1 : k0);
       float* ad = reinterpret_cast<float*>(vs == v0 ? v1 : v0);
       float carry_w = 0.f, carry_wd = 0.f;
@@ -537,18 +635,29 @@ cudaError_t launch_l1_resolve(const sf_camera& cam, const sf_settings& st, float
   (void)st;
   const int64_t npix = (int64_t)cam.width * cam.height;
   if (npix == 0) return cudaSuccess;
-  const int smem_k = ((max(max_samples, 1) + 31) / 32) * 32;
+  int64_t blocks = (npix + 3) / 4;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  count_launches(1);
+  l1_resolve_kernel<0><<<(unsigned)blocks, 128, 0, s>>>(cam, state, l1s, slots, off, cap, 0, out_l1);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || max_samples <= 256) return e;
+  count_launches(1);
+  l1_resolve_kernel<1><<<(unsigned)(blocks < 148 * 8 ? blocks : 148 * 8), 128, 0, s>>>(cam, state, l1s, slots, off,
+                                                                                     cap, 0, out_l1);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || max_samples <= 512) return e;
+  const int smem_k = ((max_samples + 31) / 32) * 32;
   const size_t per_warp = l1_resolve_smem_per_warp(smem_k);
   const size_t budget = 200 * 1024;
   if (per_warp > budget) return cudaErrorInvalidValue;
-  int warps = (int)min((size_t)4, budget / per_warp);
+  const int warps = (int)min((size_t)4, budget / per_warp);
   const size_t smem = per_warp * warps;
-  cudaError_t e = cudaFuncSetAttribute(l1_resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = cudaFuncSetAttribute(l1_resolve_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  int64_t blocks = (npix + warps - 1) / warps;
-  if (blocks > 148 * 32) blocks = 148 * 32;
+  int64_t b2 = (npix + warps - 1) / warps;
+  if (b2 > 148 * 8) b2 = 148 * 8;
   count_launches(1);
-  l1_resolve_kernel<<<(unsigned)blocks, warps * 32, smem, s>>>(cam, state, l1s, slots, off, cap, smem_k, out_l1);
+  l1_resolve_kernel<2><<<(unsigned)b2, warps * 32, smem, s>>>(cam, state, l1s, slots, off, cap, smem_k, out_l1);
   return cudaGetLastError();
 }
 
