@@ -7,7 +7,7 @@ Restates the Torch provider's differentiable renderer:
 * SH colours and pixel rays (batched_renderer.py:69-83),
 * mode extras (batched_renderer.py:90-115),
 * exact tile lists (src/splatforge/studio/tile_binning.py:10-34),
-* per-tile evaluation, compositing and epilogue (batched_renderer.py:169-338),
+* batched, padded per-tile evaluation, compositing and epilogue (batched_renderer.py:127-150, 169-370),
 * ``absgrad`` hooks on the projected means (batched_renderer.py:246-280).
 
 Gradients come from autograd through this composition, as in the reference.
@@ -158,7 +158,7 @@ def mahalanobis2(delta, conic):
     return dx * (qa * dx + qb * dy) + dy * (qb * dx + qc * dy)
 
 
-def render(
+def prepare(
     view,
     camera,
     *,
@@ -168,7 +168,9 @@ def render(
     distortions="both",
     trunc_sigma=2.0,
 ):
-    """Returns a dict of HWC images plus ``projected_means`` / ``projected_radii``."""
+    """Everything ``render`` computes before its tile loop (batched_renderer.py:
+    169-224): projection, conics, colours, mode extras and the exact tile lists.
+    Returns a dict that ``tile_batches`` / ``render_batch`` consume."""
     s = settings or RenderSettings()
     if mode not in ("radegs", "gof", "ambisur"):
         raise ValueError(f"unsupported rendering mode: {mode}")
@@ -218,105 +220,171 @@ def render(
     )
     focal = torch.stack((camera.K[0, 0], camera.K[1, 1]))
     bg = m.new_tensor(s.background)
+    return dict(
+        camera=camera, Kinv=Kinv, settings=s, mode=mode, extent=extent, distortions=distortions,
+        offsets=offsets, ids_all=ids_all, xy=xy, radii=radii, conic=conic, colors=colors,
+        ray_colors=ray_colors, opacity=opacity, m=m, normals=normals, gain=gain, qinv=qinv,
+        plane=plane, sel=sel, focal=focal, bg=bg,
+    )
+
+
+def tile_batches(ctx, tile_batch_size=64, tile_event_budget=1_048_576):
+    """Tile batches as the Torch provider forms them (batched_renderer.py:127-150,
+    337-370): tiles grouped, in raster order of first appearance, by (height, width,
+    bit length of len-1); each group cut into consecutive batches of at most
+    min(tile_batch_size, tile_event_budget // (longest * height * width)) tiles, every
+    list padded to the group's longest.  Returns [(tile indices, longest), ...]."""
+    camera, ts = ctx["camera"], ctx["settings"].tile_size
     cols = (camera.width + ts - 1) // ts
-    rows_out = []
-    tile_index = 0
-    for top in range(0, camera.height, ts):
-        row = []
-        for left in range(0, camera.width, ts):
-            h, w = min(ts, camera.height - top), min(ts, camera.width - left)
-            ids = torch.as_tensor(
-                ids_all[offsets[tile_index] : offsets[tile_index + 1]], device=m.device
-            )
-            tile_index += 1
-            trays, pix = pixel_grid(camera, Kinv, top, left, h, w)
-            out = _tile(
-                ids, trays, pix, camera, xy, conic, colors, ray_colors, opacity, m, normals,
-                gain, qinv, plane, sel, focal, bg, mode, extent, s, distortions,
-            )
-            row.append(out.reshape(h, w, -1))
-        rows_out.append(torch.cat(row, 1))
-    image = torch.cat(rows_out, 0)
+    rows = (camera.height + ts - 1) // ts
+    lens = np.diff(ctx["offsets"])
+    groups = {}
+    for t in range(rows * cols):
+        h = min(ts, camera.height - (t // cols) * ts)
+        w = min(ts, camera.width - (t % cols) * ts)
+        groups.setdefault((h, w, max(1, int(lens[t] - 1).bit_length())), []).append(t)
+    batches = []
+    for (h, w, _), members in groups.items():
+        longest = max(1, int(max(lens[t] for t in members)))
+        size = max(1, min(tile_batch_size, tile_event_budget // (longest * h * w)))
+        for i in range(0, len(members), size):
+            batches.append((members[i : i + size], longest))
+    return batches
+
+
+def render_batch(ctx, tiles, longest):
+    """[B, h*w, 13] channel blocks of a batch of equally sized tiles."""
+    camera, s = ctx["camera"], ctx["settings"]
+    ts = s.tile_size
+    cols = (camera.width + ts - 1) // ts
+    offsets, ids_all = ctx["offsets"], ctx["ids_all"]
+    idx = np.zeros((len(tiles), longest), np.int64)
+    gate = np.zeros((len(tiles), longest), bool)
+    trays, pix = [], []
+    for row, t in enumerate(tiles):
+        lo, hi = offsets[t], offsets[t + 1]
+        idx[row, : hi - lo], gate[row, : hi - lo] = ids_all[lo:hi], True
+        top, left = (t // cols) * ts, (t % cols) * ts
+        h, w = min(ts, camera.height - top), min(ts, camera.width - left)
+        r, p = pixel_grid(camera, ctx["Kinv"], top, left, h, w)
+        trays.append(r)
+        pix.append(p)
+    dev = ctx["m"].device
+    c = ctx
+    return _tile_batch(
+        torch.as_tensor(idx, device=dev), torch.as_tensor(gate, device=dev), torch.stack(trays),
+        torch.stack(pix), camera, c["xy"], c["conic"], c["colors"], c["ray_colors"], c["opacity"],
+        c["m"], c["normals"], c["gain"], c["qinv"], c["plane"], c["sel"], c["focal"], c["bg"],
+        c["mode"], c["extent"], s, c["distortions"],
+    )
+
+
+def render(
+    view,
+    camera,
+    *,
+    mode,
+    settings=None,
+    selected=None,
+    distortions="both",
+    trunc_sigma=2.0,
+):
+    """Returns a dict of HWC images plus ``projected_means`` / ``projected_radii``."""
+    ctx = prepare(view, camera, mode=mode, settings=settings, selected=selected,
+                  distortions=distortions, trunc_sigma=trunc_sigma)
+    ts = ctx["settings"].tile_size
+    cols = (camera.width + ts - 1) // ts
+    rows = (camera.height + ts - 1) // ts
+    blocks = [None] * (rows * cols)
+    for tiles, longest in tile_batches(ctx):
+        out = render_batch(ctx, tiles, longest)
+        for row, t in enumerate(tiles):
+            h = min(ts, camera.height - (t // cols) * ts)
+            w = min(ts, camera.width - (t % cols) * ts)
+            blocks[t] = out[row].reshape(h, w, -1)
+    image = torch.cat([torch.cat(blocks[r * cols : (r + 1) * cols], 1) for r in range(rows)], 0)
     parts = torch.split(image, [c for _, c in CHANNELS], dim=-1)
     result = {name: part for (name, _), part in zip(CHANNELS, parts)}
-    result["projected_means"] = xy
-    result["projected_radii"] = radii
+    result["projected_means"] = ctx["xy"]
+    result["projected_radii"] = ctx["radii"]
     result["distortion_profile"] = distortions
     return result
 
 
-def _tile(ids, trays, pix, camera, xy, conic, colors, ray_colors, opacity, m, normals,
-          gain, qinv, plane, sel, focal, bg, mode, extent, s, distortions):
-    """One tile: [L, P] evaluation, compositing and epilogue (batched_renderer.py:185-338)."""
-    delta = pix.unsqueeze(0) - xy[ids][:, None, :]
-    sq = mahalanobis2(delta, conic[ids][:, None])
-    P = trays.shape[0]
+def _tile_batch(ids, valid, trays, pix, camera, xy, conic, colors, ray_colors, opacity, m, normals,
+                gain, qinv, plane, sel, focal, bg, mode, extent, s, distortions):
+    """A batch of B tiles with padded lists ``ids`` [B, M] (``valid`` marks the real
+    entries): [B, M, P] evaluation, compositing and epilogue (batched_renderer.py:
+    169-338, the uncompiled path)."""
+    delta = pix[:, None] - xy[ids][:, :, None, :]
+    sq = mahalanobis2(delta, conic[ids][:, :, None])
+    P = trays.shape[1]
     if mode == "gof":
         pxy = (xy[ids] - camera.K[:2, 2]) * m[ids, 2:3] / focal
-        proxy = torch.cat((pxy, m[ids, 2:3]), -1)[:, None, :].expand(-1, P, -1)
+        proxy = torch.cat((pxy, m[ids, 2:3]), -1)[:, :, None, :].expand(-1, -1, P, -1)
         if proxy.requires_grad:
             zdet = m[ids, 2].detach()
 
-            def hook(g, idx=ids, zz=zdet, target=xy):
-                target.absgrad.index_add_(0, idx, (g[..., :2] * zz[:, None, None] / focal).abs().sum(1))
+            def hook(g, idx=ids, gt=valid, zz=zdet, target=xy):
+                value = (g[..., :2] * zz[:, :, None, None] / focal).abs().sum(2)
+                target.absgrad.index_add_(0, idx[gt], value[gt])
 
             proxy.register_hook(hook)
-        qd = torch.einsum("lij,pj->lpi", qinv[ids], trays)
-        den = (qd * trays[None]).sum(-1).clamp_min(1e-12)
+        qd = torch.einsum("bmij,bpj->bmpi", qinv[ids], trays)
+        den = (qd * trays[:, None]).sum(-1).clamp_min(1e-12)
         depth = (proxy * qd).sum(-1) / den
-        off = depth[..., None] * trays[None] - proxy
-        e = torch.einsum("lpi,lij,lpj->lp", off, qinv[ids], off)
+        off = depth[..., None] * trays[:, None] - proxy
+        e = torch.einsum("bmpi,bmij,bmpj->bmp", off, qinv[ids], off)
         resp = torch.exp(-0.5 * e.clamp_min(0))
         pn = ops._unit(-qd)
     else:
         if delta.requires_grad:
 
-            def hook(g, idx=ids, target=xy):
-                target.absgrad.index_add_(0, idx, g.abs().sum(1))
+            def hook(g, idx=ids, gt=valid, target=xy):
+                target.absgrad.index_add_(0, idx[gt], g.abs().sum(2)[gt])
 
             delta.register_hook(hook)
         resp = torch.exp(-0.5 * sq)
-        pn = normals[ids][:, None, :].expand(-1, P, -1)
+        pn = normals[ids][:, :, None, :].expand(-1, -1, P, -1)
         if mode == "radegs":
             depth = (
-                torch.linalg.vector_norm(m[ids], dim=-1)[:, None]
-                + (gain[ids][:, None, :] * delta).sum(-1)
-            ) / torch.linalg.vector_norm(trays, dim=-1)[None]
+                torch.linalg.vector_norm(m[ids], dim=-1)[:, :, None]
+                + (gain[ids][:, :, None, :] * delta).sum(-1)
+            ) / torch.linalg.vector_norm(trays, dim=-1)[:, None]
         else:
-            den = (pn * trays[None]).sum(-1)
+            den = (pn * trays[:, None]).sum(-1)
             ok = den.abs() > 1e-8
-            depth = plane[ids][:, None] / torch.where(ok, den, torch.ones_like(den))
+            depth = plane[ids][:, :, None] / torch.where(ok, den, torch.ones_like(den))
             resp = torch.where(ok, resp, 0)
-    resp = torch.where((sq <= extent**2) & (depth > s.near) & (depth < s.far), resp, 0)
+    keep = valid[:, :, None] & (sq <= extent**2) & (depth > s.near) & (depth < s.far)
+    resp = torch.where(keep, resp, 0)
     rgb, alpha, znum, nnum, l1, l2, median, wts = ops.alpha_composite_batch(
-        (opacity[ids][:, None] * resp)[None], colors[ids][None], depth[None], pn[None],
-        distortions=distortions,
+        opacity[ids][:, :, None] * resp, colors[ids], depth, pn, distortions=distortions,
     )
-    rgb, alpha, znum, nnum, l1, l2, median, wts = (t[0] for t in (rgb, alpha, znum, nnum, l1, l2, median, wts))
     expected = znum / alpha.clamp_min(1e-8)
     if mode == "ambisur":
-        dnum = (wts * plane[ids][:, None]).sum(0)
+        dnum = (wts * plane[ids][:, :, None]).sum(1)
         den = (nnum * trays).sum(-1)
         ok = den.abs() > 1e-8
         expected = torch.where(ok, dnum / torch.where(ok, den, torch.ones_like(den)), 0)
     expected = torch.where(alpha > 1e-8, expected, 0)
     var = (
-        ops.ray_color_variance(wts, ray_colors[ids], rgb)
+        ops.ray_color_variance_batch(wts, ray_colors[ids], rgb)
         if mode == "ambisur"
         else torch.zeros_like(alpha)
     )
-    amb = (wts * sel[ids][:, None].to(wts.dtype)).sum(0)
+    amb = (wts * sel[ids][:, :, None].to(wts.dtype)).sum(1)
     return torch.cat(
         (
-            rgb + (1 - alpha[:, None]) * bg,
-            alpha[:, None],
-            expected[:, None],
+            rgb + (1 - alpha[..., None]) * bg,
+            alpha[..., None],
+            expected[..., None],
             ops._unit(nnum),
-            l1[:, None],
-            l2[:, None],
-            median[:, None],
-            var[:, None],
-            amb[:, None],
+            l1[..., None],
+            l2[..., None],
+            median[..., None],
+            var[..., None],
+            amb[..., None],
         ),
         -1,
     )
