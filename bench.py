@@ -44,6 +44,7 @@ def parse():
     ap.add_argument("--mode", default="gof")
     ap.add_argument("--distortions", default="both")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
 
@@ -263,7 +264,7 @@ def run_b200(args):
             "clocks": clk, "e2e": e2e, "roofline": roof,
         }
         # the CPU baseline is timed once, at N=1 (other ranks would compete for the cores)
-        result["cpu_baseline"] = cpu_baseline(args) if world == 1 else None
+        result["cpu_baseline"] = cpu_baseline(args) if world == 1 and not args.no_cpu_baseline else None
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -315,4 +315,12 @@ int hc_raster_backward(const float* records, int64_t n, const int32_t* ids, cons
   return 0;
 }
 
+// box_may_pass over n Gaussians (5 floats each: qa qb qc X Y) and one box
+void hc_box_may_pass(const float* g, int64_t n, float x0, float x1, float y0, float y1, float ext2,
+                     uint8_t* out) {
+  for (int64_t i = 0; i < n; ++i)
+    out[i] = sf::box_may_pass(g[i * 5], g[i * 5 + 1], g[i * 5 + 2], g[i * 5 + 3], g[i * 5 + 4], x0, x1, y0, y1,
+                              ext2);
+}
+
 }  // extern "C"

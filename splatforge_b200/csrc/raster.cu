@@ -24,15 +24,26 @@ namespace {
 constexpr int REC4 = SF_RECORD_FLOATS / 4;  // float4 per record
 constexpr int ACC = 24;                      // accumulator floats per batch slot (20 + absgrad 2 + pad)
 
-// first slot of a pixel's contiguous L1 sample run (fixed capacity or CSR)
-__device__ __forceinline__ int64_t l1_base(int tile, int tid, int cap, const int64_t* off, int64_t pix) {
-  return off ? off[pix] : ((int64_t)tile * TILE_PIXELS + tid) * cap;
+// first slot of a pixel's contiguous L1 sample run (fixed capacity or CSR); ptid is
+// the row-major index of the pixel inside its tile
+__device__ __forceinline__ int64_t l1_base(int tile, int ptid, int cap, const int64_t* off, int64_t pix) {
+  return off ? off[pix] : ((int64_t)tile * TILE_PIXELS + ptid) * cap;
 }
 
-// Warp-level culling of a batch: bit j of mask[j / 32] is set when Gaussian j may reach
-// a pixel of this warp's 16x2 pixel block.  Conservative: the axis-aligned box of the
-// ellipse squared <= extent^2 (half-widths sqrt(extent^2 * inv(Q)_xx), ...) widened by
-// a margin, tested against the box spanned by the warp's own pixel coordinates.
+// Pixel of thread tid: each warp covers an 8x4 block of its 16x16 tile (warps 0,1 the
+// top two blocks side by side, ...), a more compact footprint than 16x2 rows, so fewer
+// Gaussians reach a warp's box without reaching one of its pixels.
+__device__ __forceinline__ void tile_pixel(int tid, int tx, int ty, int& u, int& v, int& ptid) {
+  const int w = tid >> 5, lane = tid & 31;
+  const int lx = (w & 1) * 8 + (lane & 7), ly = (w >> 1) * 4 + (lane >> 3);
+  u = tx * TILE + lx;
+  v = ty * TILE + ly;
+  ptid = ly * TILE + lx;  // row-major index of the pixel inside its tile
+}
+
+// Warp-level culling of a batch: bit j of mask[j / 32] is set when Gaussian j may pass
+// squared <= extent^2 at a pixel of this warp (box_may_pass over the box spanned by the
+// warp's pixel centres).
 __device__ __forceinline__ void warp_cull(const float4* s_rec, int n_in, int lane, float x0, float x1,
                                           float y0, float y1, float ext2, unsigned (&mask)[TILE_PIXELS / 32]) {
 #pragma unroll
@@ -41,17 +52,7 @@ __device__ __forceinline__ void warp_cull(const float4* s_rec, int n_in, int lan
     bool hit = false;
     if (j < n_in) {
       const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
-      const float qa = rec[R_QA], qb = rec[R_QB], qc = rec[R_QC];
-      const float det = qa * qc - qb * qb;
-      if (det > 0.f) {
-        const float hx = sqrtf(fmaxf(ext2 * qc / det, 0.f)) * 1.001f + 1e-2f;
-        const float hy = sqrtf(fmaxf(ext2 * qa / det, 0.f)) * 1.001f + 1e-2f;
-        const float X = rec[R_X], Y = rec[R_Y];
-        hit = (X + hx >= x0) && (X - hx <= x1) && (Y + hy >= y0) && (Y - hy <= y1);
-      } else {
-        hit = true;  // degenerate conic: never cull
-      }
-      if (!(hit == hit)) hit = true;
+      hit = box_may_pass(rec[R_QA], rec[R_QB], rec[R_QC], rec[R_X], rec[R_Y], x0, x1, y0, y1, ext2);
     }
     mask[g] = __ballot_sync(FULL, hit);
   }
@@ -76,7 +77,8 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
   const int tile = blockIdx.x;
   const int tid = threadIdx.x;
   const int tx = tile % a.tiles_x, ty = tile / a.tiles_x;
-  const int u = tx * TILE + (tid & 15), v = ty * TILE + (tid >> 4);
+  int u, v, ptid;
+  tile_pixel(tid, tx, ty, u, v, ptid);
   const int W = a.cam.width, H = a.cam.height;
   const bool inside = u < W && v < H;
   PixelRay pr;
@@ -95,7 +97,7 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
   int64_t l1_at = 0;
   int l1_room = 0;
   if ((DIST & SF_DIST_L1) && inside) {
-    l1_at = l1_base(tile, tid, a.l1_cap, a.l1_off, pix);
+    l1_at = l1_base(tile, ptid, a.l1_cap, a.l1_off, pix);
     l1_room = a.l1_off ? (int)(a.l1_off[pix + 1] - a.l1_off[pix]) : a.l1_cap;
   }
   if (tid == 0) s_max = 0;
@@ -413,7 +415,8 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
   const int tile = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31;
   const int tx = tile % a.tiles_x, ty = tile / a.tiles_x;
-  const int u = tx * TILE + (tid & 15), v = ty * TILE + (tid >> 4);
+  int u, v, ptid;
+  tile_pixel(tid, tx, ty, u, v, ptid);
   const int W = a.cam.width, H = a.cam.height;
   const bool inside = u < W && v < H;
   const int64_t pix = (int64_t)v * W + u;
@@ -449,7 +452,7 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
     last = f2i(st[PS_LAST]);
     k = f2i(st[PS_COUNT]) - 1;
     if (DIST & SF_DIST_L1) {
-      l1_at = l1_base(tile, tid, a.l1_cap, a.l1_off, pix);
+      l1_at = l1_base(tile, ptid, a.l1_cap, a.l1_off, pix);
       // never read past the pixel's run
       const int room = a.l1_off ? (int)(a.l1_off[pix + 1] - a.l1_off[pix]) : a.l1_cap;
       if (k >= room) k = room - 1;

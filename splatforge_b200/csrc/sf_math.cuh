@@ -514,6 +514,38 @@ SF_HD float mahalanobis2(float dx, float dy, float qa, float qb, float qc) {
   return radd(rmul(dx, radd(rmul(qa, dx), rmul(qb, dy))), rmul(dy, radd(rmul(qb, dx), rmul(qc, dy))));
 }
 
+// q(x, y) = qa x^2 + 2 qb x y + qc y^2 and the sum of the magnitudes of its terms
+SF_HD float quad_form(float qa, float qb, float qc, float x, float y, float& mag) {
+  const float t0 = qa * x * x, t1 = 2.f * qb * x * y, t2 = qc * y * y;
+  mag = fabsf(t0) + fabsf(t1) + fabsf(t2);
+  return t0 + t1 + t2;
+}
+
+// May a Gaussian centred at (X, Y) with conic (qa, qb; qb, qc) pass squared <= ext2 at
+// some pixel centre inside the box [x0, x1] x [y0, y1]?  Takes the minimum of the
+// quadratic form over the box: zero when the centre is inside, else the smallest of
+// the four edge minima (the 1D minimiser of a convex quadratic, clamped to the edge).
+// Conservative by a margin far above the float rounding of either evaluation; a
+// degenerate conic or a NaN always answers yes.
+SF_HD bool box_may_pass(float qa, float qb, float qc, float X, float Y, float x0, float x1, float y0, float y1,
+                        float ext2) {
+  const float ax = x0 - X, bx = x1 - X, ay = y0 - Y, by = y1 - Y;
+  if (!(qa > 0.f && qc > 0.f && qa * qc - qb * qb > 0.f)) return true;
+  if (ax <= 0.f && bx >= 0.f && ay <= 0.f && by >= 0.f) return true;
+  const float sy = -qb / qc, sx = -qb / qa;
+  float mag, val;
+  bool hit = false;
+  val = quad_form(qa, qb, qc, ax, fminf(fmaxf(sy * ax, ay), by), mag);
+  hit |= !(val > ext2 + 1e-5f * mag + 1e-6f);
+  val = quad_form(qa, qb, qc, bx, fminf(fmaxf(sy * bx, ay), by), mag);
+  hit |= !(val > ext2 + 1e-5f * mag + 1e-6f);
+  val = quad_form(qa, qb, qc, fminf(fmaxf(sx * ay, ax), bx), ay, mag);
+  hit |= !(val > ext2 + 1e-5f * mag + 1e-6f);
+  val = quad_form(qa, qb, qc, fminf(fmaxf(sx * by, ax), bx), by, mag);
+  hit |= !(val > ext2 + 1e-5f * mag + 1e-6f);
+  return hit;
+}
+
 // One (pixel, Gaussian) sample of the per-tile evaluation (batched_renderer.py:240-306)
 struct Sample {
   float dx, dy, sq;

@@ -31,8 +31,18 @@ def lib():
         h.hc_project_backward.argtypes = [P] * 5 + [ctypes.c_int64, ctypes.POINTER(Camera), ctypes.POINTER(Settings)] + [P] * 7
         h.hc_raster_forward.argtypes = [P, P, P, ctypes.POINTER(Camera), ctypes.POINTER(Settings)] + [P] * 11 + [ctypes.c_int64, ctypes.c_int32]
         h.hc_raster_backward.argtypes = [P, ctypes.c_int64, P, P, ctypes.POINTER(Camera), ctypes.POINTER(Settings), P, P, ctypes.c_int64, ctypes.c_int32] + [P] * 12
+        F = ctypes.c_float
+        h.hc_box_may_pass.argtypes = [P, ctypes.c_int64, F, F, F, F, F, P]
         _hc = h
     return _hc
+
+
+def box_may_pass(gauss, box, ext2):
+    """The kernels' warp-culling predicate for [n, 5] (qa, qb, qc, X, Y) float32 rows."""
+    g = torch.as_tensor(gauss, dtype=torch.float32).contiguous()
+    out = torch.zeros(g.shape[0], dtype=torch.uint8)
+    lib().hc_box_may_pass(_p(g), g.shape[0], *(ctypes.c_float(v) for v in box), ctypes.c_float(ext2), _p(out))
+    return out.bool().numpy()
 
 
 def _p(t):

@@ -99,3 +99,34 @@ def test_hostcheck_projection_bits_match_oracle():
     assert torch.equal(ex["records"][:, 2], conic[:, 0, 0])
     assert torch.equal(ex["records"][:, 3], conic[:, 0, 1])
     assert torch.equal(ex["records"][:, 4], conic[:, 1, 1])
+
+
+def test_warp_cull_never_drops_a_passing_sample():
+    """The culling predicate over an 8x4 block of pixel centres is conservative: every
+    Gaussian that passes squared <= extent^2 (float32, the kernels' operation order) at
+    one of the 32 centres is kept -- for round, elongated and near-degenerate conics."""
+    rng = np.random.default_rng(3)
+    n = 200_000
+    ang = rng.uniform(0, np.pi, n)
+    s1 = np.exp(rng.uniform(np.log(0.3), np.log(40.0), n))
+    s2 = s1 * np.exp(rng.uniform(np.log(1e-3), 0.0, n))
+    c, s = np.cos(ang), np.sin(ang)
+    a = c * c / s1**2 + s * s / s2**2
+    b = c * s * (1 / s1**2 - 1 / s2**2)
+    cc = s * s / s1**2 + c * c / s2**2
+    x0, y0 = 100.5, 60.5
+    X = x0 + rng.uniform(-60, 68, n)
+    Y = y0 + rng.uniform(-60, 64, n)
+    g = np.stack([a, b, cc, X, Y], 1).astype(np.float32)
+    ext2 = np.float32(9.0)
+    keep = hostcheck.box_may_pass(g, (x0, x0 + 7, y0, y0 + 3), 9.0)
+    px = (np.float32(x0) + np.arange(8, dtype=np.float32))[None, None, :]
+    py = (np.float32(y0) + np.arange(4, dtype=np.float32))[None, :, None]
+    qa, qb, qc, gx, gy = (g[:, k][:, None, None] for k in range(5))
+    dx, dy = px - gx, py - gy
+    sq = dx * (qa * dx + qb * dy) + dy * (qb * dx + qc * dy)
+    passes = (sq <= ext2).any((1, 2))
+    assert passes.sum() > 1000
+    assert not (passes & ~keep).any()
+    # and it does cull: most non-passing Gaussians whose bounding box reaches the block
+    assert (~keep).sum() > 0.5 * (~passes).sum()
