@@ -41,21 +41,18 @@ __device__ __forceinline__ void tile_pixel(int tid, int tx, int ty, int& u, int&
   ptid = ly * TILE + lx;  // row-major index of the pixel inside its tile
 }
 
-// Warp-level culling of a batch: bit j of mask[j / 32] is set when Gaussian j may pass
-// squared <= extent^2 at a pixel of this warp (box_may_pass over the box spanned by the
-// warp's pixel centres).
-__device__ __forceinline__ void warp_cull(const float4* s_rec, int n_in, int lane, float x0, float x1,
-                                          float y0, float y1, float ext2, unsigned (&mask)[TILE_PIXELS / 32]) {
-#pragma unroll
-  for (int g = 0; g < TILE_PIXELS / 32; ++g) {
-    const int j = g * 32 + lane;
-    bool hit = false;
-    if (j < n_in) {
-      const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
-      hit = box_may_pass(rec[R_QA], rec[R_QB], rec[R_QC], rec[R_X], rec[R_Y], x0, x1, y0, y1, ext2);
-    }
-    mask[g] = __ballot_sync(FULL, hit);
+// Warp-level culling of batch slots g*32 .. g*32+31: bit l is set when the Gaussian in
+// slot g*32+l may pass squared <= extent^2 at a pixel of this warp (box_may_pass over
+// the box spanned by the warp's pixel centres).
+__device__ __forceinline__ unsigned warp_cull(const float4* s_rec, int n_in, int g, int lane, float x0, float x1,
+                                              float y0, float y1, float ext2) {
+  const int j = g * 32 + lane;
+  bool hit = false;
+  if (j < n_in) {
+    const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
+    hit = box_may_pass(rec[R_QA], rec[R_QB], rec[R_QC], rec[R_X], rec[R_Y], x0, x1, y0, y1, ext2);
   }
+  return __ballot_sync(FULL, hit);
 }
 
 __device__ __forceinline__ float warp_minf(float v) {
@@ -112,11 +109,10 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
       s_rec[k] = __ldg(reinterpret_cast<const float4*>(a.records) + (int64_t)id * REC4 + comp);
     }
     __syncthreads();
-    unsigned mask[TILE_PIXELS / 32];
-    warp_cull(s_rec, n_in, tid & 31, wx0, wx1, wy0, wy1, ext2, mask);
-    for (int g = 0; g < TILE_PIXELS / 32; ++g) {
+    const int groups = (n_in + 31) >> 5;
+    for (int g = 0; g < groups; ++g) {
       if (__all_sync(FULL, done)) break;
-      unsigned m = mask[g];
+      unsigned m = warp_cull(s_rec, n_in, g, tid & 31, wx0, wx1, wy0, wy1, ext2);
       while (m) {
         const int j = g * 32 + __ffs(m) - 1;
         m &= m - 1;
@@ -240,32 +236,48 @@ __device__ __forceinline__ float l1_sort_pixel(float* col_d, float* col_w, int64
     const int e = lane * I + j;
     key[j] = e < n ? ((unsigned long long)__float_as_uint(col_d[base + e]) << 32) | (unsigned)e : ~0ull;
   }
+  // sizes up to I sort inside each lane (directions known at compile time) ...
 #pragma unroll
-  for (int size = 2; size <= NN; size <<= 1) {
+  for (int size = 2; size <= I; size <<= 1) {
 #pragma unroll
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      if (stride < I) {
 #pragma unroll
-        for (int j = 0; j < I; ++j) {
-          if ((j & stride) == 0) {
-            const bool up = ((lane * I + j) & size) == 0;
-            const unsigned long long a = key[j], b = key[j + stride];
-            const bool sw = up ? (b < a) : (a < b);
-            key[j] = sw ? b : a;
-            key[j + stride] = sw ? a : b;
-          }
+      for (int j = 0; j < I; ++j) {
+        if ((j & stride) == 0) {
+          const bool up = ((lane * I + j) & size) == 0;
+          const unsigned long long a = key[j], b = key[j + stride];
+          const bool sw = up ? (b < a) : (a < b);
+          key[j] = sw ? b : a;
+          key[j + stride] = sw ? a : b;
         }
-      } else {
-        const int lm = stride / I;
+      }
+    }
+  }
+  // ... then each larger merge: the cross-lane strides in a rolled loop (exchange with
+  // lane ^ (stride / I)), the last log2(I) strides inside the lane.  The rolled loops
+  // keep the code small enough for the instruction cache.
+#pragma unroll 1
+  for (int size = 2 * I; size <= NN; size <<= 1) {
+    const bool up = ((lane * I) & size) == 0;
+#pragma unroll 1
+    for (int lm = size / (2 * I); lm > 0; lm >>= 1) {
+      const bool take_min = ((lane & lm) == 0) == up;
 #pragma unroll
-        for (int j = 0; j < I; ++j) {
-          const int e = lane * I + j;
-          const unsigned long long o = __shfl_xor_sync(FULL, key[j], lm);
-          const bool up = (e & size) == 0;
-          const bool lower = (e & stride) == 0;
-          const bool take_min = lower == up;
-          const bool mine_less = key[j] < o;
-          key[j] = (take_min == mine_less) ? key[j] : o;
+      for (int j = 0; j < I; ++j) {
+        const unsigned long long o = __shfl_xor_sync(FULL, key[j], lm);
+        const bool mine_less = key[j] < o;
+        key[j] = (take_min == mine_less) ? key[j] : o;
+      }
+    }
+#pragma unroll
+    for (int stride = I >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int j = 0; j < I; ++j) {
+        if ((j & stride) == 0) {
+          const unsigned long long a = key[j], b = key[j + stride];
+          const bool sw = up ? (b < a) : (a < b);
+          key[j] = sw ? b : a;
+          key[j + stride] = sw ? a : b;
         }
       }
     }
@@ -345,12 +357,12 @@ __global__ void __launch_bounds__(128) l1_resolve_kernel(
       if (n <= 1) {
         if (n == 1 && lane == 0) { col_d[base] = 0.f; col_w[base] = 0.f; }
       } else if (n <= 128) {
-        raw = l1_sort_pixel<4>(col_d, col_w, base, n, lane);
+                  raw = l1_sort_pixel<4>(col_d, col_w, base, n, lane);
       } else {
-        raw = l1_sort_pixel<8>(col_d, col_w, base, n, lane);
+                  raw = l1_sort_pixel<8>(col_d, col_w, base, n, lane);
       }
     } else if (CLASS == 1) {
-      raw = l1_sort_pixel<16>(col_d, col_w, base, n, lane);
+              raw = l1_sort_pixel<16>(col_d, col_w, base, n, lane);
     } else {
       // long runs: stable warp radix sort staged in shared memory
       float Wt = 0.f, Dt = 0.f;
@@ -485,10 +497,8 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
     }
     for (int q = tid; q < n_in * ACC; q += TILE_PIXELS) s_acc[q] = 0.f;
     __syncthreads();
-    unsigned mask[TILE_PIXELS / 32];
-    warp_cull(s_rec, n_in, lane, wx0, wx1, wy0, wy1, ext2, mask);
-    for (int g = TILE_PIXELS / 32 - 1; g >= 0; --g) {
-     unsigned m = mask[g];
+    for (int g = ((n_in + 31) >> 5) - 1; g >= 0; --g) {
+     unsigned m = warp_cull(s_rec, n_in, g, lane, wx0, wx1, wy0, wy1, ext2);
      while (m) {
       const int jb = 31 - __clz(m);
       m &= ~(1u << jb);

@@ -277,3 +277,29 @@ def test_l1_long_sample_runs_match_the_oracle():
         want, wgrads, _ = run_oracle(params, cam, mode, "l1", sel, ups)
         assert_images(got, want, mode, f"long/{mode}")
         assert_grads(ggrads, wgrads, f"long/{mode}")
+
+
+def test_l1_exact_depth_ties_match_the_oracle():
+    """Every fifth Gaussian of a surface-scene crop appears twice: the twins give
+    bit-identical depths at every pixel, which the 32-bit key sort of the L1 resolve
+    cannot tell apart, so those pixels take the 64-bit (depth, index) path.  Images
+    must match; the twins' gradients are compared summed onto the original rows
+    (a tie's order decides how dL1/ddepth splits between the twins, not its sum)."""
+    torch.set_num_threads(8)
+    params, cams = scenes.workload("surfaces100k_800", seed=0)
+    n = params.means.shape[0]
+    twin = torch.arange(0, n, 5)
+    params = scenes.SceneParams(*(torch.cat((t, t[twin])) for t in params.tensors()), params.sh_degree)
+    cam = cams[0].crop(384, 384, 48, 32)
+    ups = _ups(cam, 31)
+    for mode in ("gof", "radegs"):
+        settings = RasterSettings(mode=mode, distortions="both")
+        got, ggrads, _ = run_gpu(params, cam, settings, None, ups)
+        want, wgrads, _ = run_oracle(params, cam, mode, "both", None, ups)
+        assert_images(got, want, mode, f"ties/{mode}")
+        for name in PARAM_NAMES + ("means2d_grad",):
+            a, b = ggrads[name].clone(), wgrads[name].clone()
+            a[twin] += a[n:]
+            b[twin] += b[n:]
+            e = rel_err(a[:n], b[:n])
+            assert e < GRAD_RTOL, (mode, name, e)
