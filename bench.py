@@ -111,6 +111,11 @@ class ClockSampler:
         return {"sm_mhz": med, "sm_max_mhz": maxmhz, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant
+# kernel, from a single-pass ncu capture of this exact workload.
+MEASURED_TRAFFIC = {("surfaces1m_1080p", "gof", "both", "raster_backward"): 3087120384 + 57543936}
+
+
 def algorithmic_flops(mode, n_pairs_fwd):
     """Per-pair algorithmic FP32 flops of the raster forward (SURVEY/DESIGN table)."""
     per = {"radegs": 35, "gof": 70, "ambisur": 40}[mode]
@@ -245,7 +250,8 @@ def run_b200(args):
             achieved = flops / (dom_ms * 1e-3) / 1e12
             roof = {"bound": "fp32", "kernel": dom, "achieved": round(achieved, 3),
                     "peak": round(fp32_peak, 2), "unit": "TFLOP/s", "frac": round(achieved / fp32_peak, 4),
-                    "traffic": None, "kernel_ms": round(dom_ms, 4),
+                    "traffic": MEASURED_TRAFFIC.get((args.workload, args.mode, args.distortions, dom)),
+                    "traffic_unit": "bytes per launch", "kernel_ms": round(dom_ms, 4),
                     "peak_source": f"FP32 SIMT 148 SM x 128 lanes x 2 at the sampled {sm_mhz:.0f} MHz",
                     "hbm_peak_gbs": peaks.get("hbm_gbs")}
         result = {

@@ -151,16 +151,26 @@ __global__ void __launch_bounds__(RS_THREADS) radix_upsweep_kernel(const uint32_
   hist[(int64_t)d * nb + blockIdx.x] = sum;
 }
 
+// Scatter pass: ranks within each warp from __match_any_sync (stable: keys of one digit
+// keep their input order), then the block's keys are regrouped by digit in shared
+// memory and written out from there, so consecutive threads store consecutive
+// addresses of one digit's run instead of 32 scattered runs per instruction.
 __global__ void __launch_bounds__(RS_THREADS, 2) radix_downsweep_kernel(
     const uint32_t* keys_in, const int32_t* vals_in, int64_t n, int shift, int nb,
     const uint32_t* offsets, uint32_t* keys_out, int32_t* vals_out) {
   __shared__ uint32_t s_cnt[RS_WARPS][RADIX];
-  __shared__ uint32_t s_off[RADIX];
+  __shared__ uint32_t s_off[RADIX];    // this block's first output slot per digit
+  __shared__ uint32_t s_local[RADIX];  // first slot of each digit inside the block
+  __shared__ uint32_t s_wsum[RS_WARPS];
+  __shared__ uint32_t s_keys[RS_CHUNK];
+  __shared__ int32_t s_vals[RS_CHUNK];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   for (int k = threadIdx.x; k < RS_WARPS * RADIX; k += RS_THREADS) (&s_cnt[0][0])[k] = 0;
   s_off[threadIdx.x] = offsets[(int64_t)threadIdx.x * nb + blockIdx.x];
   __syncthreads();
-  const int64_t base = (int64_t)blockIdx.x * RS_CHUNK + (int64_t)wid * (RS_CHUNK / RS_WARPS);
+  const int64_t block0 = (int64_t)blockIdx.x * RS_CHUNK;
+  const int64_t base = block0 + (int64_t)wid * (RS_CHUNK / RS_WARPS);
+  const int rows = (int)min((int64_t)RS_CHUNK, n - block0);
   const unsigned lt = (1u << lane) - 1u;
   uint32_t key[RS_ROUNDS];
   int32_t val[RS_ROUNDS];
@@ -181,6 +191,7 @@ __global__ void __launch_bounds__(RS_THREADS, 2) radix_downsweep_kernel(
   }
   __syncthreads();
   {
+    // per digit: exclusive prefix over warps, and the digit's total in this block
     const int d = threadIdx.x;
     uint32_t run = 0;
 #pragma unroll
@@ -189,6 +200,18 @@ __global__ void __launch_bounds__(RS_THREADS, 2) radix_downsweep_kernel(
       s_cnt[w][d] = run;
       run += c;
     }
+    // exclusive scan of the 256 digit totals across the block
+    uint32_t incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(FULL, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_wsum[wid] = incl;
+    __syncthreads();
+    uint32_t before = 0;
+    for (int w = 0; w < wid; ++w) before += s_wsum[w];
+    s_local[d] = before + incl - run;
   }
   __syncthreads();
 #pragma unroll
@@ -196,10 +219,18 @@ __global__ void __launch_bounds__(RS_THREADS, 2) radix_downsweep_kernel(
     const int64_t idx = base + r * 32 + lane;
     if (idx < n) {
       const uint32_t d = (key[r] >> shift) & 0xff;
-      const uint32_t pos = s_off[d] + s_cnt[wid][d] + rank[r];
-      keys_out[pos] = key[r];
-      vals_out[pos] = val[r];
+      const uint32_t lpos = s_local[d] + s_cnt[wid][d] + rank[r];
+      s_keys[lpos] = key[r];
+      s_vals[lpos] = val[r];
     }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < rows; i += RS_THREADS) {
+    const uint32_t k = s_keys[i];
+    const uint32_t d = (k >> shift) & 0xff;
+    const uint32_t pos = s_off[d] + (uint32_t)i - s_local[d];
+    keys_out[pos] = k;
+    vals_out[pos] = s_vals[i];
   }
 }
 
