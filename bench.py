@@ -8,6 +8,10 @@ of the replicated scene per step; with N > 1 ranks the per-Gaussian gradients
 (59 floats per Gaussian) are all-reduced with NCCL every step (view-sharded data
 parallelism).  ``value`` = all ranks' rendered pixels / max-over-ranks step time.
 
+``--workload surfaces3m_views64`` runs the view-batched training step instead: 3M
+Gaussians, 8 views of 1600x1064 per GPU per step (8/16/32/64 views at 1/2/4/8 GPUs),
+gradients accumulated over the views, then one all-reduce of the [N,59] buffer.
+
     python bench.py [--gpus N --steps K --warmup W]          # B200 arm
     python bench.py --impl reference [...]                     # CPU arm (oracle port)
 """
@@ -32,6 +36,8 @@ sys.path.insert(0, str(ROOT))
 CHANNELS = ("rgb", "alpha", "depth", "normals", "distortion_l1", "distortion_l2",
             "median_depth", "ray_color", "ambiguity_mask")
 METRIC = "fwd+bwd rendered Mpix/s at 1M Gaussians 1080p; views/s at 1/2/4/8 GPUs"
+# workloads rendered as a batch of views per GPU per step (the rest: one view)
+VIEW_BATCHED = {"surfaces3m_views64": 8}
 
 
 def parse():
@@ -132,11 +138,18 @@ def run_b200(args):
     rank, world, local = distributed.init_from_env(backend="nccl", timeout_s=300)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    params, _ = scenes.workload(args.workload, seed=0)
-    base_cam = scenes.workload(args.workload, seed=0)[1][0]
-    cams = scenes.orbit_cameras(max(8, world), base_cam.width, base_cam.height, 60.0 if "1080" in args.workload else 50.0,
-                                radius=3.0, seed=0)
-    cam = cams[0] if world == 1 else cams[rank]
+    params, wl_cams = scenes.workload(args.workload, seed=0)
+    if args.workload in VIEW_BATCHED:
+        # view-batched training step: VIEW_BATCHED views per GPU per step, drawn in
+        # order from the workload's 64 poses (8/16/32/64 views at 1/2/4/8 GPUs)
+        per = VIEW_BATCHED[args.workload]
+        my_cams = [wl_cams[(rank * per + v) % len(wl_cams)] for v in range(per)]
+    else:
+        base_cam = wl_cams[0]
+        cams = scenes.orbit_cameras(max(8, world), base_cam.width, base_cam.height,
+                                    60.0 if "1080" in args.workload else 50.0, radius=3.0, seed=0)
+        my_cams = [cams[0] if world == 1 else cams[rank]]
+    cam = my_cams[0]
     settings = RasterSettings(mode=args.mode, distortions=args.distortions)
     g = torch.Generator().manual_seed(1234 + rank)
     H, W = cam.height, cam.width
@@ -150,10 +163,11 @@ def run_b200(args):
     def step(timing=False):
         for t in p.tensors():
             t.grad = None
-        view = scenes.activated(p)
-        out = rasterizer.rasterize(view.means, view.quats, view.scales, view.opacities, view.sh, 3, cam, settings)
-        loss = sum((out[ch] * ups[ch]).sum() for ch in CHANNELS)
-        loss.backward()
+        for c in my_cams:
+            view = scenes.activated(p)
+            out = rasterizer.rasterize(view.means, view.quats, view.scales, view.opacities, view.sh, 3, c, settings)
+            loss = sum((out[ch] * ups[ch]).sum() for ch in CHANNELS)
+            loss.backward()
         reducer()
         return out
 
@@ -187,7 +201,7 @@ def run_b200(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    pixels = H * W * world
+    pixels = H * W * len(my_cams) * world
     value = pixels / (ms * 1e-3) / 1e6
 
     # end to end through the public renderer API: pinned host parameters in, loss out
@@ -207,12 +221,15 @@ def run_b200(args):
                 d.requires_grad_(True)
                 d.grad = None
             sp = scenes.SceneParams(*dev_params, sh_degree=3)
-            v = scenes.activated(sp)
-            o = renderer.render(v, cam, distortions=args.distortions)
-            loss = sum((getattr(o, ch) * ups[ch]).sum() for ch in CHANNELS)
-            loss.backward()
+            total = 0.0
+            for c in my_cams:
+                v = scenes.activated(sp)
+                o = renderer.render(v, c, distortions=args.distortions)
+                loss = sum((getattr(o, ch) * ups[ch]).sum() for ch in CHANNELS)
+                loss.backward()
+                total = total + loss.detach()
             e2e_reducer()
-            loss_host.copy_(loss.detach(), non_blocking=True)
+            loss_host.copy_(total, non_blocking=True)
             for d in dev_params:
                 d.requires_grad_(False)
 
@@ -260,9 +277,9 @@ def run_b200(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded surface-sampled scene, random camera poses)",
             "config": {"workload": f"{args.workload}: {n} Gaussians, {W}x{H}, mode {args.mode}, "
-                                   f"distortions {args.distortions}, fwd+bwd, 1 view per GPU per step",
+                                   f"distortions {args.distortions}, fwd+bwd, {len(my_cams)} view(s) per GPU per step",
                        "parallelism": f"view-sharded dp{world}, NCCL all-reduce of [N,59] grads" if world > 1 else "single GPU",
-                       "views_per_s": round(world / (ms * 1e-3), 3), "n_isect": int(n_isect),
+                       "views_per_s": round(world * len(my_cams) / (ms * 1e-3), 3), "n_isect": int(n_isect),
                        "l2_policy": "inputs larger than L2 (236 MB parameters + records per step)",
                        "fwd_ms": fwd, "bwd_ms": bwd, "pairs_evaluated": counters[0],
                        "pairs_contributing": counters[1], "pairs_in_tile_lists": int(n_isect) * 256},

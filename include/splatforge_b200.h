@@ -234,8 +234,9 @@ int sf_b200_raster_forward(const float* records, int64_t n, const int32_t* isect
                            int32_t* l1_needed, int64_t* counters, void* stream);
 
 /* Per-pixel sample counts (pixel_state column) -> CSR offsets[H*W+1] (int64) for the
- * rerun of an L1 forward whose capacity was exceeded.  workspace as for binning with
- * n = H*W. */
+ * rerun of an L1 forward whose capacity was exceeded.  Each pixel's run is its count
+ * rounded up to a multiple of 8 samples, so runs start 32-byte aligned.  workspace as
+ * for binning with n = H*W. */
 int sf_b200_l1_offsets(const sf_camera* camera, const float* pixel_state, int64_t* offsets,
                        void* workspace, size_t workspace_bytes, void* stream);
 

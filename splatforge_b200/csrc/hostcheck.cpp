@@ -266,12 +266,12 @@ int hc_raster_backward(const float* records, int64_t n, const int32_t* ids, cons
         }
         if (!contrib || !(s.alpha > 0.f)) continue;
         const float al = s.alpha, om = 1.f - al;
-        const float Ti = T / om, w = al * Ti;
+        const float Ti = T * (1.f / om), w = al * Ti;
         float adj;
         if (mode == SF_MODE_GOF) adj = sample_adj<SF_MODE_GOF>(rec, s, pg, auxw);
         else if (mode == SF_MODE_RADEGS) adj = sample_adj<SF_MODE_RADEGS>(rec, s, pg, auxw);
         else adj = sample_adj<SF_MODE_AMBISUR>(rec, s, pg, auxw);
-        const float g_alpha_s = Ti * adj - S / om;
+        const float g_alpha_s = Ti * adj - S * (1.f / om);
         S += w * adj;
         T = Ti;
         float g_d = w * pg.gD + (pos == pg.med_pos ? pg.gMed : 0.f) + pg.gL1 * auxd;
@@ -281,15 +281,15 @@ int hc_raster_backward(const float* records, int64_t n, const int32_t* ids, cons
         float* g = grad_records + (int64_t)ids[pos] * SF_RECORD_FLOATS;
         float* ab = absgrad + (int64_t)ids[pos] * 2;
         if (mode == SF_MODE_GOF) {
-          sample_backward<SF_MODE_GOF>(rec, pr, s, pg, w, g_alpha_s, g_d, fx, fy, vals);
+          sample_backward<SF_MODE_GOF>(rec, pr, s, pg, w, g_alpha_s, g_d, 1.f / fx, 1.f / fy, vals);
           nv = SampleLayout<SF_MODE_GOF>::NV;
           for (int q = 0; q < nv; ++q) { int sl = SampleLayout<SF_MODE_GOF>::slot(q); if (sl < 20) g[sl] += vals[q]; else ab[sl - 20] += vals[q]; }
         } else if (mode == SF_MODE_RADEGS) {
-          sample_backward<SF_MODE_RADEGS>(rec, pr, s, pg, w, g_alpha_s, g_d, fx, fy, vals);
+          sample_backward<SF_MODE_RADEGS>(rec, pr, s, pg, w, g_alpha_s, g_d, 1.f / fx, 1.f / fy, vals);
           nv = SampleLayout<SF_MODE_RADEGS>::NV;
           for (int q = 0; q < nv; ++q) { int sl = SampleLayout<SF_MODE_RADEGS>::slot(q); if (sl < 20) g[sl] += vals[q]; else ab[sl - 20] += vals[q]; }
         } else {
-          sample_backward<SF_MODE_AMBISUR>(rec, pr, s, pg, w, g_alpha_s, g_d, fx, fy, vals);
+          sample_backward<SF_MODE_AMBISUR>(rec, pr, s, pg, w, g_alpha_s, g_d, 1.f / fx, 1.f / fy, vals);
           nv = SampleLayout<SF_MODE_AMBISUR>::NV;
           for (int q = 0; q < nv; ++q) { int sl = SampleLayout<SF_MODE_AMBISUR>::slot(q); if (sl < 20) g[sl] += vals[q]; else ab[sl - 20] += vals[q]; }
         }

@@ -67,9 +67,36 @@ __device__ __forceinline__ float warp_maxf(float v) {
 }
 
 // ------------------------------------------------------------------ forward
+// L1 samples are staged per pixel in an 8-deep shared-memory ring and written out 8 at
+// a time as two 16-byte stores per column: a full 32-byte sector of depths and one of
+// weights, instead of sixteen 4-byte stores that each touch their own sector.  Runs
+// start on 8-float boundaries (fixed capacities are multiples of 32; CSR runs are
+// rounded up to multiples of 8); an unaligned caller layout takes scalar stores.
+constexpr int L1_RING = 8;
+
+__device__ __forceinline__ void l1_flush(float* l1s, int64_t slots, int64_t at, int first, int count, int room,
+                                         bool vec_ok, const float (*ring)[L1_RING][TILE_PIXELS], int tid) {
+  if (vec_ok && count == L1_RING && first + L1_RING <= room) {
+    float4* d = reinterpret_cast<float4*>(l1s + at + first);
+    float4* w = reinterpret_cast<float4*>(l1s + slots + at + first);
+    d[0] = make_float4(ring[0][0][tid], ring[0][1][tid], ring[0][2][tid], ring[0][3][tid]);
+    d[1] = make_float4(ring[0][4][tid], ring[0][5][tid], ring[0][6][tid], ring[0][7][tid]);
+    w[0] = make_float4(ring[1][0][tid], ring[1][1][tid], ring[1][2][tid], ring[1][3][tid]);
+    w[1] = make_float4(ring[1][4][tid], ring[1][5][tid], ring[1][6][tid], ring[1][7][tid]);
+  } else {
+    for (int i = 0; i < count; ++i) {
+      if (first + i < room) {
+        l1s[at + first + i] = ring[0][i][tid];
+        l1s[slots + at + first + i] = ring[1][i][tid];
+      }
+    }
+  }
+}
+
 template <int MODE, int DIST>
 __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const RasterFwdArgs a) {
   __shared__ float4 s_rec[TILE_PIXELS * REC4];
+  __shared__ float s_ring[(DIST & SF_DIST_L1) ? 2 : 1][L1_RING][TILE_PIXELS];
   __shared__ int s_max;
   const int tile = blockIdx.x;
   const int tid = threadIdx.x;
@@ -93,9 +120,11 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
   const int64_t pix = (int64_t)v * W + u;
   int64_t l1_at = 0;
   int l1_room = 0;
+  bool l1_vec = false;
   if ((DIST & SF_DIST_L1) && inside) {
     l1_at = l1_base(tile, ptid, a.l1_cap, a.l1_off, pix);
     l1_room = a.l1_off ? (int)(a.l1_off[pix + 1] - a.l1_off[pix]) : a.l1_cap;
+    l1_vec = ((l1_at | a.l1_slots) & 3) == 0 && (reinterpret_cast<uintptr_t>(a.l1s) & 15) == 0;
   }
   if (tid == 0) s_max = 0;
   __syncthreads();
@@ -136,10 +165,11 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
         Wd += (double)w;
         if (med < 0 && (float)Wd >= 0.5f) { med = pos; med_depth = s.depth; }
         if (DIST & SF_DIST_L1) {
-          if (cnt < l1_room) {
-            a.l1s[l1_at + cnt] = s.depth;
-            a.l1s[a.l1_slots + l1_at + cnt] = w;
-          }
+          const int slot = cnt & (L1_RING - 1);
+          s_ring[0][slot][tid] = s.depth;
+          s_ring[(DIST & SF_DIST_L1) ? 1 : 0][slot][tid] = w;
+          if (slot == L1_RING - 1)
+            l1_flush(a.l1s, a.l1_slots, l1_at, cnt - (L1_RING - 1), L1_RING, l1_room, l1_vec, s_ring, tid);
         }
         ++cnt;
         last = pos + 1;
@@ -149,6 +179,8 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
     }
   }
 
+  if ((DIST & SF_DIST_L1) && inside && (cnt & (L1_RING - 1)))
+    l1_flush(a.l1s, a.l1_slots, l1_at, cnt & ~(L1_RING - 1), cnt & (L1_RING - 1), l1_room, l1_vec, s_ring, tid);
   if (inside) {
     const float Wf = (float)Wd;
     const float* bg = a.st.background;
@@ -438,12 +470,13 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
   const float wy0 = warp_minf(pr.py), wy1 = warp_maxf(pr.py);
   const int2 rg = a.ranges[tile];
   const float ext2 = a.st.extent_sq, nearp = a.st.near_plane, farp = a.st.far_plane;
-  const float fx = a.cam.K[0], fy = a.cam.K[4];
+  const float inv_fx = 1.f / a.cam.K[0], inv_fy = 1.f / a.cam.K[4];
 
   PixelGrads pg;
   float T = 1.f;
   int last = rg.x, k = -1;
   int64_t l1_at = 0;
+  float next_auxw = 0.f, next_auxd = 0.f;
   if (inside) {
     const float* st = a.state + pix * SF_PIXEL_STATE_FLOATS;
     PixelUpstream up;
@@ -468,6 +501,10 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
       // never read past the pixel's run
       const int room = a.l1_off ? (int)(a.l1_off[pix + 1] - a.l1_off[pix]) : a.l1_cap;
       if (k >= room) k = room - 1;
+      if (k >= 0) {
+        next_auxw = a.l1s[l1_at + k];
+        next_auxd = a.l1s[a.l1_slots + l1_at + k];
+      }
     }
   } else {
     pg.gW = pg.gD = pg.gDnum = pg.gA = pg.gL1 = pg.gL2 = pg.gMed = pg.gVar = 0.f;
@@ -517,25 +554,31 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const Rast
         // k-th contributing sample (counted from the end) is its k-th stored sample
         const bool contrib = eval_sample<MODE>(rec, pr, ext2, nearp, farp, s);
         if ((DIST & SF_DIST_L1) && contrib) {
-          if (k >= 0) {
-            auxw = a.l1s[l1_at + k];
-            auxd = a.l1s[a.l1_slots + l1_at + k];
-          }
+          // the factors of this sample were fetched one contributing sample ahead
+          auxw = next_auxw;
+          auxd = next_auxd;
           --k;
+          if (k >= 0) {
+            next_auxw = a.l1s[l1_at + k];
+            next_auxd = a.l1s[a.l1_slots + l1_at + k];
+          } else {
+            next_auxw = next_auxd = 0.f;
+          }
         }
         if (contrib) {
           act = true;
           const float al = s.alpha;
-          const float om = 1.f - al;
-          const float Ti = T / om;
+          const float om = 1.f - al;  // >= 0.001: alpha is clamped to 0.999
+          const float inv_om = fast_rcp(om);
+          const float Ti = T * inv_om;
           const float w = al * Ti;
           const float adj = sample_adj<MODE>(rec, s, pg, auxw);
-          const float g_alpha = Ti * adj - S / om;
+          const float g_alpha = Ti * adj - S * inv_om;
           S += w * adj;
           T = Ti;
           float g_depth = w * pg.gD + (pos == pg.med_pos ? pg.gMed : 0.f) + pg.gL1 * auxd;
           if (DIST & SF_DIST_L2) g_depth += pg.gL2 * 4.f * w * (pg.W * s.depth - pg.D);
-          sample_backward<MODE>(rec, pr, s, pg, w, g_alpha, g_depth, fx, fy, vals);
+          sample_backward<MODE>(rec, pr, s, pg, w, g_alpha, g_depth, inv_fx, inv_fy, vals);
         }
       }
       if (__any_sync(FULL, act)) {
@@ -593,7 +636,9 @@ __global__ void raster_finalize_kernel(const float* records, int64_t n, sf_camer
 
 __global__ void pixel_counts_kernel(const float* state, int64_t npix, int32_t* counts) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < npix) counts[i] = f2i(state[i * SF_PIXEL_STATE_FLOATS + PS_COUNT]);
+  // runs rounded up to whole 8-sample groups (32-byte aligned starts for the forward's
+  // sector-sized L1 stores)
+  if (i < npix) counts[i] = (f2i(state[i * SF_PIXEL_STATE_FLOATS + PS_COUNT]) + 7) & ~7;
 }
 
 template <int MODE>

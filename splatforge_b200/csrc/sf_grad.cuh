@@ -90,7 +90,7 @@ template <> struct SampleLayout<SF_MODE_AMBISUR> {
 template <int MODE>
 SF_HD void sample_backward(const float* rec, const PixelRay& pr, const Sample& s,
                            const PixelGrads& pg, float w, float g_alpha, float g_depth,
-                           float fx, float fy, float* v) {
+                           float inv_fx, float inv_fy, float* v) {
   float g_a = (s.a_raw >= 0.f && s.a_raw <= 0.999f) ? g_alpha : 0.f;
   float opa = rec[R_OPA];
   float g_resp = opa * g_a;
@@ -113,8 +113,9 @@ SF_HD void sample_backward(const float* rec, const PixelRay& pr, const Sample& s
     gQ[5] = g_e * s.off[2] * s.off[2];
     float g_t = g_depth + (r[0] * goff0 + r[1] * goff1 + r[2] * goff2);
     float gp0 = -goff0, gp1 = -goff1, gp2 = -goff2;
-    float g_num = g_t / s.den;
-    float g_den = -g_t * s.t / s.den;
+    const float inv_den = 1.f / s.den;
+    float g_num = g_t * inv_den;
+    float g_den = -g_num * s.t;
     gp0 += g_num * s.qd[0]; gp1 += g_num * s.qd[1]; gp2 += g_num * s.qd[2];
     float gqd0 = g_num * pm[0], gqd1 = g_num * pm[1], gqd2 = g_num * pm[2];
     if (s.den_raw >= 1e-12f) { gqd0 += g_den * r[0]; gqd1 += g_den * r[1]; gqd2 += g_den * r[2]; }
@@ -134,8 +135,8 @@ SF_HD void sample_backward(const float* rec, const PixelRay& pr, const Sample& s
     v[1] = w * pg.gC[0]; v[2] = w * pg.gC[1]; v[3] = w * pg.gC[2];
     v[4] = gp0; v[5] = gp1; v[6] = gp2;
     for (int k = 0; k < 6; ++k) v[7 + k] = gQ[k];
-    v[13] = fabsf(gp0 * z / fx);
-    v[14] = fabsf(gp1 * z / fy);
+    v[13] = fabsf(gp0 * z * inv_fx);
+    v[14] = fabsf(gp1 * z * inv_fy);
   } else {
     float g_sq = -0.5f * s.resp * g_resp;
     float qa = rec[R_QA], qb = rec[R_QB], qc = rec[R_QC];
@@ -156,8 +157,9 @@ SF_HD void sample_backward(const float* rec, const PixelRay& pr, const Sample& s
       v[12] = w * pg.gN[0]; v[13] = w * pg.gN[1]; v[14] = w * pg.gN[2];
       v[15] = fabsf(gdx); v[16] = fabsf(gdy);
     } else {
-      float g_plane = g_depth / s.aden + w * pg.gDnum;
-      float g_aden = -g_depth * s.depth / s.aden;
+      const float inv_aden = 1.f / s.aden;
+      float g_plane = g_depth * inv_aden + w * pg.gDnum;
+      float g_aden = -g_depth * s.depth * inv_aden;
       v[0] = -gdx; v[1] = -gdy;
       v[2] = gqa; v[3] = gqb; v[4] = gqc;
       v[5] = d_op;

@@ -73,6 +73,15 @@ SF_HD float dot3(float a0, float a1, float a2, float b0, float b1, float b2) {
 }
 
 SF_HD float fmaxr(float a, float b) { return a > b ? a : b; }
+
+// reciprocal for values that feed no discrete decision (within 2 ulp on the device)
+SF_HD float fast_rcp(float a) {
+#if defined(__CUDA_ARCH__)
+  return __fdividef(1.f, a);
+#else
+  return 1.f / a;
+#endif
+}
 SF_HD int f2i(float f) {
 #if defined(__CUDA_ARCH__)
   return __float_as_int(f);
@@ -174,6 +183,19 @@ SF_HD void unit3(const float* v, float* out) {
   float n = fmaxr(norm3(v), 1e-12f);
   out[0] = v[0] / n; out[1] = v[1] / n; out[2] = v[2] / n;
 }
+// unit3 for values that feed no discrete decision (the per-sample GOF normal): one
+// reciprocal square root instead of a square root and three divisions.  Same guard
+// as F.normalize: v / max(|v|, 1e-12).
+SF_HD void unit3_fast(const float* v, float* out) {
+  const float s = v[0] * v[0] + v[1] * v[1] + v[2] * v[2];
+#if defined(__CUDA_ARCH__)
+  const float inv = rsqrtf(fmaxf(s, 1e-24f));
+#else
+  const float inv = 1.f / sqrtf(s > 1e-24f ? s : 1e-24f);
+#endif
+  out[0] = v[0] * inv; out[1] = v[1] * inv; out[2] = v[2] * inv;
+}
+
 SF_HD void unit3_backward(const float* v, const float* g, float* gv) {
   float n = norm3(v);
   if (n >= 1e-12f) {
@@ -591,7 +613,7 @@ SF_HD bool eval_sample(const float* rec, const PixelRay& pr, float ext2, float n
     resp = expf(rmul(-0.5f, fmaxr(s.e, 0.f)));
     s.depth = s.t;
     float mq[3] = {-s.qd[0], -s.qd[1], -s.qd[2]};
-    unit3(mq, s.n);
+    unit3_fast(mq, s.n);
   } else {
     resp = expf(rmul(-0.5f, s.sq));
     if (MODE == SF_MODE_RADEGS) {
