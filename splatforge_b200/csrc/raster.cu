@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const Raste
 // factors per sample, written back in place (by compositing index) once every lane has
 // read its originals.  Returns this lane's share of the raw L1.
 template <int I>
-__device__ __forceinline__ float l1_sort_pixel(float* col_d, float* col_w, int64_t base, int n, int lane) {
+__device__ __noinline__ float l1_sort_pixel(float* col_d, float* col_w, int64_t base, int n, int lane) {
   constexpr int NN = 32 * I;
   // key = depth bits (positive depths order like their bit patterns) : sample index;
   // padding sorts last
@@ -350,6 +350,116 @@ __device__ __forceinline__ float l1_sort_pixel(float* col_d, float* col_w, int64
   return raw;
 }
 
+// The same resolve with 32-bit keys: key = ((depth bits - smallest depth bits) << LOGN)
+// | compositing index, LOGN = log2(32 I).  Depths of contributing samples are positive
+// and finite, so their bit patterns order like their values; when the pixel's span of
+// depth bit patterns fits in 32 - LOGN bits (for 256 samples: max/min depth ratio
+// below about 4), the packed keys are exact, unique and order like (depth, index),
+// and the network needs no payload: unsigned min/max only.  Returns false (nothing
+// written) when the span does not fit; the caller then runs the 64-bit path.
+template <int I>
+__device__ __forceinline__ bool l1_sort_pixel_packed(float* col_d, float* col_w, int64_t base, int n, int lane,
+                                                     float& raw_out) {
+  constexpr int NN = 32 * I;
+  constexpr int LOGN = (NN == 128) ? 7 : (NN == 256 ? 8 : 9);
+  static_assert(NN == (1 << LOGN), "power of two");
+  uint32_t key[I];
+  uint32_t lo = 0xffffffffu, hi = 0u;
+#pragma unroll
+  for (int j = 0; j < I; ++j) {
+    const int e = lane * I + j;
+    key[j] = e < n ? __float_as_uint(col_d[base + e]) : 0u;
+    if (e < n) { lo = min(lo, key[j]); hi = max(hi, key[j]); }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = min(lo, __shfl_xor_sync(FULL, lo, o));
+    hi = max(hi, __shfl_xor_sync(FULL, hi, o));
+  }
+  if (hi - lo >= (1u << (32 - LOGN))) return false;  // warp-uniform
+#pragma unroll
+  for (int j = 0; j < I; ++j) {
+    const int e = lane * I + j;
+    // padding sorts last: a real key is at most (2^(32-LOGN) - 1) << LOGN | (n - 1),
+    // and n - 1 < NN - 1 whenever there is padding
+    key[j] = e < n ? ((key[j] - lo) << LOGN) | (uint32_t)e : 0xffffffffu;
+  }
+  // sizes up to I sort inside each lane ...
+#pragma unroll
+  for (int size = 2; size <= I; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int j = 0; j < I; ++j) {
+        if ((j & stride) == 0) {
+          const bool up = ((lane * I + j) & size) == 0;
+          const uint32_t a = min(key[j], key[j + stride]), b = max(key[j], key[j + stride]);
+          key[j] = up ? a : b;
+          key[j + stride] = up ? b : a;
+        }
+      }
+    }
+  }
+  // ... then each larger merge: cross-lane strides rolled, in-lane strides unrolled
+#pragma unroll 1
+  for (int size = 2 * I; size <= NN; size <<= 1) {
+    const bool up = ((lane * I) & size) == 0;
+#pragma unroll 1
+    for (int lm = size / (2 * I); lm > 0; lm >>= 1) {
+      const bool take_min = ((lane & lm) == 0) == up;
+#pragma unroll
+      for (int j = 0; j < I; ++j) {
+        const uint32_t o = __shfl_xor_sync(FULL, key[j], lm);
+        key[j] = take_min ? min(key[j], o) : max(key[j], o);
+      }
+    }
+#pragma unroll
+    for (int stride = I >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int j = 0; j < I; ++j) {
+        if ((j & stride) == 0) {
+          const uint32_t a = min(key[j], key[j + stride]), b = max(key[j], key[j + stride]);
+          key[j] = up ? a : b;
+          key[j + stride] = up ? b : a;
+        }
+      }
+    }
+  }
+  float w[I];
+  float lw = 0.f, lwd = 0.f;
+#pragma unroll
+  for (int j = 0; j < I; ++j) {
+    const bool live = key[j] != 0xffffffffu;
+    w[j] = live ? col_w[base + (key[j] & (NN - 1))] : 0.f;
+    lw += w[j];
+    lwd += w[j] * (live ? __uint_as_float((key[j] >> LOGN) + lo) : 0.f);
+  }
+  float iw = lw, iwd = lwd;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float a1 = __shfl_up_sync(FULL, iw, o), a2 = __shfl_up_sync(FULL, iwd, o);
+    if (lane >= o) { iw += a1; iwd += a2; }
+  }
+  const float Wt = __shfl_sync(FULL, iw, 31), Dt = __shfl_sync(FULL, iwd, 31);
+  float pw = iw - lw, pwd = iwd - lwd;
+  float raw = 0.f;
+  __syncwarp();  // every lane has read its originals
+#pragma unroll
+  for (int j = 0; j < I; ++j) {
+    if (key[j] != 0xffffffffu) {
+      const uint32_t k = key[j] & (NN - 1);
+      const float d = __uint_as_float((key[j] >> LOGN) + lo);
+      raw += 2.f * w[j] * (d * pw - pwd);
+      col_d[base + k] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
+      col_w[base + k] = 2.f * w[j] * (2.f * pw + w[j] - Wt);
+      pw += w[j];
+      pwd += w[j] * d;
+    }
+  }
+  raw_out = raw;
+  return true;
+}
+
 // CLASS 0 resolves pixels with at most 256 samples (register sorts), CLASS 1 those
 // with 257..512 (16 per lane), CLASS 2 longer runs (shared-memory radix sort); each
 // launch skips the pixels of the other classes, so the register budget of the rare
@@ -389,12 +499,15 @@ __global__ void __launch_bounds__(128) l1_resolve_kernel(
       if (n <= 1) {
         if (n == 1 && lane == 0) { col_d[base] = 0.f; col_w[base] = 0.f; }
       } else if (n <= 128) {
-                  raw = l1_sort_pixel<4>(col_d, col_w, base, n, lane);
+        if (!l1_sort_pixel_packed<4>(col_d, col_w, base, n, lane, raw))
+          raw = l1_sort_pixel<4>(col_d, col_w, base, n, lane);
       } else {
-                  raw = l1_sort_pixel<8>(col_d, col_w, base, n, lane);
+        if (!l1_sort_pixel_packed<8>(col_d, col_w, base, n, lane, raw))
+          raw = l1_sort_pixel<8>(col_d, col_w, base, n, lane);
       }
     } else if (CLASS == 1) {
-              raw = l1_sort_pixel<16>(col_d, col_w, base, n, lane);
+      if (!l1_sort_pixel_packed<16>(col_d, col_w, base, n, lane, raw))
+        raw = l1_sort_pixel<16>(col_d, col_w, base, n, lane);
     } else {
       // long runs: stable warp radix sort staged in shared memory
       float Wt = 0.f, Dt = 0.f;
