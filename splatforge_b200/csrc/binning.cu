@@ -131,17 +131,29 @@ constexpr int RS_ROUNDS = 16;                         // 32-key rounds per warp
 constexpr int RS_CHUNK = RS_THREADS * RS_ROUNDS;      // keys per CTA
 constexpr int RADIX = 256;
 
+// Per-block digit histograms.  Each thread reads its keys four at a time (128-bit
+// loads) when the block's slab is 16-byte aligned.
 __global__ void __launch_bounds__(RS_THREADS) radix_upsweep_kernel(const uint32_t* keys, int64_t n,
                                                                    int shift, int nb, uint32_t* hist) {
   __shared__ uint32_t s_hist[RS_WARPS][RADIX];
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int wid = threadIdx.x >> 5;
   for (int k = threadIdx.x; k < RS_WARPS * RADIX; k += RS_THREADS) (&s_hist[0][0])[k] = 0;
   __syncthreads();
-  const int64_t base = (int64_t)blockIdx.x * RS_CHUNK + (int64_t)wid * (RS_CHUNK / RS_WARPS);
-#pragma unroll 4
-  for (int r = 0; r < RS_ROUNDS; ++r) {
-    const int64_t idx = base + r * 32 + lane;
-    if (idx < n) atomicAdd(&s_hist[wid][(keys[idx] >> shift) & 0xff], 1u);
+  const int64_t block0 = (int64_t)blockIdx.x * RS_CHUNK;
+  const int rows = (int)min((int64_t)RS_CHUNK, n - block0);
+  if (rows == RS_CHUNK && (reinterpret_cast<uintptr_t>(keys + block0) & 15) == 0) {
+    const uint4* k4 = reinterpret_cast<const uint4*>(keys + block0);
+#pragma unroll
+    for (int r = 0; r < RS_CHUNK / 4 / RS_THREADS; ++r) {
+      const uint4 v = k4[r * RS_THREADS + threadIdx.x];
+      atomicAdd(&s_hist[wid][(v.x >> shift) & 0xff], 1u);
+      atomicAdd(&s_hist[wid][(v.y >> shift) & 0xff], 1u);
+      atomicAdd(&s_hist[wid][(v.z >> shift) & 0xff], 1u);
+      atomicAdd(&s_hist[wid][(v.w >> shift) & 0xff], 1u);
+    }
+  } else {
+    for (int i = threadIdx.x; i < rows; i += RS_THREADS)
+      atomicAdd(&s_hist[wid][(keys[block0 + i] >> shift) & 0xff], 1u);
   }
   __syncthreads();
   const int d = threadIdx.x;  // RS_THREADS == RADIX
@@ -320,12 +332,29 @@ __global__ void emit_kernel(const int32_t* order, const int64_t* offsets, const 
   }
 }
 
+// Per-tile [begin, end) of the sorted tile indices: each thread checks four
+// consecutive entries (one 128-bit load plus its two neighbours) for boundaries.
 __global__ void ranges_kernel(const uint32_t* tiles, int64_t n, int2* ranges) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const uint32_t t = tiles[i];
-  if (i == 0 || tiles[i - 1] != t) ranges[t].x = (int)i;
-  if (i == n - 1 || tiles[i + 1] != t) ranges[t].y = (int)(i + 1);
+  const int64_t i0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i0 >= n) return;
+  constexpr uint32_t NONE = 0xffffffffu;  // never a tile index
+  uint32_t t[6];
+  t[0] = i0 > 0 ? tiles[i0 - 1] : NONE;
+  if (i0 + 4 <= n) {
+    const uint4 v = *reinterpret_cast<const uint4*>(tiles + i0);
+    t[1] = v.x; t[2] = v.y; t[3] = v.z; t[4] = v.w;
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) t[1 + k] = i0 + k < n ? tiles[i0 + k] : NONE;
+  }
+  t[5] = i0 + 4 < n ? tiles[i0 + 4] : NONE;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t cur = t[1 + k];
+    if (cur == NONE) break;
+    if (t[k] != cur) ranges[cur].x = (int)(i0 + k);
+    if (t[k + 2] != cur) ranges[cur].y = (int)(i0 + k + 1);
+  }
 }
 
 __global__ void keys_kernel(const int32_t* ids, const int2* ranges, const uint32_t* depth_key,
@@ -432,7 +461,7 @@ cudaError_t bin_emit(const int32_t* order, const int64_t* offsets, const int32_t
   e = radix_sort(tA, vA, tB, vB, m, bits, sc, &kf, &vf, ids, s);
   if (e != cudaSuccess) return e;
   count_launches(1);
-  ranges_kernel<<<grid_for(m, 256), 256, 0, s>>>(kf, m, reinterpret_cast<int2*>(ranges));
+  ranges_kernel<<<grid_for((m + 3) / 4, 256), 256, 0, s>>>(kf, m, reinterpret_cast<int2*>(ranges));
   return cudaGetLastError();
 }
 

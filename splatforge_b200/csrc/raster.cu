@@ -94,7 +94,7 @@ __device__ __forceinline__ void l1_flush(float* l1s, int64_t slots, int64_t at, 
 }
 
 template <int MODE, int DIST>
-__global__ void __launch_bounds__(TILE_PIXELS) raster_forward_kernel(const RasterFwdArgs a) {
+__global__ void __launch_bounds__(TILE_PIXELS, 4) raster_forward_kernel(const RasterFwdArgs a) {
   __shared__ float4 s_rec[TILE_PIXELS * REC4];
   __shared__ float s_ring[(DIST & SF_DIST_L1) ? 2 : 1][L1_RING][TILE_PIXELS];
   __shared__ int s_max;

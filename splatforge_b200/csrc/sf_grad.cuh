@@ -96,14 +96,10 @@ SF_HD void sample_backward(const float* rec, const PixelRay& pr, const Sample& s
   float g_resp = opa * g_a;
   float d_op = s.resp * g_a;
   if (MODE == SF_MODE_GOF) {
-    const float* q = rec + R_Q3;
     const float* r = pr.r;
     const float* pm = rec + R_PROXY;
     float g_e = (s.e >= 0.f) ? -0.5f * s.resp * g_resp : 0.f;
-    float qo0 = q[0] * s.off[0] + q[1] * s.off[1] + q[2] * s.off[2];
-    float qo1 = q[1] * s.off[0] + q[3] * s.off[1] + q[4] * s.off[2];
-    float qo2 = q[2] * s.off[0] + q[4] * s.off[1] + q[5] * s.off[2];
-    float goff0 = 2.f * g_e * qo0, goff1 = 2.f * g_e * qo1, goff2 = 2.f * g_e * qo2;
+    float goff0 = 2.f * g_e * s.qo[0], goff1 = 2.f * g_e * s.qo[1], goff2 = 2.f * g_e * s.qo[2];
     float gQ[6];
     gQ[0] = g_e * s.off[0] * s.off[0];
     gQ[1] = 2.f * g_e * s.off[0] * s.off[1];
@@ -119,11 +115,15 @@ SF_HD void sample_backward(const float* rec, const PixelRay& pr, const Sample& s
     gp0 += g_num * s.qd[0]; gp1 += g_num * s.qd[1]; gp2 += g_num * s.qd[2];
     float gqd0 = g_num * pm[0], gqd1 = g_num * pm[1], gqd2 = g_num * pm[2];
     if (s.den_raw >= 1e-12f) { gqd0 += g_den * r[0]; gqd1 += g_den * r[1]; gqd2 += g_den * r[2]; }
-    float gn[3] = {w * pg.gN[0], w * pg.gN[1], w * pg.gN[2]};
-    float mq[3] = {-s.qd[0], -s.qd[1], -s.qd[2]};
-    float gmq[3];
-    unit3_backward(mq, gn, gmq);
-    gqd0 -= gmq[0]; gqd1 -= gmq[1]; gqd2 -= gmq[2];
+    // adjoint of n = normalize(-qd) with the forward's unit vector and inverse norm
+    {
+      const float g0 = w * pg.gN[0], g1 = w * pg.gN[1], g2 = w * pg.gN[2];
+      const float d = s.n[0] * g0 + s.n[1] * g1 + s.n[2] * g2;
+      const float c = s.ninv < 1e12f ? 1.f : 0.f;  // below the guard: n = -qd * 1e12
+      gqd0 -= (g0 - c * s.n[0] * d) * s.ninv;
+      gqd1 -= (g1 - c * s.n[1] * d) * s.ninv;
+      gqd2 -= (g2 - c * s.n[2] * d) * s.ninv;
+    }
     gQ[0] += gqd0 * r[0];
     gQ[1] += gqd0 * r[1] + gqd1 * r[0];
     gQ[2] += gqd0 * r[2] + gqd2 * r[0];

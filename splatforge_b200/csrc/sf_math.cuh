@@ -183,19 +183,6 @@ SF_HD void unit3(const float* v, float* out) {
   float n = fmaxr(norm3(v), 1e-12f);
   out[0] = v[0] / n; out[1] = v[1] / n; out[2] = v[2] / n;
 }
-// unit3 for values that feed no discrete decision (the per-sample GOF normal): one
-// reciprocal square root instead of a square root and three divisions.  Same guard
-// as F.normalize: v / max(|v|, 1e-12).
-SF_HD void unit3_fast(const float* v, float* out) {
-  const float s = v[0] * v[0] + v[1] * v[1] + v[2] * v[2];
-#if defined(__CUDA_ARCH__)
-  const float inv = rsqrtf(fmaxf(s, 1e-24f));
-#else
-  const float inv = 1.f / sqrtf(s > 1e-24f ? s : 1e-24f);
-#endif
-  out[0] = v[0] * inv; out[1] = v[1] * inv; out[2] = v[2] * inv;
-}
-
 SF_HD void unit3_backward(const float* v, const float* g, float* gv) {
   float n = norm3(v);
   if (n >= 1e-12f) {
@@ -576,8 +563,8 @@ struct Sample {
   float alpha;     // clamped
   float depth;
   float n[3];      // sample normal (GOF: normalize(-Q d); else per-Gaussian)
-  // GOF intermediates
-  float qd[3], den_raw, den, t, off[3], e;
+  // GOF intermediates (qo = Q off; ninv = 1 / max(|Q r|, 1e-12))
+  float qd[3], den_raw, den, t, off[3], e, qo[3], ninv;
   // AmbiSuR intermediates
   float aden;
   bool aok;
@@ -606,14 +593,20 @@ SF_HD bool eval_sample(const float* rec, const PixelRay& pr, float ext2, float n
     s.off[0] = ffma(s.t, r[0], -pm[0]);
     s.off[1] = ffma(s.t, r[1], -pm[1]);
     s.off[2] = ffma(s.t, r[2], -pm[2]);
-    const float o0 = dot3(q[0], q[1], q[2], s.off[0], s.off[1], s.off[2]);
-    const float o1 = dot3(q[1], q[3], q[4], s.off[0], s.off[1], s.off[2]);
-    const float o2 = dot3(q[2], q[4], q[5], s.off[0], s.off[1], s.off[2]);
-    s.e = dot3(s.off[0], s.off[1], s.off[2], o0, o1, o2);
+    s.qo[0] = dot3(q[0], q[1], q[2], s.off[0], s.off[1], s.off[2]);
+    s.qo[1] = dot3(q[1], q[3], q[4], s.off[0], s.off[1], s.off[2]);
+    s.qo[2] = dot3(q[2], q[4], q[5], s.off[0], s.off[1], s.off[2]);
+    s.e = dot3(s.off[0], s.off[1], s.off[2], s.qo[0], s.qo[1], s.qo[2]);
     resp = expf(rmul(-0.5f, fmaxr(s.e, 0.f)));
     s.depth = s.t;
-    float mq[3] = {-s.qd[0], -s.qd[1], -s.qd[2]};
-    unit3_fast(mq, s.n);
+    // normal = normalize(-Q r), one reciprocal square root (F.normalize's 1e-12 guard)
+    const float nn = s.qd[0] * s.qd[0] + s.qd[1] * s.qd[1] + s.qd[2] * s.qd[2];
+#if defined(__CUDA_ARCH__)
+    s.ninv = rsqrtf(fmaxf(nn, 1e-24f));
+#else
+    s.ninv = 1.f / sqrtf(nn > 1e-24f ? nn : 1e-24f);
+#endif
+    s.n[0] = -s.qd[0] * s.ninv; s.n[1] = -s.qd[1] * s.ninv; s.n[2] = -s.qd[2] * s.ninv;
   } else {
     resp = expf(rmul(-0.5f, s.sq));
     if (MODE == SF_MODE_RADEGS) {
