@@ -212,6 +212,27 @@ int sf_b200_opacity_field(const float* points, int64_t n_points, const float* me
                           int64_t n_gaussians, const float* origins, int32_t n_origins,
                           float* field, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same field for large query sets (the GOF exporter's grid, exporters.py:42-102):
+ * per view, Gaussians are binned into a cube map of face_cells x face_cells cells per
+ * face around the origin by the cone of directions in which each can contribute more
+ * than `cutoff` (0 < cutoff < 1); a query visits only its own direction's cell.
+ * Contributions at or below `cutoff` are dropped, so the field differs from
+ * sf_b200_opacity_field by at most about cutoff times the number of dropped terms.
+ * No counterpart in the reference (its field is the brute-force loop).  Synchronises
+ * the stream once per origin (candidate counts are read back).  max_pairs sizes the
+ * per-view candidate lists in the workspace; *pairs_needed (host, may be NULL)
+ * receives the largest per-view count; if that exceeds max_pairs the call returns
+ * SF_ERR_CAPACITY and the caller retries with a larger workspace. */
+int sf_b200_opacity_field_culled_workspace_bytes(int64_t n_points, int64_t n_gaussians,
+                                                 int64_t max_pairs, int32_t face_cells,
+                                                 size_t* bytes);
+int sf_b200_opacity_field_culled(const float* points, int64_t n_points, const float* means,
+                                 const float* inverse_covariances, const float* opacities,
+                                 int64_t n_gaussians, const float* origins, int32_t n_origins,
+                                 float cutoff, int32_t face_cells, float* field, void* workspace,
+                                 size_t workspace_bytes, int64_t max_pairs, int64_t* pairs_needed,
+                                 void* stream);
+
 /* ---- raster forward (batched_renderer.py:169-338 + alpha_composite@3) -----------
  * One CTA per 16x16 tile.  Images are HWC float32: rgb/normals [H,W,3], the rest
  * [H,W].  pixel_state [H*W, SF_PIXEL_STATE_FLOATS] is kept for the backward pass.

@@ -14,6 +14,7 @@ PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libsf_b200.so"
 
 SF_OK = 0
+SF_ERR_CAPACITY = 3
 MODE = {"radegs": 0, "gof": 1, "ambisur": 2}
 DISTORTIONS = {"none": 0, "l1": 1, "l2": 2, "both": 3}
 RECORD_FLOATS = 20
@@ -90,6 +91,13 @@ _SIGNATURES = {
     "sf_b200_alpha_composite_backward": (
         ctypes.c_int,
         [P, P, P, P, c_int64, c_int64, c_int64, c_int32, P, P, c_size_t] + [P] * 8 + [P] * 4 + [P],
+    ),
+    "sf_b200_opacity_field_culled_workspace_bytes": (
+        ctypes.c_int, [c_int64, c_int64, c_int64, c_int32, POINTER(c_size_t)]
+    ),
+    "sf_b200_opacity_field_culled": (
+        ctypes.c_int,
+        [P, c_int64, P, P, P, c_int64, P, c_int32, c_float, c_int32, P, P, c_size_t, c_int64, POINTER(c_int64), P],
     ),
     "sf_b200_raster_forward": (
         ctypes.c_int,

@@ -465,6 +465,43 @@ cudaError_t bin_emit(const int32_t* order, const int64_t* offsets, const int32_t
   return cudaGetLastError();
 }
 
+size_t sort_pairs_workspace_bytes(int64_t n) {
+  Carve c{nullptr};
+  c.take<uint32_t>(n); c.take<int32_t>(n);
+  c.take<uint32_t>(RADIX * radix_blocks(n));
+  c.take<uint32_t>(scan_blocks(RADIX * radix_blocks(n)) + 1);
+  return c.used;
+}
+
+cudaError_t sort_pairs(uint32_t* keys, int32_t* vals, int64_t n, int bits, void* ws, size_t ws_bytes,
+                       cudaStream_t s) {
+  if (ws_bytes < sort_pairs_workspace_bytes(n)) return cudaErrorInvalidValue;
+  if (n == 0 || bits <= 0) return cudaSuccess;
+  Carve c{reinterpret_cast<char*>(ws)};
+  uint32_t* k1 = c.take<uint32_t>(n);
+  int32_t* v1 = c.take<int32_t>(n);
+  RadixScratch sc;
+  sc.hist = c.take<uint32_t>(RADIX * radix_blocks(n));
+  sc.partial = c.take<uint32_t>(scan_blocks(RADIX * radix_blocks(n)) + 1);
+  uint32_t* kf;
+  int32_t* vf;
+  cudaError_t e = radix_sort(keys, vals, k1, v1, n, bits, sc, &kf, &vf, nullptr, s);
+  if (e != cudaSuccess) return e;
+  if (kf != keys) {
+    e = cudaMemcpyAsync(keys, kf, (size_t)n * sizeof(uint32_t), cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(vals, vf, (size_t)n * sizeof(int32_t), cudaMemcpyDeviceToDevice, s);
+  }
+  return e;
+}
+
+cudaError_t key_ranges(const uint32_t* keys, int64_t n, int64_t n_keys, int32_t* ranges, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(ranges, 0, sizeof(int2) * (size_t)n_keys, s);
+  if (e != cudaSuccess || n == 0) return e;
+  count_launches(1);
+  ranges_kernel<<<grid_for((n + 3) / 4, 256), 256, 0, s>>>(keys, n, reinterpret_cast<int2*>(ranges));
+  return cudaGetLastError();
+}
+
 cudaError_t bin_keys(const int32_t* ids, const int32_t* ranges, const uint32_t* depth_key,
                      int n_tiles, int64_t m, uint64_t* keys, cudaStream_t s) {
   (void)m;

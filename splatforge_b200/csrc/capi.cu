@@ -321,6 +321,48 @@ int sf_b200_opacity_field(const float* points, int64_t n_points, const float* me
                      "opacity_field");
 }
 
+int sf_b200_opacity_field_culled_workspace_bytes(int64_t n_points, int64_t n_gaussians, int64_t max_pairs,
+                                                 int32_t face_cells, size_t* bytes) {
+  if (n_points < 0 || n_gaussians < 0 || max_pairs < 0 || face_cells < 1 || face_cells > 1024 || !bytes)
+    return fail(SF_ERR_ARGUMENT, "opacity_field_culled_workspace_bytes: bad arguments");
+  *bytes = sf::field_culled_workspace_bytes(n_gaussians, max_pairs, face_cells) +
+           sf::field_culled_query_bytes(n_points, face_cells);
+  return SF_OK;
+}
+
+int sf_b200_opacity_field_culled(const float* points, int64_t n_points, const float* means,
+                                 const float* inverse_covariances, const float* opacities, int64_t n_gaussians,
+                                 const float* origins, int32_t n_origins, float cutoff, int32_t face_cells,
+                                 float* field, void* workspace, size_t workspace_bytes, int64_t max_pairs,
+                                 int64_t* pairs_needed, void* stream) {
+  if (n_points < 0 || n_gaussians < 0 || max_pairs < 0) return fail(SF_ERR_ARGUMENT, "opacity_field_culled: negative size");
+  if (n_origins < 1) return fail(SF_ERR_ARGUMENT, "opacity_field_culled: requires at least one origin");
+  if (!(cutoff > 0.f && cutoff < 1.f)) return fail(SF_ERR_ARGUMENT, "opacity_field_culled: cutoff must be in (0, 1)");
+  if (face_cells < 1 || face_cells > 1024) return fail(SF_ERR_ARGUMENT, "opacity_field_culled: face_cells in 1..1024");
+  if (n_points > 0 && (!points || !field || !origins)) return fail(SF_ERR_ARGUMENT, "opacity_field_culled: NULL buffer");
+  if (n_gaussians > 0 && (!means || !inverse_covariances || !opacities || !workspace))
+    return fail(SF_ERR_ARGUMENT, "opacity_field_culled: NULL buffer");
+  if (n_gaussians > INT32_MAX || max_pairs > ((int64_t)1 << 31))
+    return fail(SF_ERR_ARGUMENT, "opacity_field_culled: 32-bit index range exceeded");
+  if (n_points > INT32_MAX) return fail(SF_ERR_ARGUMENT, "opacity_field_culled: 32-bit index range exceeded");
+  const size_t need = sf::field_culled_workspace_bytes(n_gaussians, max_pairs, face_cells) +
+                      sf::field_culled_query_bytes(n_points, face_cells);
+  if (workspace_bytes < need) return fail(SF_ERR_CAPACITY, "opacity_field_culled: workspace of %zu bytes, %zu needed",
+                                          workspace_bytes, need);
+  int64_t most = 0;
+  const int rc = cuda_status(sf::launch_opacity_field_culled(points, n_points, means, inverse_covariances, opacities,
+                                                             n_gaussians, origins, n_origins, cutoff, face_cells,
+                                                             field, workspace, workspace_bytes, max_pairs, &most,
+                                                             as_stream(stream)),
+                             "opacity_field_culled");
+  if (pairs_needed) *pairs_needed = most;
+  if (rc != SF_OK) return rc;
+  if (most > max_pairs)
+    return fail(SF_ERR_CAPACITY, "opacity_field_culled: %lld candidate pairs in one view, max_pairs is %lld",
+                (long long)most, (long long)max_pairs);
+  return SF_OK;
+}
+
 int sf_b200_composite_workspace_bytes(int64_t B, int64_t N, int64_t P, int32_t distortions, size_t* bytes) {
   if (B < 0 || N < 0 || P < 0 || !bytes) return fail(SF_ERR_ARGUMENT, "composite_workspace_bytes: bad arguments");
   const size_t aux = (distortions & SF_DIST_L1) ? (size_t)2 * B * N * P * sizeof(float) : 0;

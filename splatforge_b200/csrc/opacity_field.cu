@@ -86,6 +86,293 @@ __global__ void field_pack_kernel(const float* means, const float* invcov, const
   r[9] = op[i];
 }
 
+// ------------------------------------------------------------------ culled field
+// For large queries the field is evaluated against per-view candidate lists instead of
+// every Gaussian.  A Gaussian whose opacity o exceeds the cutoff c0 contributes more
+// than c0 only within the ball of radius R = sqrt(2 ln(o / c0) / lambda_min(Q)) around
+// its mean (there (x-m)^T Q (x-m) >= |x-m|^2 lambda_min), and the field samples it on
+// the ray from the view origin through the query point.  So per view the Gaussians are
+// binned into the cells of a cube map around the origin that their ball's cone of
+// directions can reach, and a query only visits the cells of its own direction (plus
+// the Gaussians whose ball contains the origin).  Contributions below c0 are dropped;
+// everything else is evaluated exactly as the brute-force kernel does.
+constexpr int CF_REC = 12;  // mean 3, symmetric Q 6, opacity, bound radius, pad
+
+__device__ __forceinline__ double sym3_min_eig(double a, double b, double c, double d, double e, double f) {
+  // [[a b c] [b d e] [c e f]]: closed-form eigenvalues of a symmetric 3x3 matrix
+  const double p1 = b * b + c * c + e * e;
+  if (p1 == 0.0) return fmin(a, fmin(d, f));
+  const double q = (a + d + f) / 3.0;
+  const double p2 = (a - q) * (a - q) + (d - q) * (d - q) + (f - q) * (f - q) + 2.0 * p1;
+  const double p = sqrt(p2 / 6.0);
+  const double ia = (a - q) / p, id = (d - q) / p, iff = (f - q) / p, ib = b / p, ic = c / p, ie = e / p;
+  double r = 0.5 * (ia * (id * iff - ie * ie) - ib * (ib * iff - ie * ic) + ic * (ib * ie - id * ic));
+  r = fmin(1.0, fmax(-1.0, r));
+  const double phi = acos(r) / 3.0;
+  return q + 2.0 * p * cos(phi + 2.0943951023931957);  // + 2 pi / 3: the smallest
+}
+
+__global__ void cfield_prep_kernel(const float* means, const float* invcov, const float* op, int64_t n,
+                                   float cutoff, float* rec) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float* q = invcov + i * 9;
+  const float a = q[0], b = 0.5f * (q[1] + q[3]), c = 0.5f * (q[2] + q[6]);
+  const float d = q[4], e = 0.5f * (q[5] + q[7]), f = q[8];
+  const float o = op[i];
+  float R;
+  if (!(o > cutoff)) {
+    R = -1.f;  // its contribution never exceeds the cutoff
+  } else {
+    const double lmax = fabs((double)a) + fabs((double)d) + fabs((double)f) + 2.0 * (fabs((double)b) + fabs((double)c) + fabs((double)e));
+    const double lmin = sym3_min_eig(a, b, c, d, e, f) - 1e-9 * lmax;  // err on the small side
+    if (!(lmin > 0.0)) {
+      R = INFINITY;  // not positive definite: never culled
+    } else {
+      const double k2 = 2.0 * log((double)o / (double)cutoff);
+      R = (float)(sqrt(k2 / lmin) * 1.001 + 1e-6);
+    }
+  }
+  float* r = rec + i * CF_REC;
+  r[0] = means[i * 3]; r[1] = means[i * 3 + 1]; r[2] = means[i * 3 + 2];
+  r[3] = a; r[4] = b; r[5] = c; r[6] = d; r[7] = e; r[8] = f;
+  r[9] = o; r[10] = R; r[11] = 0.f;
+}
+
+// Cube map around the origin: face 2*a + (negative), a the major axis of the direction;
+// u = d[b] / |d[a]|, v = d[c] / |d[a]| with b = (a+1)%3, c = (a+2)%3; F x F cells per face.
+__device__ __forceinline__ int cube_cell(float dx, float dy, float dz, int F) {
+  const float ax = fabsf(dx), ay = fabsf(dy), az = fabsf(dz);
+  int a;
+  float m, ub, vc;
+  if (ax >= ay && ax >= az) { a = 0; m = ax; ub = dy; vc = dz; }
+  else if (ay >= az) { a = 1; m = ay; ub = dz; vc = dx; }
+  else { a = 2; m = az; ub = dx; vc = dy; }
+  const float major = a == 0 ? dx : (a == 1 ? dy : dz);
+  const int face = 2 * a + (major < 0.f ? 1 : 0);
+  const float inv = 1.f / m;
+  int ix = (int)floorf((ub * inv + 1.f) * 0.5f * F);
+  int iy = (int)floorf((vc * inv + 1.f) * 0.5f * F);
+  ix = min(max(ix, 0), F - 1);
+  iy = min(max(iy, 0), F - 1);
+  return (face * F + iy) * F + ix;
+}
+
+// Cells [x0, x1] x [y0, y1] of face (axis a, sign s) that a cone of half-angle alpha
+// around the unit direction c can reach: on the face u = tan(psi), psi the angle of
+// the direction in the (a, b) plane, and a cap's psi stays within its centre's psi
+// +- asin(sin(alpha) / cos(latitude about the c axis)) (every psi when the cap holds
+// that axis); likewise v in the (a, c) plane.  Returns false when the cap misses the face.
+__device__ __forceinline__ bool cap_face_box(const float* cv, float sin_a, int a, int s, int F, int& x0, int& x1,
+                                             int& y0, int& y1) {
+  const int b = (a + 1) % 3, c = (a + 2) % 3;
+  const float ca = s > 0 ? cv[a] : -cv[a];
+  const float margin = 1e-4f;
+  float lo[2], hi[2];
+  const int other[2] = {b, c};
+  for (int k = 0; k < 2; ++k) {
+    const int ax = other[k];
+    const float r = sqrtf(ca * ca + cv[ax] * cv[ax]);
+    const float psi = atan2f(cv[ax], ca);
+    float half;
+    if (sin_a >= r) half = 3.2f;  // the cap holds the pole: every angle
+    else half = asinf(sin_a / r) + margin;
+    float p0 = psi - half, p1 = psi + half;
+    const float qpi = 0.78539816f;
+    if (p1 < -qpi || p0 > qpi) return false;
+    p0 = fmaxf(p0, -qpi);
+    p1 = fminf(p1, qpi);
+    lo[k] = tanf(p0);
+    hi[k] = tanf(p1);
+  }
+  x0 = max(0, (int)floorf((lo[0] + 1.f) * 0.5f * F) - 1);
+  x1 = min(F - 1, (int)floorf((hi[0] + 1.f) * 0.5f * F) + 1);
+  y0 = max(0, (int)floorf((lo[1] + 1.f) * 0.5f * F) - 1);
+  y1 = min(F - 1, (int)floorf((hi[1] + 1.f) * 0.5f * F) + 1);
+  return x0 <= x1 && y0 <= y1;
+}
+
+// Per Gaussian and view: the number of cube-map cells its cone reaches (0 for skipped
+// Gaussians and for those whose ball holds the origin, which go to the global list).
+// key: float bits of the ball's nearest distance D - R (positive here), so that the
+// stable depth order puts every cell list front to back; near[i] = D - R for the queries.
+__global__ void cfield_count_kernel(const float* rec, int64_t n, float ox, float oy, float oz, int F,
+                                    int32_t* count, int32_t* global_flag, uint32_t* key, float* near) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float* r = rec + i * CF_REC;
+  const float R = r[10];
+  int total = 0, glob = 0;
+  uint32_t k = 0xffffffffu;
+  float nd = 0.f;
+  if (R >= 0.f) {
+    const float cx = r[0] - ox, cy = r[1] - oy, cz = r[2] - oz;
+    const float D = sqrtf(cx * cx + cy * cy + cz * cz);
+    if (!(D > R * 1.0001f + 1e-6f)) {
+      glob = 1;
+    } else {
+      nd = fmaxf((D - R) * 0.9999f - 1e-6f, 0.f);  // rounded towards the origin
+      k = __float_as_uint(nd);
+      const float cv[3] = {cx / D, cy / D, cz / D};
+      const float sin_a = R / D;
+      for (int face = 0; face < 6; ++face) {
+        int x0, x1, y0, y1;
+        if (cap_face_box(cv, sin_a, face >> 1, (face & 1) ? -1 : 1, F, x0, x1, y0, y1))
+          total += (x1 - x0 + 1) * (y1 - y0 + 1);
+      }
+    }
+  }
+  count[i] = total;
+  global_flag[i] = glob;
+  key[i] = total > 0 ? k : 0xffffffffu;
+  near[i] = nd;
+}
+
+// thread j emits the cells of the j-th Gaussian in depth order (order[j]) at offsets[j]
+__global__ void cfield_emit_kernel(const float* rec, int64_t n, float ox, float oy, float oz, int F,
+                                   const int32_t* order, const int64_t* offsets, const int64_t* goffsets,
+                                   uint32_t* keys, int32_t* vals, int32_t* global_ids) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= n) return;
+  if (goffsets[j + 1] != goffsets[j]) global_ids[goffsets[j]] = (int32_t)j;
+  int64_t at = offsets[j];
+  if (offsets[j + 1] == at) return;
+  const int64_t i = order[j];
+  const float* r = rec + i * CF_REC;
+  const float cx = r[0] - ox, cy = r[1] - oy, cz = r[2] - oz;
+  const float D = sqrtf(cx * cx + cy * cy + cz * cz);
+  const float cv[3] = {cx / D, cy / D, cz / D};
+  const float sin_a = r[10] / D;
+  for (int face = 0; face < 6; ++face) {
+    int x0, x1, y0, y1;
+    if (!cap_face_box(cv, sin_a, face >> 1, (face & 1) ? -1 : 1, F, x0, x1, y0, y1)) continue;
+    for (int y = y0; y <= y1; ++y)
+      for (int x = x0; x <= x1; ++x) {
+        keys[at] = (uint32_t)((face * F + y) * F + x);
+        vals[at] = (int32_t)i;
+        ++at;
+      }
+  }
+}
+
+__device__ __forceinline__ float field_contribution(const float* g, float ox, float oy, float oz, float dx, float dy,
+                                                    float dz, float dist) {
+  // same arithmetic as field_kernel: peak along the ray, evaluated at min(peak, dist)
+  const float d0 = ox - g[0], d1 = oy - g[1], d2 = oz - g[2];
+  const float qd0 = g[3] * dx + g[4] * dy + g[5] * dz;
+  const float qd1 = g[4] * dx + g[6] * dy + g[7] * dz;
+  const float qd2 = g[5] * dx + g[7] * dy + g[8] * dz;
+  const float den = fmaxf(dx * qd0 + dy * qd1 + dz * qd2, 1e-12f);
+  const float t = -(d0 * qd0 + d1 * qd1 + d2 * qd2) / den;
+  if (!(t > 0.f)) return 0.f;
+  const float te = fminf(t, dist);
+  const float f0 = d0 + te * dx, f1 = d1 + te * dy, f2 = d2 + te * dz;
+  const float e = f0 * (g[3] * f0 + g[4] * f1 + g[5] * f2) + f1 * (g[4] * f0 + g[6] * f1 + g[7] * f2) +
+                  f2 * (g[5] * f0 + g[7] * f1 + g[8] * f2);
+  return fminf(fmaxf(g[9] * expf(-0.5f * fmaxf(e, 0.f)), 0.f), 0.999f);
+}
+
+// Per view, every query's cube-map cell (a query at the origin has no direction and
+// gets field 0 for this view right here) as a sort key with the query's index.
+__global__ void cfield_qcell_kernel(const float* pts, int64_t np, float ox, float oy, float oz, int F,
+                                    uint32_t* qkey, int32_t* qidx, uint32_t* out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= np) return;
+  const float dx = pts[i * 3] - ox, dy = pts[i * 3 + 1] - oy, dz = pts[i * 3 + 2] - oz;
+  const bool at_origin = !(dx * dx + dy * dy + dz * dz > 0.f);
+  qkey[i] = at_origin ? (uint32_t)(6 * F * F) : (uint32_t)cube_cell(dx, dy, dz, F);
+  qidx[i] = (int32_t)i;
+  if (at_origin) atomicMin(out + i, 0u);
+}
+
+constexpr int CF_THREADS = 256;
+
+// One CTA per cube-map cell: the cell's queries (in chunks of CF_THREADS, one per
+// thread) walk the cell's front-to-back candidate list, staged CF_THREADS records at a
+// time in shared memory.  A query stops at the first candidate whose ball starts
+// beyond it or once its transmittance is below 1e-7; the CTA stops when all have.
+// number of CF_THREADS-query chunks of every cell
+__global__ void cfield_chunks_kernel(const int2* qranges, int ncells, int32_t* chunks) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= ncells) return;
+  const int2 r = qranges[c];
+  chunks[c] = (r.y - r.x + CF_THREADS - 1) / CF_THREADS;
+}
+
+// One CTA per (cell, chunk of CF_THREADS queries): work item w belongs to the cell c
+// with chunk_off[c] <= w < chunk_off[c + 1] (binary search), so a cell holding many
+// queries (a plane seen edge-on) spreads over many SMs.
+__global__ void __launch_bounds__(CF_THREADS) cfield_cell_kernel(
+    const float* pts, const int32_t* qidx, const int2* qranges, const int64_t* chunk_off, int ncells, float ox,
+    float oy, float oz, const float* rec, const float* near, const int32_t* cell_ids, const int2* cell_ranges,
+    const int32_t* global_ids, int64_t n_global, uint32_t* out) {
+  __shared__ float4 s_g[CF_THREADS * 3];
+  __shared__ float4 s_c[CF_THREADS];  // mean - origin, |mean - origin|^2
+  __shared__ float s_near[CF_THREADS];
+  const int64_t w = blockIdx.x;
+  if (w >= chunk_off[ncells]) return;
+  int lo = 0, hi = ncells - 1;  // largest c with chunk_off[c] <= w
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (chunk_off[mid] <= w) lo = mid; else hi = mid - 1;
+  }
+  const int cell = lo;
+  const int2 qr = qranges[cell];
+  const int2 cr = cell_ranges[cell];
+  const int tid = threadIdx.x;
+  {
+    const int q0 = qr.x + (int)(w - chunk_off[cell]) * CF_THREADS;
+    const int qi = q0 + tid < qr.y ? qidx[q0 + tid] : -1;
+    float dx = 0.f, dy = 0.f, dz = 0.f, dist = 0.f, T = 1.f;
+    bool stop = qi < 0;
+    if (!stop) {
+      dx = pts[(int64_t)qi * 3] - ox; dy = pts[(int64_t)qi * 3 + 1] - oy; dz = pts[(int64_t)qi * 3 + 2] - oz;
+      dist = sqrtf(dx * dx + dy * dy + dz * dz);
+      const float inv = 1.f / fmaxf(dist, 1e-12f);
+      dx *= inv; dy *= inv; dz *= inv;
+      for (int64_t k = 0; k < n_global && T >= 1e-7f; ++k) {
+        const float4* g4 = reinterpret_cast<const float4*>(rec + (int64_t)global_ids[k] * CF_REC);
+        const float4 a = g4[0], b = g4[1], c = g4[2];
+        const float g[10] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y};
+        T *= 1.f - field_contribution(g, ox, oy, oz, dx, dy, dz, dist);
+      }
+      stop = T < 1e-7f;
+    }
+    for (int c0 = cr.x; c0 < cr.y; c0 += CF_THREADS) {
+      if (__syncthreads_count(stop) == CF_THREADS) break;
+      const int nc = min(CF_THREADS, cr.y - c0);
+      if (tid < nc) {
+        const int id = cell_ids[c0 + tid];
+        const float4* g4 = reinterpret_cast<const float4*>(rec + (int64_t)id * CF_REC);
+        const float4 a = g4[0];
+        s_g[tid * 3] = a;
+        s_g[tid * 3 + 1] = g4[1];
+        s_g[tid * 3 + 2] = g4[2];
+        s_near[tid] = near[id];
+        const float cx = a.x - ox, cy = a.y - oy, cz = a.z - oz;
+        s_c[tid] = make_float4(cx, cy, cz, cx * cx + cy * cy + cz * cz);
+      }
+      __syncthreads();
+      if (!stop) {
+        for (int k = 0; k < nc; ++k) {
+          // sorted front to back: this and every later ball start beyond the query
+          if (s_near[k] > dist) { stop = true; break; }
+          const float* g = reinterpret_cast<const float*>(&s_g[k * 3]);
+          // the ray misses the ball (squared distance of the mean from the ray's line
+          // above R^2, with a margin for the rounding of the difference): skip
+          const float4 c = s_c[k];
+          const float cd = c.x * dx + c.y * dy + c.z * dz;
+          const float R = g[10];
+          if (c.w - cd * cd > R * R * 1.002f + 1e-6f * c.w) continue;
+          T *= 1.f - field_contribution(g, ox, oy, oz, dx, dy, dz, dist);
+          if (T < 1e-7f) { stop = true; break; }
+        }
+      }
+    }
+    if (qi >= 0) atomicMin(out + qi, __float_as_uint(fmaxf(1.f - T, 0.f)));
+  }
+}
+
 }  // namespace
 
 size_t field_workspace_bytes(int64_t n) { return (size_t)n * OF_FLOATS * sizeof(float) + 256; }
@@ -106,6 +393,159 @@ cudaError_t launch_opacity_field(const float* pts, int64_t np, const float* mean
   count_launches(1);
   field_kernel<<<grid, OF_THREADS, 0, s>>>(pts, np, g, ng, origins, o);
   return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ culled launcher
+namespace {
+size_t aup(size_t v) { return (v + 255) & ~(size_t)255; }
+int cube_bits(int F) {
+  const int64_t cells = 6LL * F * F;
+  int bits = 1;
+  while ((1LL << bits) < cells) ++bits;
+  return bits;
+}
+}  // namespace
+
+size_t field_culled_workspace_bytes(int64_t ng, int64_t max_pairs, int F) {
+  size_t b = 0;
+  b += aup((size_t)ng * CF_REC * sizeof(float));
+  b += 2 * aup((size_t)ng * sizeof(int32_t));          // count, global flag
+  b += 2 * aup((size_t)(ng + 1) * sizeof(int64_t));    // offsets, global offsets
+  b += aup(scan_workspace_bytes(ng));
+  b += aup((size_t)ng * sizeof(int32_t));              // global ids
+  b += aup((size_t)ng * sizeof(uint32_t));             // depth keys
+  b += aup((size_t)ng * sizeof(float));                // near distances
+  b += aup((size_t)ng * sizeof(int32_t));              // depth order
+  b += aup(bin_workspace_bytes(ng, 0, 0));             // depth sort scratch
+  b += 2 * aup((size_t)max_pairs * sizeof(uint32_t));  // keys, ids
+  b += aup(sort_pairs_workspace_bytes(max_pairs));
+  b += aup((size_t)6 * F * F * 2 * sizeof(int32_t));   // cell ranges
+  return b;
+}
+
+// per-query buffers of the culled field (sorted by cell each view)
+size_t field_culled_query_bytes(int64_t np, int F) {
+  const int64_t cells = 6LL * F * F + 1;
+  return 2 * aup((size_t)np * sizeof(uint32_t)) + aup(sort_pairs_workspace_bytes(np)) +
+         aup((size_t)cells * 2 * sizeof(int32_t)) + aup((size_t)cells * sizeof(int32_t)) +
+         aup((size_t)(cells + 1) * sizeof(int64_t)) + aup(scan_workspace_bytes(cells));
+}
+
+cudaError_t launch_opacity_field_culled(const float* pts, int64_t np, const float* means, const float* invcov,
+                                        const float* op, int64_t ng, const float* origins, int nc, float cutoff,
+                                        int F, float* out, void* ws, size_t ws_bytes, int64_t max_pairs,
+                                        int64_t* pairs_needed, cudaStream_t s) {
+  if (ws_bytes < field_culled_workspace_bytes(ng, max_pairs, F) + field_culled_query_bytes(np, F))
+    return cudaErrorInvalidValue;
+  uint32_t* o = reinterpret_cast<uint32_t*>(out);
+  if (np == 0) return cudaSuccess;
+  count_launches(1);
+  field_init_kernel<<<(unsigned)((np + 255) / 256), 256, 0, s>>>(o, np);
+  if (ng == 0 || nc == 0) return cudaGetLastError();
+  char* p = reinterpret_cast<char*>(ws);
+  auto take = [&](size_t bytes) { char* r = p; p += aup(bytes); return r; };
+  float* rec = reinterpret_cast<float*>(take((size_t)ng * CF_REC * sizeof(float)));
+  int32_t* count = reinterpret_cast<int32_t*>(take((size_t)ng * sizeof(int32_t)));
+  int32_t* gflag = reinterpret_cast<int32_t*>(take((size_t)ng * sizeof(int32_t)));
+  int64_t* offs = reinterpret_cast<int64_t*>(take((size_t)(ng + 1) * sizeof(int64_t)));
+  int64_t* goffs = reinterpret_cast<int64_t*>(take((size_t)(ng + 1) * sizeof(int64_t)));
+  const size_t scan_bytes = scan_workspace_bytes(ng);
+  void* scan_ws = take(scan_bytes);
+  int32_t* gids = reinterpret_cast<int32_t*>(take((size_t)ng * sizeof(int32_t)));
+  uint32_t* dkey = reinterpret_cast<uint32_t*>(take((size_t)ng * sizeof(uint32_t)));
+  float* near = reinterpret_cast<float*>(take((size_t)ng * sizeof(float)));
+  int32_t* order = reinterpret_cast<int32_t*>(take((size_t)ng * sizeof(int32_t)));
+  const size_t order_ws_bytes = bin_workspace_bytes(ng, 0, 0);
+  void* order_ws = take(order_ws_bytes);
+  uint32_t* keys = reinterpret_cast<uint32_t*>(take((size_t)max_pairs * sizeof(uint32_t)));
+  int32_t* vals = reinterpret_cast<int32_t*>(take((size_t)max_pairs * sizeof(int32_t)));
+  const size_t sort_bytes = sort_pairs_workspace_bytes(max_pairs);
+  void* sort_ws = take(sort_bytes);
+  int32_t* ranges = reinterpret_cast<int32_t*>(take((size_t)6 * F * F * 2 * sizeof(int32_t)));
+  uint32_t* qkey = reinterpret_cast<uint32_t*>(take((size_t)np * sizeof(uint32_t)));
+  int32_t* qidx = reinterpret_cast<int32_t*>(take((size_t)np * sizeof(int32_t)));
+  const size_t qsort_bytes = sort_pairs_workspace_bytes(np);
+  void* qsort_ws = take(qsort_bytes);
+  int32_t* qranges = reinterpret_cast<int32_t*>(take((size_t)(6 * F * F + 1) * 2 * sizeof(int32_t)));
+  const int ncells = 6 * F * F;
+  int32_t* chunks = reinterpret_cast<int32_t*>(take((size_t)(ncells + 1) * sizeof(int32_t)));
+  int64_t* chunk_off = reinterpret_cast<int64_t*>(take((size_t)(ncells + 2) * sizeof(int64_t)));
+  const size_t cscan_bytes = scan_workspace_bytes(ncells + 1);
+  void* cscan_ws = take(cscan_bytes);
+  int qbits = 1;
+  while ((1LL << qbits) < 6LL * F * F + 1) ++qbits;
+
+  const unsigned gb = (unsigned)((ng + 255) / 256), qb = (unsigned)((np + 255) / 256);
+  count_launches(1);
+  cfield_prep_kernel<<<gb, 256, 0, s>>>(means, invcov, op, ng, cutoff, rec);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  float* host_origins = new float[(size_t)nc * 3];
+  e = cudaMemcpyAsync(host_origins, origins, (size_t)nc * 3 * sizeof(float), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  int64_t most = 0;
+  // first pass: the largest per-view candidate count, so that an undersized workspace
+  // is reported before any view is evaluated
+  for (int v = 0; v < nc && e == cudaSuccess; ++v) {
+    const float ox = host_origins[v * 3], oy = host_origins[v * 3 + 1], oz = host_origins[v * 3 + 2];
+    count_launches(1);
+    cfield_count_kernel<<<gb, 256, 0, s>>>(rec, ng, ox, oy, oz, F, count, gflag, dkey, near);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = scan_counts(count, ng, offs, scan_ws, scan_bytes, s);
+    int64_t total = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&total, offs + ng, sizeof(int64_t), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (total > most) most = total;
+  }
+  if (e != cudaSuccess || most > max_pairs) {
+    delete[] host_origins;
+    if (pairs_needed) *pairs_needed = most;
+    return e;
+  }
+  for (int v = 0; v < nc && e == cudaSuccess; ++v) {
+    const float ox = host_origins[v * 3], oy = host_origins[v * 3 + 1], oz = host_origins[v * 3 + 2];
+    count_launches(1);
+    cfield_count_kernel<<<gb, 256, 0, s>>>(rec, ng, ox, oy, oz, F, count, gflag, dkey, near);
+    e = cudaGetLastError();
+    // stable order by nearest ball distance, and the counts' exclusive scan in that order
+    if (e == cudaSuccess) e = bin_order(count, dkey, ng, order, offs, order_ws, order_ws_bytes, s);
+    if (e == cudaSuccess) e = scan_counts(gflag, ng, goffs, scan_ws, scan_bytes, s);
+    int64_t totals[2] = {0, 0};
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&totals[0], offs + ng, sizeof(int64_t), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&totals[1], goffs + ng, sizeof(int64_t), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) break;
+    const int64_t m = totals[0], n_global = totals[1];
+    if (m > max_pairs) break;  // cannot happen after the first pass
+    count_launches(1);
+    cfield_emit_kernel<<<gb, 256, 0, s>>>(rec, ng, ox, oy, oz, F, order, offs, goffs, keys, vals, gids);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = sort_pairs(keys, vals, m, cube_bits(F), sort_ws, sort_bytes, s);
+    if (e == cudaSuccess) e = key_ranges(keys, m, 6LL * F * F, ranges, s);
+    if (e != cudaSuccess) break;
+    count_launches(1);
+    cfield_qcell_kernel<<<qb, 256, 0, s>>>(pts, np, ox, oy, oz, F, qkey, qidx, o);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = sort_pairs(qkey, qidx, np, qbits, qsort_ws, qsort_bytes, s);
+    if (e == cudaSuccess) e = key_ranges(qkey, np, 6LL * F * F + 1, qranges, s);
+    if (e != cudaSuccess) break;
+    count_launches(1);
+    cfield_chunks_kernel<<<(unsigned)((ncells + 255) / 256), 256, 0, s>>>(reinterpret_cast<const int2*>(qranges),
+                                                                           ncells, chunks);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = scan_counts(chunks, ncells, chunk_off, cscan_ws, cscan_bytes, s);
+    if (e != cudaSuccess) break;
+    // at most one partial chunk per cell beyond the full ones
+    const int64_t max_items = (np + CF_THREADS - 1) / CF_THREADS + ncells;
+    count_launches(1);
+    cfield_cell_kernel<<<(unsigned)max_items, CF_THREADS, 0, s>>>(
+        pts, qidx, reinterpret_cast<const int2*>(qranges), chunk_off, ncells, ox, oy, oz, rec, near, vals,
+        reinterpret_cast<const int2*>(ranges), gids, n_global, o);
+    e = cudaGetLastError();
+  }
+  delete[] host_origins;
+  if (pairs_needed) *pairs_needed = most;
+  return e;
 }
 
 }  // namespace sf

@@ -93,6 +93,15 @@ cudaError_t launch_composite_backward(const float* al, const float* col, const f
                                       const float* g_median, const float* g_w, float* da, float* dc, float* dd,
                                       float* dn, cudaStream_t s);
 
+// gaussian.opacity_field@1, culled per view (cube-map candidate lists; contributions
+// below `cutoff` dropped).  Synchronises the stream once per view; pairs_needed (host)
+// receives the largest per-view candidate-pair count (views above max_pairs are skipped)
+size_t field_culled_workspace_bytes(int64_t ng, int64_t max_pairs, int F);
+size_t field_culled_query_bytes(int64_t np, int F);
+cudaError_t launch_opacity_field_culled(const float* pts, int64_t np, const float* means, const float* invcov,
+                                        const float* op, int64_t ng, const float* origins, int nc, float cutoff,
+                                        int F, float* out, void* ws, size_t ws_bytes, int64_t max_pairs,
+                                        int64_t* pairs_needed, cudaStream_t s);
 // gaussian.opacity_field@1
 size_t field_workspace_bytes(int64_t n);
 cudaError_t launch_opacity_field(const float* pts, int64_t np, const float* means, const float* invcov,
@@ -112,6 +121,12 @@ cudaError_t bin_emit(const int32_t* order, const int64_t* offsets, const int32_t
                      int32_t* ranges, void* ws, size_t ws_bytes, cudaStream_t s);
 cudaError_t bin_keys(const int32_t* ids, const int32_t* ranges, const uint32_t* depth_key,
                      int n_tiles, int64_t n_isect, uint64_t* keys, cudaStream_t s);
+// stable sort of n (key, value) pairs by key bits [0, bits), in place (keys, vals)
+size_t sort_pairs_workspace_bytes(int64_t n);
+cudaError_t sort_pairs(uint32_t* keys, int32_t* vals, int64_t n, int bits, void* ws, size_t ws_bytes,
+                       cudaStream_t s);
+// [begin, end) of every key value in sorted keys; ranges is int2[n_keys], zero for absent keys
+cudaError_t key_ranges(const uint32_t* keys, int64_t n, int64_t n_keys, int32_t* ranges, cudaStream_t s);
 // exclusive scan int32 -> int64 of n values; out has n+1 entries (out[n] = total)
 cudaError_t scan_counts(const int32_t* in, int64_t n, int64_t* out, void* ws, size_t ws_bytes,
                         cudaStream_t s);

@@ -142,6 +142,18 @@ def alpha_composite_selected(alphas, colors, depths, normals, *, distortions):
 
 
 # ---------------------------------------------------------------- gaussian.opacity_field@1
+# Above this many (point, Gaussian, origin) evaluations the runner switches from the
+# brute-force kernel to the per-view culled one (the GOF exporter's grids).
+CULL_EVALUATIONS = 1 << 33
+# contributions at or below this are dropped by the culled kernel
+FIELD_CUTOFF = 1e-7
+FIELD_FACE_CELLS = 128
+# per-view candidate pairs above this make the runner coarsen the cube map instead
+FIELD_PAIR_LIMIT = 1 << 28
+_FIELD_WS = {}   # device index -> workspace tensor
+_FIELD_CFG = {}  # (device, N, P, requested face_cells) -> (face_cells, max_pairs) that fit
+
+
 def opacity_field(points, means, inverse_covariances, opacities, origins, *, gaussian_chunk=1024):
     """Forward only (the manifest declares ``backward: false``).  ``gaussian_chunk``
     only affects the reference's memory use; the field does not depend on it."""
@@ -149,6 +161,9 @@ def opacity_field(points, means, inverse_covariances, opacities, origins, *, gau
     del gaussian_chunk
     if origins.shape[0] < 1:
         raise ValueError("opacity field requires at least one origin")
+    evaluations = points.shape[0] * means.shape[0] * origins.shape[0]
+    if evaluations > CULL_EVALUATIONS:
+        return opacity_field_culled(points, means, inverse_covariances, opacities, origins)
     with torch.cuda.device(dev), torch.no_grad():
         p, m, q, o, org = (t.contiguous() for t in (points, means, inverse_covariances, opacities, origins))
         out = torch.empty((p.shape[0],), device=dev, dtype=torch.float32)
@@ -158,3 +173,45 @@ def opacity_field(points, means, inverse_covariances, opacities, origins, *, gau
         call("sf_b200_opacity_field", _ptr(p), p.shape[0], _ptr(m), _ptr(q), _ptr(o), m.shape[0], _ptr(org),
              org.shape[0], _ptr(out), _ptr(ws), size.value, _stream(dev))
     return out
+
+
+def opacity_field_culled(points, means, inverse_covariances, opacities, origins, *, cutoff=FIELD_CUTOFF,
+                         face_cells=None):
+    """The opacity field through per-view cube-map candidate lists: contributions at or
+    below ``cutoff`` are dropped, everything else is evaluated as in the brute-force
+    kernel.  The cube-map resolution (``face_cells``, default FIELD_FACE_CELLS, lowered
+    when a view's candidate lists would exceed FIELD_PAIR_LIMIT) and the list capacity
+    are remembered per problem shape, and the workspace is kept per device."""
+    dev = _require_cuda_f32("gaussian.opacity_field@1", points, means, inverse_covariances, opacities, origins)
+    if origins.shape[0] < 1:
+        raise ValueError("opacity field requires at least one origin")
+    with torch.cuda.device(dev), torch.no_grad():
+        p, m, q, o, org = (t.contiguous() for t in (points, means, inverse_covariances, opacities, origins))
+        n, npts = m.shape[0], p.shape[0]
+        out = torch.empty((npts,), device=dev, dtype=torch.float32)
+        shape = (dev.index, n, npts, face_cells)
+        cells, pairs = _FIELD_CFG.get(shape, (face_cells or FIELD_FACE_CELLS, 64 * max(n, 1)))
+        needed = ctypes.c_int64()
+        for _ in range(8):
+            size = ctypes.c_size_t()
+            call("sf_b200_opacity_field_culled_workspace_bytes", npts, n, pairs, cells, ctypes.byref(size))
+            ws = _FIELD_WS.get(dev.index)
+            if ws is None or ws.numel() < size.value:
+                _FIELD_WS.pop(dev.index, None)
+                ws = torch.empty((size.value,), device=dev, dtype=torch.uint8)
+                _FIELD_WS[dev.index] = ws
+            status = _lib.lib().sf_b200_opacity_field_culled(
+                _ptr(p), npts, _ptr(m), _ptr(q), _ptr(o), n, _ptr(org), org.shape[0], ctypes.c_float(cutoff),
+                cells, _ptr(out), _ptr(ws), ws.numel(), pairs, ctypes.byref(needed), _stream(dev))
+            if status == _lib.SF_OK:
+                _FIELD_CFG[shape] = (cells, pairs)
+                return out
+            if status != _lib.SF_ERR_CAPACITY or needed.value <= pairs:
+                raise _lib.NativeError(_lib.lib().sf_b200_last_error().decode())
+            if needed.value > FIELD_PAIR_LIMIT and cells > 8 and face_cells is None:
+                # fewer, larger cells: pairs scale with the square of the face resolution
+                cells = max(8, int(cells * 0.97 * (FIELD_PAIR_LIMIT / needed.value) ** 0.5))
+                pairs = FIELD_PAIR_LIMIT
+            else:
+                pairs = int(needed.value * 1.1) + 1024
+        raise _lib.NativeError("opacity_field_culled: candidate lists did not fit after resizing")

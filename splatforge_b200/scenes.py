@@ -238,6 +238,43 @@ def orbit_cameras(count, width, height, fov_deg, *, radius=3.0, seed=0, radius_r
 
 # --- named workloads --------------------------------------------------------
 
+def rotations(quats: torch.Tensor) -> torch.Tensor:
+    """[N,4] wxyz (normalised here) -> [N,3,3] rotation matrices."""
+    q = quats / quats.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+    w, x, y, z = q.unbind(-1)
+    return torch.stack(
+        (
+            1 - 2 * (y * y + z * z), 2 * (x * y - w * z), 2 * (x * z + w * y),
+            2 * (x * y + w * z), 1 - 2 * (x * x + z * z), 2 * (y * z - w * x),
+            2 * (x * z - w * y), 2 * (y * z + w * x), 1 - 2 * (x * x + y * y),
+        ),
+        -1,
+    ).reshape(-1, 3, 3)
+
+
+def inverse_covariances(params: SceneParams) -> torch.Tensor:
+    """[N,3,3] inverse covariances R diag(1/s^2) R^T of the activated scales."""
+    R = rotations(params.quats)
+    inv_s2 = torch.exp(-2.0 * params.log_scales)
+    return (R * inv_s2[:, None, :]) @ R.transpose(-1, -2)
+
+
+def field_queries(params: SceneParams, n_uniform: int, *, extent: float = 3.0, seed: int = 0) -> torch.Tensor:
+    """Query points of a GOF extraction grid: every Gaussian's centre and the 8 corners
+    of its extent-sigma box along its own axes (the shape of the exporter's
+    gaussian_grid, src/splatforge/studio/exporters.py:20-38, without deduplication),
+    plus ``n_uniform`` points uniform in the bounding box of the means."""
+    R = rotations(params.quats)
+    s = torch.exp(params.log_scales)
+    signs = torch.tensor([[0.0, 0.0, 0.0]] + [[a, b, c] for a in (-1.0, 1.0) for b in (-1.0, 1.0) for c in (-1.0, 1.0)])
+    local = signs[None] * s[:, None, :] * extent                      # [N, 9, 3]
+    pts = params.means[:, None, :] + torch.einsum("nij,nkj->nki", R, local)
+    g = torch.Generator().manual_seed(seed + 2718)
+    lo, hi = params.means.min(0).values, params.means.max(0).values
+    uni = lo + (hi - lo) * torch.rand(n_uniform, 3, generator=g)
+    return torch.cat((pts.reshape(-1, 3), uni), 0).contiguous()
+
+
 def workload(name: str, seed: int = 0):
     """Returns ``(SceneParams, [PinholeCamera])`` for a named workload."""
     if name == "demo48":
@@ -250,4 +287,7 @@ def workload(name: str, seed: int = 0):
         return surfaces(3_000_000, seed), orbit_cameras(
             64, 1600, 1064, 60.0, seed=seed, radius_range=(2.5, 4.0)
         )
+    if name == "field2m_views32":
+        # the GOF opacity-field workload: 2M Gaussians, 32 training-view origins
+        return surfaces(2_000_000, seed), orbit_cameras(32, 1280, 720, 60.0, radius=3.0, seed=seed)
     raise ValueError(f"unknown workload {name}")

@@ -114,3 +114,61 @@ def test_opacity_field_larger_against_oracle():
     want = oracle_ops.opacity_field(pts, m, Q, op, origins)
     got = ops.opacity_field(*(t.to(DEV) for t in (pts, m, Q, op, origins)))
     np.testing.assert_allclose(got.cpu().numpy(), want.numpy(), atol=2e-5)
+
+
+def _field_case(n, n_uniform, n_views, seed=0):
+    from splatforge_b200 import scenes
+
+    params = scenes.surfaces(n, seed)
+    v = scenes.activated(params)
+    Q = scenes.inverse_covariances(params)
+    pts = scenes.field_queries(params, n_uniform, seed=seed)
+    cams = scenes.orbit_cameras(n_views, 64, 64, 60.0, radius=3.0, seed=seed)
+    origins = torch.stack([c.origin for c in cams])
+    return pts, v.means.contiguous(), Q.contiguous(), v.opacities.contiguous(), origins
+
+
+def _brute(*args):
+    saved = ops.CULL_EVALUATIONS
+    ops.CULL_EVALUATIONS = 1 << 62
+    try:
+        return ops.opacity_field(*args)
+    finally:
+        ops.CULL_EVALUATIONS = saved
+
+
+def test_opacity_field_culled_matches_brute_force():
+    """The culled field (per-view cube-map candidate lists, contributions <= 1e-7
+    dropped) against the brute-force kernel on an exporter-shaped query set:
+    9 points per Gaussian of a 20k surface scene plus 20k uniform points, 6 views."""
+    args = [t.to(DEV) for t in _field_case(20_000, 20_000, 6)]
+    full = _brute(*args)
+    cull = ops.opacity_field_culled(*args)
+    assert torch.isfinite(cull).all()
+    assert (full - cull).abs().max().item() < 1e-5
+    assert full.max().item() > 0.5  # the grid does reach dense regions
+    # above the evaluation threshold the runner takes the culled path by itself
+    assert args[0].shape[0] * args[1].shape[0] * args[4].shape[0] > ops.CULL_EVALUATIONS
+    np.testing.assert_array_equal(ops.opacity_field(*args).cpu().numpy(), cull.cpu().numpy())
+
+
+def test_opacity_field_culled_edge_cases_against_oracle():
+    """An origin inside a Gaussian's bounding ball (its global list), a query at an
+    origin (no direction: zero field for that view), a Gaussian below the cutoff, and
+    a wide face_cells range, against the oracle."""
+    pts, m, Q, o, org = _field_case(300, 400, 3, seed=4)
+    org = torch.cat((org, m[7:8] + 1e-3), 0)                # origin inside Gaussian 7
+    pts = torch.cat((pts, org[1:2], m[7:8] + 2e-3), 0)        # a query at origin 1
+    o = o.clone()
+    o[11] = 5e-8                                               # below the cutoff
+    want = oracle_ops.opacity_field(pts, m, Q, o, org)
+    for cells in (1, 16, 128):
+        got = ops.opacity_field_culled(*(t.to(DEV) for t in (pts, m, Q, o, org)), face_cells=cells)
+        np.testing.assert_allclose(got.cpu().numpy(), want.numpy(), atol=2e-5, err_msg=f"face_cells={cells}")
+    assert want[-2].item() == 0.0
+
+
+def test_opacity_field_culled_reference_fixture(golden):
+    f = golden("ops")
+    out = ops.opacity_field_culled(*(T(f[f"field/{k}"]) for k in ("p", "m", "Q", "o", "origins")))
+    np.testing.assert_allclose(out.cpu().numpy(), f["field/out"], atol=1e-5)
