@@ -322,7 +322,7 @@ def run_field(args):
     n_q = hi - lo
 
     def step():
-        return ops.opacity_field(d["pts"], d["means"], d["Q"], d["opac"], d["origins"])
+        return ops.opacity_field_culled(d["pts"], d["means"], d["Q"], d["opac"], d["origins"])
 
     launches0 = None
     for _ in range(args.warmup):

@@ -20,6 +20,8 @@
  *     splat.alpha_composite@3  src/splatforge/providers/torch/gaussian/composite_cuda.cu:26-98
  *   backward (autograd)        same functions, reverse mode
  *   gaussian.opacity_field@1   src/splatforge/providers/torch/gaussian/reference.py:194-222
+ *   camera.pixel_rays@1, gaussian.ray_peak@1, geometry.depth_normals@1
+ *                              src/splatforge/providers/torch/gaussian/reference.py:38-83
  */
 #ifndef SPLATFORGE_B200_H
 #define SPLATFORGE_B200_H
@@ -232,6 +234,23 @@ int sf_b200_opacity_field_culled(const float* points, int64_t n_points, const fl
                                  float cutoff, int32_t face_cells, float* field, void* workspace,
                                  size_t workspace_bytes, int64_t max_pairs, int64_t* pairs_needed,
                                  void* stream);
+
+/* ---- small geometry operators -------------------------------------------------
+ * camera.pixel_rays@1 (reference.py:49-56): K [3,3] -> rays [height, width, 3].
+ * gaussian.ray_peak@1 (reference.py:38-46): means [N,3], inverse_covariances [N,3,3],
+ *   origins [P,3], directions [P,3] -> t [N,P], response [N,P], normals [N,P,3].
+ * geometry.depth_normals@1 (reference.py:59-83): depth [H,W], K [3,3] -> normals
+ *   [H,W,3], valid [H,W] (uint8 0/1); the backward maps grad_normals to grad_depth
+ *   and needs a workspace of 6*H*W floats. */
+int sf_b200_pixel_rays(const float* K, int32_t width, int32_t height, float* rays, void* stream);
+int sf_b200_ray_peak(const float* means, const float* inverse_covariances, int64_t n_gaussians,
+                     const float* origins, const float* directions, int64_t n_rays, float* t,
+                     float* response, float* normals, void* stream);
+int sf_b200_depth_normals(const float* depth, const float* K, int32_t width, int32_t height,
+                          float* normals, uint8_t* valid, void* stream);
+int sf_b200_depth_normals_backward(const float* depth, const float* K, int32_t width, int32_t height,
+                                   const float* grad_normals, float* grad_depth, float* workspace,
+                                   void* stream);
 
 /* ---- raster forward (batched_renderer.py:169-338 + alpha_composite@3) -----------
  * One CTA per 16x16 tile.  Images are HWC float32: rgb/normals [H,W,3], the rest

@@ -57,6 +57,32 @@ def pixel_rays(K, *, width, height):
     return pix @ torch.linalg.inv(K).T
 
 
+def depth_normals(depth, K):
+    """``geometry.depth_normals@1`` (reference.py:59-83): back-project z-depth, face
+    normals from centred differences, oriented towards the camera; borders and
+    pixels with a non-positive neighbour are invalid (zero normal)."""
+    height, width = depth.shape
+    points = pixel_rays(K, width=width, height=height) * depth.unsqueeze(-1)
+    normals = torch.zeros_like(points)
+    valid = torch.zeros_like(depth, dtype=torch.bool)
+    if height < 3 or width < 3:
+        return normals, valid
+    dx = points[1:-1, 2:] - points[1:-1, :-2]
+    dy = points[2:, 1:-1] - points[:-2, 1:-1]
+    n = _unit(torch.linalg.cross(dy, dx))
+    facing = (n * points[1:-1, 1:-1]).sum(-1, keepdim=True)
+    n = torch.where(facing > 0, -n, n)
+    good = (
+        (depth[1:-1, 1:-1] > 0) & (depth[1:-1, 2:] > 0) & (depth[1:-1, :-2] > 0)
+        & (depth[2:, 1:-1] > 0) & (depth[:-2, 1:-1] > 0)
+        & torch.isfinite(n).all(-1) & (n.square().sum(-1) > 0)
+    )
+    inner = torch.where(good.unsqueeze(-1), n, 0)
+    normals = torch.nn.functional.pad(inner.permute(2, 0, 1), (1, 1, 1, 1)).permute(1, 2, 0)
+    valid = torch.nn.functional.pad(good, (1, 1, 1, 1))
+    return normals, valid
+
+
 # Real SH basis constants of the gsplat/3DGS convention (reference.py:85-109).
 _C0 = 1 / math.sqrt(4 * math.pi)
 _C1 = math.sqrt(3 / (4 * math.pi))

@@ -99,6 +99,10 @@ _SIGNATURES = {
         ctypes.c_int,
         [P, c_int64, P, P, P, c_int64, P, c_int32, c_float, c_int32, P, P, c_size_t, c_int64, POINTER(c_int64), P],
     ),
+    "sf_b200_pixel_rays": (ctypes.c_int, [P, c_int32, c_int32, P, P]),
+    "sf_b200_ray_peak": (ctypes.c_int, [P, P, c_int64, P, P, c_int64, P, P, P, P]),
+    "sf_b200_depth_normals": (ctypes.c_int, [P, P, c_int32, c_int32, P, P, P]),
+    "sf_b200_depth_normals_backward": (ctypes.c_int, [P, P, c_int32, c_int32, P, P, P, P]),
     "sf_b200_raster_forward": (
         ctypes.c_int,
         [P, c_int64, P, P, POINTER(Camera), POINTER(Settings)]

@@ -363,6 +363,43 @@ int sf_b200_opacity_field_culled(const float* points, int64_t n_points, const fl
   return SF_OK;
 }
 
+int sf_b200_pixel_rays(const float* K, int32_t width, int32_t height, float* rays, void* stream) {
+  if (width <= 0 || height <= 0) return fail(SF_ERR_ARGUMENT, "pixel_rays: width and height must be positive");
+  if (!K || !rays) return fail(SF_ERR_ARGUMENT, "pixel_rays: NULL buffer");
+  return cuda_status(sf::launch_pixel_rays(K, width, height, rays, as_stream(stream)), "pixel_rays");
+}
+
+int sf_b200_ray_peak(const float* means, const float* inverse_covariances, int64_t n_gaussians, const float* origins,
+                     const float* directions, int64_t n_rays, float* t, float* response, float* normals,
+                     void* stream) {
+  if (n_gaussians < 0 || n_rays < 0) return fail(SF_ERR_ARGUMENT, "ray_peak: negative size");
+  if (n_gaussians * n_rays > 0 && (!means || !inverse_covariances || !origins || !directions || !t || !response ||
+                                   !normals))
+    return fail(SF_ERR_ARGUMENT, "ray_peak: NULL buffer");
+  return cuda_status(sf::launch_ray_peak(means, inverse_covariances, n_gaussians, origins, directions, n_rays, t,
+                                         response, normals, as_stream(stream)),
+                     "ray_peak");
+}
+
+int sf_b200_depth_normals(const float* depth, const float* K, int32_t width, int32_t height, float* normals,
+                          uint8_t* valid, void* stream) {
+  if (width < 0 || height < 0) return fail(SF_ERR_ARGUMENT, "depth_normals: negative size");
+  if ((int64_t)width * height > 0 && (!depth || !K || !normals || !valid))
+    return fail(SF_ERR_ARGUMENT, "depth_normals: NULL buffer");
+  return cuda_status(sf::launch_depth_normals(depth, K, width, height, normals, valid, as_stream(stream)),
+                     "depth_normals");
+}
+
+int sf_b200_depth_normals_backward(const float* depth, const float* K, int32_t width, int32_t height,
+                                   const float* grad_normals, float* grad_depth, float* workspace, void* stream) {
+  if (width < 0 || height < 0) return fail(SF_ERR_ARGUMENT, "depth_normals_backward: negative size");
+  if ((int64_t)width * height > 0 && (!depth || !K || !grad_normals || !grad_depth || !workspace))
+    return fail(SF_ERR_ARGUMENT, "depth_normals_backward: NULL buffer");
+  return cuda_status(sf::launch_depth_normals_backward(depth, K, width, height, grad_normals, grad_depth, workspace,
+                                                       as_stream(stream)),
+                     "depth_normals_backward");
+}
+
 int sf_b200_composite_workspace_bytes(int64_t B, int64_t N, int64_t P, int32_t distortions, size_t* bytes) {
   if (B < 0 || N < 0 || P < 0 || !bytes) return fail(SF_ERR_ARGUMENT, "composite_workspace_bytes: bad arguments");
   const size_t aux = (distortions & SF_DIST_L1) ? (size_t)2 * B * N * P * sizeof(float) : 0;

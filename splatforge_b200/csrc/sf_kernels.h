@@ -93,6 +93,15 @@ cudaError_t launch_composite_backward(const float* al, const float* col, const f
                                       const float* g_median, const float* g_w, float* da, float* dc, float* dd,
                                       float* dn, cudaStream_t s);
 
+// camera.pixel_rays@1, gaussian.ray_peak@1, geometry.depth_normals@1
+cudaError_t launch_pixel_rays(const float* K, int W, int H, float* out, cudaStream_t s);
+cudaError_t launch_ray_peak(const float* means, const float* Q, int64_t N, const float* origins, const float* dirs,
+                            int64_t P, float* t, float* r, float* n, cudaStream_t s);
+cudaError_t launch_depth_normals(const float* depth, const float* K, int W, int H, float* normals, uint8_t* valid,
+                                 cudaStream_t s);
+// ws: 6 * W * H floats
+cudaError_t launch_depth_normals_backward(const float* depth, const float* K, int W, int H, const float* g_normals,
+                                          float* g_depth, float* ws, cudaStream_t s);
 // gaussian.opacity_field@1, culled per view (cube-map candidate lists; contributions
 // below `cutoff` dropped).  Synchronises the stream once per view; pairs_needed (host)
 // receives the largest per-view candidate-pair count (views above max_pairs are skipped)

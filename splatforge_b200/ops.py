@@ -142,9 +142,10 @@ def alpha_composite_selected(alphas, colors, depths, normals, *, distortions):
 
 
 # ---------------------------------------------------------------- gaussian.opacity_field@1
-# Above this many (point, Gaussian, origin) evaluations the runner switches from the
-# brute-force kernel to the per-view culled one (the GOF exporter's grids).
-CULL_EVALUATIONS = 1 << 33
+# Two implementations: ``opacity_field`` evaluates every (point, Gaussian, origin)
+# triple and never synchronises; ``opacity_field_culled`` walks per-view candidate
+# lists (for the exporter's large grids) and synchronises once per origin, which its
+# manifest declares.
 # contributions at or below this are dropped by the culled kernel
 FIELD_CUTOFF = 1e-7
 FIELD_FACE_CELLS = 128
@@ -161,9 +162,6 @@ def opacity_field(points, means, inverse_covariances, opacities, origins, *, gau
     del gaussian_chunk
     if origins.shape[0] < 1:
         raise ValueError("opacity field requires at least one origin")
-    evaluations = points.shape[0] * means.shape[0] * origins.shape[0]
-    if evaluations > CULL_EVALUATIONS:
-        return opacity_field_culled(points, means, inverse_covariances, opacities, origins)
     with torch.cuda.device(dev), torch.no_grad():
         p, m, q, o, org = (t.contiguous() for t in (points, means, inverse_covariances, opacities, origins))
         out = torch.empty((p.shape[0],), device=dev, dtype=torch.float32)
@@ -175,14 +173,15 @@ def opacity_field(points, means, inverse_covariances, opacities, origins, *, gau
     return out
 
 
-def opacity_field_culled(points, means, inverse_covariances, opacities, origins, *, cutoff=FIELD_CUTOFF,
-                         face_cells=None):
+def opacity_field_culled(points, means, inverse_covariances, opacities, origins, *, gaussian_chunk=1024,
+                         cutoff=FIELD_CUTOFF, face_cells=None):
     """The opacity field through per-view cube-map candidate lists: contributions at or
     below ``cutoff`` are dropped, everything else is evaluated as in the brute-force
     kernel.  The cube-map resolution (``face_cells``, default FIELD_FACE_CELLS, lowered
     when a view's candidate lists would exceed FIELD_PAIR_LIMIT) and the list capacity
     are remembered per problem shape, and the workspace is kept per device."""
     dev = _require_cuda_f32("gaussian.opacity_field@1", points, means, inverse_covariances, opacities, origins)
+    del gaussian_chunk
     if origins.shape[0] < 1:
         raise ValueError("opacity field requires at least one origin")
     with torch.cuda.device(dev), torch.no_grad():
@@ -215,3 +214,63 @@ def opacity_field_culled(points, means, inverse_covariances, opacities, origins,
             else:
                 pairs = int(needed.value * 1.1) + 1024
         raise _lib.NativeError("opacity_field_culled: candidate lists did not fit after resizing")
+
+
+# ---------------------------------------------------------------- small geometry ops
+def pixel_rays(K, *, width, height):
+    """``camera.pixel_rays@1``: inv(K) (u + 0.5, v + 0.5, 1) as [height, width, 3]."""
+    dev = _require_cuda_f32("camera.pixel_rays@1", K)
+    if int(width) <= 0 or int(height) <= 0:
+        raise ValueError("pixel_rays: width and height must be positive")
+    with torch.cuda.device(dev), torch.no_grad():
+        out = torch.empty((int(height), int(width), 3), device=dev, dtype=torch.float32)
+        call("sf_b200_pixel_rays", _ptr(K.contiguous()), int(width), int(height), _ptr(out), _stream(dev))
+    return out
+
+
+def ray_peak(means, inverse_covariances, origins, directions):
+    """``gaussian.ray_peak@1``: (t [N,P], response [N,P], normals [N,P,3]); forward only."""
+    dev = _require_cuda_f32("gaussian.ray_peak@1", means, inverse_covariances, origins, directions)
+    with torch.cuda.device(dev), torch.no_grad():
+        m, q, o, d = (t.contiguous() for t in (means, inverse_covariances, origins, directions))
+        N, P = m.shape[0], o.shape[0]
+        t = torch.empty((N, P), device=dev, dtype=torch.float32)
+        r = torch.empty((N, P), device=dev, dtype=torch.float32)
+        nrm = torch.empty((N, P, 3), device=dev, dtype=torch.float32)
+        call("sf_b200_ray_peak", _ptr(m), _ptr(q), N, _ptr(o), _ptr(d), P, _ptr(t), _ptr(r), _ptr(nrm), _stream(dev))
+    return t, r, nrm
+
+
+class _DepthNormals(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, depth, K):
+        dev = depth.device
+        d, k = depth.contiguous(), K.contiguous()
+        H, W = d.shape
+        normals = torch.empty((H, W, 3), device=dev, dtype=torch.float32)
+        valid = torch.empty((H, W), device=dev, dtype=torch.uint8)
+        call("sf_b200_depth_normals", _ptr(d), _ptr(k), W, H, _ptr(normals), _ptr(valid), _stream(dev))
+        ctx.save_for_backward(d, k)
+        ctx.mark_non_differentiable(valid)
+        return normals, valid.bool()
+
+    @staticmethod
+    def backward(ctx, g_normals, g_valid):
+        d, k = ctx.saved_tensors
+        dev = d.device
+        H, W = d.shape
+        if g_normals is None:
+            return None, None
+        gd = torch.empty_like(d)
+        ws = torch.empty((6 * H * W,), device=dev, dtype=torch.float32)
+        call("sf_b200_depth_normals_backward", _ptr(d), _ptr(k), W, H, _ptr(g_normals.contiguous()), _ptr(gd), _ptr(ws),
+             _stream(dev))
+        return gd, None
+
+
+def depth_normals(depth, K):
+    """``geometry.depth_normals@1``: (normals [H,W,3], valid [H,W] bool); differentiable
+    with respect to depth (the normal-consistency losses backpropagate through it)."""
+    dev = _require_cuda_f32("geometry.depth_normals@1", depth, K)
+    with torch.cuda.device(dev):
+        return _DepthNormals.apply(depth, K)

@@ -7,7 +7,10 @@ Operator seam (src/splatforge/gaussian/ops.py:175-254, src/splatforge/core/model
 reference's own CUDA composite provider does (providers/torch/gaussian/cuda_composite.py:90-136).
 Every manifest names provider ``native_cuda`` (the first provider of the default
 ``ExecutionPolicy``), devices ``["cuda"]``, dtype ``float32`` and the sha256 of the installed
-``semantics.json`` as its ``op_spec_revision``.
+``semantics.json`` as its ``op_spec_revision``.  The culled opacity field is registered as a
+second implementation of ``gaussian.opacity_field@1`` that declares host synchronisation
+(one candidate-count read per origin); the default policy (``host_sync="forbid"``) refuses
+it, so it runs only when selected explicitly under a policy that allows it.
 
 Renderer seam (src/splatforge/studio/renderers.py:356-439): ``register_renderer(renderers)``
 adds the ``b200`` backend; the same factory is published as the ``splatforge.renderers``
@@ -39,6 +42,21 @@ _OPS = {
                                 ("composite.cu", "sf_device.cuh")),
     "gaussian.opacity_field@1": ("splatforge_b200.native_cuda.opacity_field.v1", ops.opacity_field,
                                  "sf_b200_opacity_field", "sm100a-float32-forward", False, ("opacity_field.cu",)),
+    "camera.pixel_rays@1": ("splatforge_b200.native_cuda.pixel_rays.v1", ops.pixel_rays, "sf_b200_pixel_rays",
+                            "sm100a-float32-forward", False, ("geometry.cu",)),
+    "gaussian.ray_peak@1": ("splatforge_b200.native_cuda.ray_peak.v1", ops.ray_peak, "sf_b200_ray_peak",
+                            "sm100a-float32-forward", False, ("geometry.cu",)),
+    "geometry.depth_normals@1": ("splatforge_b200.native_cuda.depth_normals.v1", ops.depth_normals,
+                                 "sf_b200_depth_normals", "sm100a-float32", True, ("geometry.cu",)),
+}
+
+# Additional implementations of an operator already listed above, selected explicitly
+# (not by selection()): the culled opacity field synchronises the host once per origin,
+# so only a policy that allows declared host synchronisation may run it.
+_ALTERNATIVES = {
+    "splatforge_b200.native_cuda.opacity_field_culled.v1": (
+        "gaussian.opacity_field@1", ops.opacity_field_culled, "sf_b200_opacity_field_culled",
+        "sm100a-float32-forward-culled", False, ("opacity_field.cu", "binning.cu"), "per_origin"),
 }
 
 
@@ -55,8 +73,18 @@ def build_fingerprint(sources):
     return "sha256:" + h.hexdigest()
 
 
-def manifest_dict(op, revision):
-    identifier, runner, target, variant, backward, sources = _OPS[op]
+def _entry(key):
+    """(op, implementation id, runner, target, variant, backward, sources, host sync) of an
+    operator key (its default implementation) or of an alternative implementation id."""
+    if key in _OPS:
+        identifier, runner, target, variant, backward, sources = _OPS[key]
+        return key, identifier, runner, target, variant, backward, sources, "none"
+    op, runner, target, variant, backward, sources, sync = _ALTERNATIVES[key]
+    return op, key, runner, target, variant, backward, sources, sync
+
+
+def manifest_dict(key, revision):
+    op, identifier, runner, target, variant, backward, sources, sync = _entry(key)
     return {
         "schema_version": 1,
         "implementation_id": identifier,
@@ -75,7 +103,7 @@ def manifest_dict(op, revision):
             "backward": backward,
             "jvp": False,
             "determinism_guarantee": "none",
-            "host_synchronization": "none",
+            "host_synchronization": sync,
             "cuda_graph": False,
             "execution": {"eager": "supported"},
         },
@@ -83,15 +111,23 @@ def manifest_dict(op, revision):
     }
 
 
+def _keys(ops_keys):
+    """Default implementations of the given operators (all by default), followed by the
+    alternatives of those operators."""
+    ops_list = list(ops_keys or _OPS)
+    return ops_list + [alt for alt, entry in _ALTERNATIVES.items() if entry[0] in ops_list]
+
+
 def implementations(ops_keys=None):
-    """Manifests + runners for SplatForge's ``create_surface_runtime``."""
+    """Manifests + runners for SplatForge's ``create_surface_runtime``: every operator's
+    default implementation plus the alternatives (selected only by explicit id)."""
     from splatforge.core.models import ImplementationManifest
 
     revision = spec_revision()
     out = []
-    for op in ops_keys or _OPS:
-        manifest = ImplementationManifest.from_dict(manifest_dict(op, revision))
-        out.append(SimpleNamespace(manifest=manifest, runner=_OPS[op][1], support=None))
+    for key in _keys(ops_keys):
+        manifest = ImplementationManifest.from_dict(manifest_dict(key, revision))
+        out.append(SimpleNamespace(manifest=manifest, runner=_entry(key)[2], support=None))
     return out
 
 
@@ -99,14 +135,19 @@ def capabilities(ops_keys=None):
     from splatforge.core.models import CapabilityRecord
 
     return [
-        CapabilityRecord(_OPS[op][0], "experimental", "splatforge-b200", "b200-sm100a")
-        for op in ops_keys or _OPS
+        CapabilityRecord(_entry(key)[1], "experimental", "splatforge-b200", "b200-sm100a")
+        for key in _keys(ops_keys)
     ]
 
 
-def selection(ops_keys=None):
-    """``{op: implementation_id}`` for ``SurfaceOperators(runtime, implementations=...)``."""
-    return {op: _OPS[op][0] for op in ops_keys or _OPS}
+def selection(ops_keys=None, *, culled_field=False):
+    """``{op: implementation_id}`` for ``SurfaceOperators(runtime, implementations=...)``.
+    ``culled_field`` selects the culled opacity field, which needs an execution policy
+    with ``host_sync="allow_declared"``."""
+    sel = {op: _OPS[op][0] for op in ops_keys or _OPS}
+    if culled_field and "gaussian.opacity_field@1" in sel:
+        sel["gaussian.opacity_field@1"] = "splatforge_b200.native_cuda.opacity_field_culled.v1"
+    return sel
 
 
 def surface_operators(ops_keys=None):

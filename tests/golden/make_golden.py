@@ -14,6 +14,8 @@ Fixtures (all float32 unless noted):
 
 * ``binning.npz``   -- the reference's rng(703) tangency fixture plus larger
                        random cases: bounds in, CSR tile lists out (int64).
+* ``geometry.npz``  -- pixel_rays@1, ray_peak@1, depth_normals@1 (with the depth
+                       adjoint of a seeded loss on the normals).
 * ``ops.npz``       -- covariance@1, sh_color@1 (deg 0..3), pixel_rays@1,
                        ray_peak@1, alpha_composite@3 (all profiles, with input
                        gradients), opacity_field@1.
@@ -152,6 +154,40 @@ def op_cases():
     np.savez_compressed(HERE / "ops.npz", **out)
 
 
+def geometry_cases():
+    """camera.pixel_rays@1, gaussian.ray_peak@1 and geometry.depth_normals@1 (with the
+    depth adjoint of a seeded linear loss on the normals)."""
+    from splatforge.gaussian import SurfaceOperators
+
+    ops = SurfaceOperators()
+    out = {}
+    g = torch.Generator().manual_seed(13)
+    K = torch.tensor([[420.0, 0.0, 311.5], [0.0, 415.0, 237.25], [0.0, 0.0, 1.0]])
+    out["rays/K"] = K.numpy()
+    out["rays/out"] = ops("camera.pixel_rays@1", K, width=64, height=48).numpy()
+    m = torch.randn(31, 3, generator=g)
+    A = torch.randn(31, 3, 3, generator=g)
+    Q = A @ A.transpose(-1, -2) + 0.1 * torch.eye(3)
+    o = torch.randn(23, 3, generator=g) * 2
+    d = torch.randn(23, 3, generator=g)
+    t, r, n = ops("gaussian.ray_peak@1", m, Q, o, d)
+    out.update({"peak/means": m.numpy(), "peak/Q": Q.numpy(), "peak/o": o.numpy(), "peak/d": d.numpy(),
+                "peak/t": t.numpy(), "peak/r": r.numpy(), "peak/n": n.numpy()})
+    H, W = 37, 53
+    yy, xx = torch.meshgrid(torch.arange(H, dtype=torch.float32), torch.arange(W, dtype=torch.float32), indexing="ij")
+    depth = 2.0 + 0.3 * torch.sin(xx / 7.0) + 0.2 * torch.cos(yy / 5.0) + 0.05 * torch.rand(H, W, generator=g)
+    depth[5, 9] = 0.0     # a hole: its neighbours become invalid
+    depth[20, 30] = -1.0  # a negative depth
+    depth = depth.requires_grad_()
+    Kd = torch.tensor([[60.0, 0.0, 26.0], [0.0, 58.0, 18.5], [0.0, 0.0, 1.0]])
+    normals, valid = ops("geometry.depth_normals@1", depth, Kd)
+    up = torch.randn(normals.shape, generator=g)
+    (gd,) = torch.autograd.grad((normals * up).sum(), depth)
+    out.update({"dn/depth": depth.detach().numpy(), "dn/K": Kd.numpy(), "dn/normals": normals.detach().numpy(),
+                "dn/valid": valid.numpy(), "dn/up": up.numpy(), "dn/gdepth": gd.numpy()})
+    np.savez_compressed(HERE / "geometry.npz", **out)
+
+
 CHANNELS = ("rgb", "alpha", "depth", "normals", "distortion_l1", "distortion_l2",
             "median_depth", "ray_color", "ambiguity_mask")
 
@@ -256,11 +292,13 @@ def render_cases():
 
 if __name__ == "__main__":
     _setup(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
-    which = sys.argv[2:] or ["binning", "ops", "render"]
+    which = sys.argv[2:] or ["binning", "ops", "geometry", "render"]
     if "binning" in which:
         binning_cases()
     if "ops" in which:
         op_cases()
+    if "geometry" in which:
+        geometry_cases()
     if "render" in which:
         render_cases()
     for f in sorted(HERE.glob("*.npz")):

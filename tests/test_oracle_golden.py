@@ -131,3 +131,21 @@ def test_oracle_crop_of_surface_scene(golden, mode):
     params = scenes.surfaces(20_000, seed=3)
     cam = camera_from(fix, "crop/")
     _check_render(fix, params, [cam], mode, "both", 1, sparse=True)
+
+
+def test_geometry_ops_match_reference_fixture(golden):
+    """camera.pixel_rays@1, gaussian.ray_peak@1 and geometry.depth_normals@1 (normals,
+    validity and the depth adjoint) of the oracle against the reference's outputs."""
+    f = golden("geometry")
+    K = torch.from_numpy(f["rays/K"])
+    np.testing.assert_allclose(ops.pixel_rays(K, width=64, height=48).numpy(), f["rays/out"], atol=1e-6)
+    t, r, n = ops.ray_peak(*(torch.from_numpy(f[f"peak/{k}"]) for k in ("means", "Q", "o", "d")))
+    np.testing.assert_allclose(t.numpy(), f["peak/t"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(r.numpy(), f["peak/r"], atol=1e-6)
+    np.testing.assert_allclose(n.numpy(), f["peak/n"], atol=1e-6)
+    depth = torch.from_numpy(f["dn/depth"]).requires_grad_()
+    normals, valid = ops.depth_normals(depth, torch.from_numpy(f["dn/K"]))
+    np.testing.assert_array_equal(valid.numpy(), f["dn/valid"])
+    np.testing.assert_allclose(normals.detach().numpy(), f["dn/normals"], atol=1e-6)
+    (gd,) = torch.autograd.grad((normals * torch.from_numpy(f["dn/up"])).sum(), depth)
+    np.testing.assert_allclose(gd.numpy(), f["dn/gdepth"], rtol=1e-4, atol=1e-5)

@@ -83,3 +83,24 @@ def test_renderer_factory_registers_and_builds():
     r.mode = "gof"
     r.render_training(None, None, geometric=False)
     assert calls == ["l1", "l2", "none", "none"]
+
+
+def test_geometry_ops_and_the_culled_field_register():
+    runtime = create_surface_runtime(implementations=provider.implementations(), capabilities=provider.capabilities())
+    sel = provider.selection()
+    for op in ("camera.pixel_rays@1", "gaussian.ray_peak@1", "geometry.depth_normals@1"):
+        impl = runtime.implementations.get(sel[op])
+        assert impl is not None and str(impl.manifest.op_key) == op
+    assert runtime.implementations.get(sel["geometry.depth_normals@1"]).manifest.eligibility.backward is True
+    culled = provider.selection(culled_field=True)["gaussian.opacity_field@1"]
+    impl = runtime.implementations.get(culled)
+    assert str(impl.manifest.op_key) == "gaussian.opacity_field@1"
+    assert impl.manifest.eligibility.host_synchronization != "none"
+    # the default policy forbids host synchronisation: the culled field is refused
+    p = torch.randn(5, 3, device="meta")
+    policy = ExecutionPolicy(implementation_id=culled, allow_unverified=True)
+    exp = runtime.explain_dispatch("gaussian.opacity_field@1", p, torch.randn(4, 3, device="meta"),
+                                   torch.randn(4, 3, 3, device="meta"), torch.rand(4, device="meta"),
+                                   torch.randn(2, 3, device="meta"), policy=policy)
+    cand = [c for c in exp.candidates if c.implementation_id == culled][0]
+    assert "host_synchronization_forbidden" in cand.reasons
