@@ -104,3 +104,11 @@ def test_geometry_ops_and_the_culled_field_register():
                                    torch.randn(2, 3, device="meta"), policy=policy)
     cand = [c for c in exp.candidates if c.implementation_id == culled][0]
     assert "host_synchronization_forbidden" in cand.reasons
+    # a policy that allows declared host synchronisation clears that reason
+    allowed = ExecutionPolicy(implementation_id=culled, providers=("native_cuda",), allow_unverified=True,
+                              host_sync="allow_declared")
+    exp = runtime.explain_dispatch("gaussian.opacity_field@1", p, torch.randn(4, 3, device="meta"),
+                                   torch.randn(4, 3, 3, device="meta"), torch.rand(4, device="meta"),
+                                   torch.randn(2, 3, device="meta"), policy=allowed)
+    cand = [c for c in exp.candidates if c.implementation_id == culled][0]
+    assert "host_synchronization_forbidden" not in cand.reasons
