@@ -399,12 +399,36 @@ def run_field(args):
             "gpu_launches": int(launches), "clocks": clk,
             "e2e": {"value": round(n_q * world / (ems * 1e-3), 1), "unit": "queries/s",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(n_q * 4), "ms_per_step": round(ems, 3)},
-            "roofline": None, "cpu_baseline": None,
+            "roofline": None, "cpu_baseline": field_cpu_baseline(host) if world == 1 and not args.no_cpu_baseline else None,
         }
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+def field_cpu_baseline(host, budget_s=15.0):
+    """The oracle's field (the reference's brute-force restatement) on the host cores: a
+    growing number of (query, origin) pairs (queries from this rank, one origin at a time)
+    until the budget is used; its cost is linear in both, so the rate of pairs divided by
+    the origin count gives queries/s over all origins."""
+    from oracle import ops as oracle_ops
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    pts, m, Q, o, org = (host[k] for k in ("pts", "means", "Q", "opac", "origins"))
+    pairs, spent, count, v = 0, 0.0, 2, 0
+    while spent < budget_s:
+        t0 = time.perf_counter()
+        oracle_ops.opacity_field(pts[:count], m, Q, o, org[v % org.shape[0]:v % org.shape[0] + 1], gaussian_chunk=65536)
+        spent += time.perf_counter() - t0
+        pairs += count
+        v += 1
+        count = min(count * 2, 64)
+    rate = pairs / spent / org.shape[0] if spent > 0 else 0.0
+    return {"value": round(rate, 4), "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"oracle opacity field on {pairs} (query, origin) pairs ({spent:.1f} s) against all "
+                      f"{m.shape[0]} Gaussians; linear in queries and origins, scaled to {org.shape[0]} origins"}
 
 
 def settings_config(settings):
