@@ -384,32 +384,53 @@ __device__ __forceinline__ bool l1_sort_pixel_packed(float* col_d, float* col_w,
     // and n - 1 < NN - 1 whenever there is padding
     key[j] = e < n ? ((key[j] - lo) << LOGN) | (uint32_t)e : 0xffffffffu;
   }
-  // sizes up to I sort inside each lane ...
+  // Bitonic sort in its all-ascending form: each merge of size s first compares
+  // position p with its mirror p ^ (s - 1), then runs half-cleaners p vs p ^ t for
+  // t = s/4 .. 1, the lower position always taking the minimum, so compare-exchanges
+  // inside a lane need no direction select.  Position p = lane * I + j; the mirror of
+  // (lane, j) is (lane ^ (s/I - 1), I - 1 - j) once s > I.
 #pragma unroll
   for (int size = 2; size <= I; size <<= 1) {
 #pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+    for (int j = 0; j < I; ++j) {
+      const int m = j ^ (size - 1);
+      if (j < m) {
+        const uint32_t a = min(key[j], key[m]), b = max(key[j], key[m]);
+        key[j] = a;
+        key[m] = b;
+      }
+    }
+#pragma unroll
+    for (int stride = size >> 2; stride > 0; stride >>= 1) {
 #pragma unroll
       for (int j = 0; j < I; ++j) {
         if ((j & stride) == 0) {
-          const bool up = ((lane * I + j) & size) == 0;
           const uint32_t a = min(key[j], key[j + stride]), b = max(key[j], key[j + stride]);
-          key[j] = up ? a : b;
-          key[j + stride] = up ? b : a;
+          key[j] = a;
+          key[j + stride] = b;
         }
       }
     }
   }
-  // ... then each larger merge: cross-lane strides rolled, in-lane strides unrolled
 #pragma unroll 1
   for (int size = 2 * I; size <= NN; size <<= 1) {
-    const bool up = ((lane * I) & size) == 0;
+    {
+      const int lm = size / I - 1;
+      const bool take_min = (lane & (size / (2 * I))) == 0;
+#pragma unroll
+      for (int j = 0; j < I / 2; ++j) {
+        const uint32_t o1 = __shfl_xor_sync(FULL, key[I - 1 - j], lm);
+        const uint32_t o2 = __shfl_xor_sync(FULL, key[j], lm);
+        key[j] = take_min ? min(key[j], o1) : max(key[j], o1);
+        key[I - 1 - j] = take_min ? min(key[I - 1 - j], o2) : max(key[I - 1 - j], o2);
+      }
+    }
 #pragma unroll 1
-    for (int lm = size / (2 * I); lm > 0; lm >>= 1) {
-      const bool take_min = ((lane & lm) == 0) == up;
+    for (int ls = size / (4 * I); ls > 0; ls >>= 1) {
+      const bool take_min = (lane & ls) == 0;
 #pragma unroll
       for (int j = 0; j < I; ++j) {
-        const uint32_t o = __shfl_xor_sync(FULL, key[j], lm);
+        const uint32_t o = __shfl_xor_sync(FULL, key[j], ls);
         key[j] = take_min ? min(key[j], o) : max(key[j], o);
       }
     }
@@ -419,8 +440,8 @@ __device__ __forceinline__ bool l1_sort_pixel_packed(float* col_d, float* col_w,
       for (int j = 0; j < I; ++j) {
         if ((j & stride) == 0) {
           const uint32_t a = min(key[j], key[j + stride]), b = max(key[j], key[j + stride]);
-          key[j] = up ? a : b;
-          key[j + stride] = up ? b : a;
+          key[j] = a;
+          key[j + stride] = b;
         }
       }
     }
