@@ -584,7 +584,7 @@ __global__ void __launch_bounds__(128) l1_resolve_kernel(
 
 // ------------------------------------------------------------------ backward
 template <int MODE, int DIST>
-__global__ void __launch_bounds__(TILE_PIXELS) raster_backward_kernel(const RasterBwdArgs a) {
+__global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const RasterBwdArgs a) {
   __shared__ float4 s_rec[TILE_PIXELS * REC4];
   __shared__ int s_id[TILE_PIXELS];
   __shared__ float s_acc[TILE_PIXELS * ACC];

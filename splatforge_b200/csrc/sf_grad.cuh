@@ -144,7 +144,7 @@ SF_HD void sample_backward(const float* rec, const PixelRay& pr, const Sample& s
     float gdy = g_sq * 2.f * (qb * s.dx + qc * s.dy);
     float gqa = g_sq * s.dx * s.dx, gqb = g_sq * 2.f * s.dx * s.dy, gqc = g_sq * s.dy * s.dy;
     if (MODE == SF_MODE_RADEGS) {
-      float inv = 1.f / pr.rnorm;
+      float inv = pr.inv_rnorm;
       float g_rad = g_depth * inv;
       float gg0 = g_depth * s.dx * inv, gg1 = g_depth * s.dy * inv;
       gdx += g_depth * rec[R_GAIN] * inv;

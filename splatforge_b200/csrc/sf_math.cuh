@@ -505,6 +505,7 @@ struct PixelRay {
   float r[3];   // inv(K) (u+.5, v+.5, 1)
   float px, py; // K r (pixel coordinates as the reference recomputes them)
   float rnorm;  // |r|
+  float inv_rnorm;  // 1 / |r|
 };
 
 SF_HD void pixel_ray(const sf_camera& cam, int u, int v, PixelRay& pr) {
@@ -516,6 +517,18 @@ SF_HD void pixel_ray(const sf_camera& cam, int u, int v, PixelRay& pr) {
   pr.px = radd(radd(rmul(pr.r[0], K[0]), rmul(pr.r[1], K[1])), rmul(pr.r[2], K[2]));
   pr.py = radd(radd(rmul(pr.r[0], K[3]), rmul(pr.r[1], K[4])), rmul(pr.r[2], K[5]));
   pr.rnorm = rsqrt_rn(dot3(pr.r[0], pr.r[1], pr.r[2], pr.r[0], pr.r[1], pr.r[2]));
+  pr.inv_rnorm = rdiv(1.f, pr.rnorm);
+}
+
+// exp for the per-sample response: the hardware exp2 path on the device (within a few
+// ulp), the C library on the host.  The response feeds no bit-exact comparison with
+// the oracle; the forward and backward kernels evaluate it with the same instructions.
+SF_HD float fast_exp(float x) {
+#if defined(__CUDA_ARCH__)
+  return __expf(x);
+#else
+  return expf(x);
+#endif
 }
 
 // delta^T Q delta as dx (Q delta)_x + dy (Q delta)_y, exact sequence
@@ -589,7 +602,7 @@ SF_HD bool eval_sample(const float* rec, const PixelRay& pr, float ext2, float n
     s.den_raw = dot3(s.qd[0], s.qd[1], s.qd[2], r[0], r[1], r[2]);
     s.den = fmaxr(s.den_raw, 1e-12f);
     const float* pm = rec + R_PROXY;
-    s.t = rdiv(dot3(pm[0], pm[1], pm[2], s.qd[0], s.qd[1], s.qd[2]), s.den);
+    s.t = dot3(pm[0], pm[1], pm[2], s.qd[0], s.qd[1], s.qd[2]) * fast_rcp(s.den);
     s.off[0] = ffma(s.t, r[0], -pm[0]);
     s.off[1] = ffma(s.t, r[1], -pm[1]);
     s.off[2] = ffma(s.t, r[2], -pm[2]);
@@ -597,7 +610,7 @@ SF_HD bool eval_sample(const float* rec, const PixelRay& pr, float ext2, float n
     s.qo[1] = dot3(q[1], q[3], q[4], s.off[0], s.off[1], s.off[2]);
     s.qo[2] = dot3(q[2], q[4], q[5], s.off[0], s.off[1], s.off[2]);
     s.e = dot3(s.off[0], s.off[1], s.off[2], s.qo[0], s.qo[1], s.qo[2]);
-    resp = expf(rmul(-0.5f, fmaxr(s.e, 0.f)));
+    resp = fast_exp(rmul(-0.5f, fmaxr(s.e, 0.f)));
     s.depth = s.t;
     // normal = normalize(-Q r), one reciprocal square root (F.normalize's 1e-12 guard)
     const float nn = s.qd[0] * s.qd[0] + s.qd[1] * s.qd[1] + s.qd[2] * s.qd[2];
@@ -608,15 +621,15 @@ SF_HD bool eval_sample(const float* rec, const PixelRay& pr, float ext2, float n
 #endif
     s.n[0] = -s.qd[0] * s.ninv; s.n[1] = -s.qd[1] * s.ninv; s.n[2] = -s.qd[2] * s.ninv;
   } else {
-    resp = expf(rmul(-0.5f, s.sq));
+    resp = fast_exp(rmul(-0.5f, s.sq));
     if (MODE == SF_MODE_RADEGS) {
-      s.depth = rdiv(radd(rec[R_RADIAL], ffma(rec[R_GAIN + 1], s.dy, rmul(rec[R_GAIN], s.dx))), pr.rnorm);
+      s.depth = radd(rec[R_RADIAL], ffma(rec[R_GAIN + 1], s.dy, rmul(rec[R_GAIN], s.dx))) * pr.inv_rnorm;
       s.n[0] = rec[R_NRM]; s.n[1] = rec[R_NRM + 1]; s.n[2] = rec[R_NRM + 2];
     } else {
       s.n[0] = rec[R_ANRM]; s.n[1] = rec[R_ANRM + 1]; s.n[2] = rec[R_ANRM + 2];
       s.aden = dot3(s.n[0], s.n[1], s.n[2], pr.r[0], pr.r[1], pr.r[2]);
       s.aok = fabsf(s.aden) > 1e-8f;
-      s.depth = rdiv(rec[R_PLANE], s.aok ? s.aden : 1.f);
+      s.depth = rec[R_PLANE] * fast_rcp(s.aok ? s.aden : 1.f);
       if (!s.aok) resp = 0.f;
     }
   }
