@@ -187,12 +187,18 @@ __global__ void __launch_bounds__(RS_THREADS, 2) radix_downsweep_kernel(
   uint32_t key[RS_ROUNDS];
   int32_t val[RS_ROUNDS];
   uint32_t rank[RS_ROUNDS];
+  // all loads first, so that the 32 per thread are in flight together
 #pragma unroll
   for (int r = 0; r < RS_ROUNDS; ++r) {
     const int64_t idx = base + r * 32 + lane;
     const bool valid = idx < n;
-    key[r] = valid ? keys_in[idx] : 0u;
-    val[r] = valid ? vals_in[idx] : 0;
+    key[r] = valid ? __ldg(keys_in + idx) : 0u;
+    val[r] = valid ? __ldg(vals_in + idx) : 0;
+  }
+#pragma unroll
+  for (int r = 0; r < RS_ROUNDS; ++r) {
+    const int64_t idx = base + r * 32 + lane;
+    const bool valid = idx < n;
     const uint32_t d = (key[r] >> shift) & 0xff;
     const unsigned peers = __match_any_sync(FULL, valid ? d : 0x100u + lane);
     const uint32_t before = valid ? s_cnt[wid][d] : 0u;
