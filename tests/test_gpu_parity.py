@@ -42,7 +42,7 @@ def run_gpu(params, cam, settings, sel, ups):
     p = params.detach_clone().requires_grad_()
     v = scenes.activated(p)
     view = [t.to(DEV) for t in (v.means, v.quats, v.scales, v.opacities, v.sh)]
-    out = rasterize(*view, 3, cam, settings, selected=None if sel is None else sel.to(DEV))
+    out = rasterize(*view, params.sh_degree, cam, settings, selected=None if sel is None else sel.to(DEV))
     loss = sum((out[ch] * ups[ch].to(DEV)).sum() for ch in CHANNELS)
     loss.backward()
     grads = {name: t.grad.cpu() for name, t in zip(PARAM_NAMES, p.tensors())}
@@ -54,9 +54,10 @@ def run_gpu(params, cam, settings, sel, ups):
     return imgs, grads, out
 
 
-def run_oracle(params, cam, mode, distortions, sel, ups):
+def run_oracle(params, cam, mode, distortions, sel, ups, settings=None):
     p = params.detach_clone().requires_grad_()
-    out = oracle_render.render(scenes.activated(p), cam, mode=mode, selected=sel, distortions=distortions)
+    out = oracle_render.render(scenes.activated(p), cam, mode=mode, selected=sel, distortions=distortions,
+                               settings=settings)
     loss = sum((out[ch] * ups[ch]).sum() for ch in CHANNELS)
     loss.backward()
     grads = {name: t.grad for name, t in zip(PARAM_NAMES, p.tensors())}
@@ -333,3 +334,33 @@ def test_l1_wide_depth_span_matches_the_oracle():
         want, wgrads, _ = run_oracle(params, cam, mode, "both", None, ups)
         assert_images(got, want, mode, f"span/{mode}")
         assert_grads(ggrads, wgrads, f"span/{mode}")
+
+
+@pytest.mark.parametrize("mode", ["radegs", "gof", "ambisur"])
+def test_render_settings_variants(mode):
+    """The RenderConfig fields besides the mode: the antialiasing opacity compensation,
+    a coloured background, a raised near plane and a lowered far plane that cut
+    samples, a larger eps2d, and SH degrees below 3."""
+    torch.set_num_threads(4)
+    params, cams = scenes.workload("demo48", seed=0)
+    sel = torch.arange(48) % 3 == 0
+    variants = [
+        dict(antialiased=True, background=(0.1, 0.5, 0.9), sh_degree=3),
+        dict(near=2.6, far=3.4, eps2d=0.5, sh_degree=1),
+        dict(antialiased=True, near=0.5, sh_degree=0),
+        dict(background=(0.0, 0.0, 0.0), eps2d=0.1, sh_degree=2),
+    ]
+    for k, var in enumerate(variants):
+        var = dict(var)
+        degree = var.pop("sh_degree")
+        p = scenes.SceneParams(params.means, params.log_scales, params.quats, params.opacity_logits,
+                               params.sh, degree)
+        gpu_settings = RasterSettings(mode=mode, distortions="both", **var)
+        ora = oracle_render.RenderSettings(**var)
+        for v in (0, 3, 6):
+            cam = cams[v]
+            ups = _ups(cam, 300 + 10 * k + v)
+            got, ggrads, _ = run_gpu(p, cam, gpu_settings, sel, ups)
+            want, wgrads, _ = run_oracle(p, cam, mode, "both", sel, ups, settings=ora)
+            assert_images(got, want, mode, f"{mode}/variant{k}/v{v}")
+            assert_grads(ggrads, wgrads, f"{mode}/variant{k}/v{v}")
