@@ -109,8 +109,7 @@ SF_HD void sample_backward(const float* rec, const PixelRay& pr, const Sample& s
     gQ[5] = g_e * s.off[2] * s.off[2];
     float g_t = g_depth + (r[0] * goff0 + r[1] * goff1 + r[2] * goff2);
     float gp0 = -goff0, gp1 = -goff1, gp2 = -goff2;
-    const float inv_den = 1.f / s.den;
-    float g_num = g_t * inv_den;
+    float g_num = g_t * s.inv_den;
     float g_den = -g_num * s.t;
     gp0 += g_num * s.qd[0]; gp1 += g_num * s.qd[1]; gp2 += g_num * s.qd[2];
     float gqd0 = g_num * pm[0], gqd1 = g_num * pm[1], gqd2 = g_num * pm[2];

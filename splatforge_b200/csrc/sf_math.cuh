@@ -576,8 +576,8 @@ struct Sample {
   float alpha;     // clamped
   float depth;
   float n[3];      // sample normal (GOF: normalize(-Q d); else per-Gaussian)
-  // GOF intermediates (qo = Q off; ninv = 1 / max(|Q r|, 1e-12))
-  float qd[3], den_raw, den, t, off[3], e, qo[3], ninv;
+  // GOF intermediates (qo = Q off; ninv = 1 / max(|Q r|, 1e-12); inv_den = 1 / den)
+  float qd[3], den_raw, den, inv_den, t, off[3], e, qo[3], ninv;
   // AmbiSuR intermediates
   float aden;
   bool aok;
@@ -602,7 +602,8 @@ SF_HD bool eval_sample(const float* rec, const PixelRay& pr, float ext2, float n
     s.den_raw = dot3(s.qd[0], s.qd[1], s.qd[2], r[0], r[1], r[2]);
     s.den = fmaxr(s.den_raw, 1e-12f);
     const float* pm = rec + R_PROXY;
-    s.t = dot3(pm[0], pm[1], pm[2], s.qd[0], s.qd[1], s.qd[2]) * fast_rcp(s.den);
+    s.inv_den = fast_rcp(s.den);
+    s.t = dot3(pm[0], pm[1], pm[2], s.qd[0], s.qd[1], s.qd[2]) * s.inv_den;
     s.off[0] = ffma(s.t, r[0], -pm[0]);
     s.off[1] = ffma(s.t, r[1], -pm[1]);
     s.off[2] = ffma(s.t, r[2], -pm[2]);
