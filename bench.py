@@ -123,7 +123,8 @@ MEASURED_TRAFFIC = {("surfaces1m_1080p", "gof", "both", "raster_backward"): 3216
 
 
 def algorithmic_flops(mode, n_pairs_fwd):
-    """Per-pair algorithmic FP32 flops of the raster forward (SURVEY/DESIGN table)."""
+    """Per-pair algorithmic FP32 flops of the raster forward: the sample equations of
+    each mode (GOF: Q r, the ray peak, the offset, its quadratic form, the normal)."""
     per = {"radegs": 35, "gof": 70, "ambisur": 40}[mode]
     return per * n_pairs_fwd
 
