@@ -206,6 +206,21 @@ class _Project(torch.autograd.Function):
         return (*outs, None)
 
 
+_PINNED = {}
+
+
+def _pinned_scratch(dtype=torch.int64):
+    """A small pinned host buffer for the synchronous read-backs (per thread, per dtype)."""
+    import threading
+
+    key = (threading.get_ident(), dtype)
+    buf = _PINNED.get(key)
+    if buf is None:
+        buf = torch.empty((4,), dtype=dtype, pin_memory=True)
+        _PINNED[key] = buf
+    return buf
+
+
 def bin_gaussians(plan):
     """Device tile binning; one host read (intersection count + non-finite flag)."""
     n, dev = plan.n, plan.device
@@ -218,7 +233,12 @@ def bin_gaussians(plan):
         "sf_b200_bin_order", _ptr(plan.count), _ptr(plan.depth_key), n, _ptr(order), _ptr(offsets),
         _ptr(ws), size.value, _stream(dev),
     )
-    total, bad = torch.stack((offsets[n], plan.nonfinite[0].to(torch.int64))).tolist()
+    # the one read-back of the binning: two small async copies into pinned memory
+    host, host32 = _pinned_scratch(), _pinned_scratch(torch.int32)
+    host[0:1].copy_(offsets[n:n + 1], non_blocking=True)
+    host32[0:1].copy_(plan.nonfinite[0:1], non_blocking=True)
+    torch.cuda.current_stream(dev).synchronize()
+    total, bad = int(host[0]), int(host32[0])
     if bad:
         raise FloatingPointError("non-finite projected bounds")
     plan.n_isect = int(total)
@@ -286,7 +306,10 @@ class _Raster(torch.autograd.Function):
         else:
             run()
         if use_l1:
-            most = int(needed.item())
+            host32 = _pinned_scratch(torch.int32)
+            host32[1:2].copy_(needed, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+            most = int(host32[1])
             plan.stats["l1_max_samples"] = most
             plan.stats["l1_capacity"] = cap
             if plan.l1_capacity is None:
