@@ -17,18 +17,32 @@ namespace {
 
 constexpr int PB = 128;  // Gaussians per CTA
 
-// Copy rows [first, first+rows) of a [N, width] float array into shared memory with
-// 128-bit loads when the slab is 16-byte aligned, scalar loads otherwise.
-__device__ __forceinline__ void stage_rows(float* dst, const float* src, int64_t first, int rows,
-                                           int width) {
-  const int64_t count = (int64_t)rows * width;
+// Copy rows [first, first+rows) of a [N, width] float array into shared memory rows of
+// `stride` floats (stride = width + 1: an odd row stride, so that the threads of a warp,
+// each reading its own row, hit distinct banks).  128-bit global loads when the slab
+// is 16-byte aligned, scalar loads otherwise.
+__device__ __forceinline__ int row_stride(int width) { return width + ((width & 1) ^ 1); }
+
+__device__ __forceinline__ void stage_rows(float* dst, const float* src, int64_t first, int rows, int width,
+                                           int stride) {
+  const int count = rows * width;
   const float* base = src + first * width;
   if ((((uintptr_t)base) & 15) == 0 && (count & 3) == 0) {
     const float4* s4 = reinterpret_cast<const float4*>(base);
-    float4* d4 = reinterpret_cast<float4*>(dst);
-    for (int64_t k = threadIdx.x; k < count / 4; k += blockDim.x) d4[k] = __ldg(s4 + k);
+    for (int k = threadIdx.x; k < count / 4; k += blockDim.x) {
+      const float4 v = __ldg(s4 + k);
+      const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int idx = 4 * k + c, r = idx / width;
+        dst[r * stride + (idx - r * width)] = e[c];
+      }
+    }
   } else {
-    for (int64_t k = threadIdx.x; k < count; k += blockDim.x) dst[k] = __ldg(base + k);
+    for (int k = threadIdx.x; k < count; k += blockDim.x) {
+      const int r = k / width;
+      dst[r * stride + (k - r * width)] = __ldg(base + k);
+    }
   }
 }
 
@@ -56,11 +70,12 @@ __global__ void __launch_bounds__(PB) project_forward_kernel(
     const sf_camera cam, const sf_settings st, float* __restrict__ means2d,
     float* __restrict__ radii, float* __restrict__ records, int32_t* __restrict__ rect,
     int32_t* __restrict__ count, uint32_t* __restrict__ depth_key, int32_t* nonfinite) {
-  extern __shared__ float s_sh[];  // [PB, K*3]
+  extern __shared__ float s_sh[];  // [PB, row_stride(K*3)]
   const int K = st.sh_coeffs;
   const int64_t first = (int64_t)blockIdx.x * PB;
   const int rows = (int)min((int64_t)PB, n - first);
-  stage_rows(s_sh, sh, first, rows, K * 3);
+  const int stride = row_stride(K * 3);
+  stage_rows(s_sh, sh, first, rows, K * 3, stride);
   __syncthreads();
   if ((int)threadIdx.x >= rows) return;
   const int64_t i = first + threadIdx.x;
@@ -83,7 +98,7 @@ __global__ void __launch_bounds__(PB) project_forward_kernel(
   rec[R_QA] = p.qa; rec[R_QB] = p.qb; rec[R_QC] = p.qc;
   rec[R_OPA] = opa;
   const float dir[3] = {m[0] - cam.origin[0], m[1] - cam.origin[1], m[2] - cam.origin[2]};
-  sh_color(s_sh + threadIdx.x * K * 3, st.sh_degree, dir, rec + R_RGB);
+  sh_color(s_sh + threadIdx.x * stride, st.sh_degree, dir, rec + R_RGB);
   rec[R_SEL] = selected && selected[i] ? 1.f : 0.f;
   rec[R_Z] = p.mc[2];
   if (st.mode == SF_MODE_RADEGS) {
@@ -120,11 +135,12 @@ __global__ void __launch_bounds__(PB) project_backward_kernel(
     const float* __restrict__ sh, int64_t n, const sf_camera cam, const sf_settings st,
     const float* __restrict__ gxy, const float* __restrict__ grec, float* g_means,
     float* g_quats, float* g_scales, float* g_opacities, float* g_sh) {
-  extern __shared__ float s_sh[];  // [PB, K*3] coefficients, reused for their adjoints
+  extern __shared__ float s_sh[];  // [PB, row_stride(K*3)] coefficients, then their adjoints
   const int K = st.sh_coeffs;
   const int64_t first = (int64_t)blockIdx.x * PB;
   const int rows = (int)min((int64_t)PB, n - first);
-  stage_rows(s_sh, sh, first, rows, K * 3);
+  const int stride = row_stride(K * 3);
+  stage_rows(s_sh, sh, first, rows, K * 3, stride);
   __syncthreads();
   if ((int)threadIdx.x < rows) {
     const int64_t i = first + threadIdx.x;
@@ -140,24 +156,26 @@ __global__ void __launch_bounds__(PB) project_backward_kernel(
     }
     const float gx[2] = {gxy[i * 2], gxy[i * 2 + 1]};
     float gm[3], gq[4], gs[3], go;
-    float gsh[48];
-    float* coeffs = s_sh + threadIdx.x * K * 3;
+    float* coeffs = s_sh + threadIdx.x * stride;
+    // the SH adjoint replaces the staged coefficients in place (read before written)
     project_backward(m, q, sc, opacities[i], coeffs, st.sh_degree, cam, st, gx, g, gm, gq, gs,
-                     &go, gsh);
+                     &go, coeffs);
     if (g_means) { g_means[i * 3] = gm[0]; g_means[i * 3 + 1] = gm[1]; g_means[i * 3 + 2] = gm[2]; }
     if (g_quats)
       reinterpret_cast<float4*>(g_quats)[i] = make_float4(gq[0], gq[1], gq[2], gq[3]);
     if (g_scales) { g_scales[i * 3] = gs[0]; g_scales[i * 3 + 1] = gs[1]; g_scales[i * 3 + 2] = gs[2]; }
     if (g_opacities) g_opacities[i] = go;
-    const int used = sh_count(st.sh_degree) * 3;
-    for (int k = 0; k < K * 3; ++k) coeffs[k] = k < used ? gsh[k] : 0.f;
+    for (int k = sh_count(st.sh_degree) * 3; k < K * 3; ++k) coeffs[k] = 0.f;
   }
   __syncthreads();
   if (g_sh) {
     // coalesced write-back of the staged coefficient adjoints
     const int64_t count = (int64_t)rows * K * 3;
     float* base = g_sh + first * K * 3;
-    for (int64_t k = threadIdx.x; k < count; k += blockDim.x) base[k] = s_sh[k];
+    for (int64_t k = threadIdx.x; k < count; k += blockDim.x) {
+      const int r = (int)(k / (K * 3));
+      base[k] = s_sh[r * stride + (int)(k - (int64_t)r * K * 3)];
+    }
   }
 }
 
@@ -223,7 +241,7 @@ cudaError_t launch_project_forward(const float* means, const float* quats, const
                                    float* records, int32_t* rect, int32_t* count,
                                    uint32_t* depth_key, int32_t* nonfinite, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
-  const size_t smem = (size_t)PB * st.sh_coeffs * 3 * sizeof(float);
+  const size_t smem = (size_t)PB * (st.sh_coeffs * 3 + 1) * sizeof(float);
   count_launches(1);
   project_forward_kernel<<<blocks_for(n, PB), PB, smem, s>>>(
       means, quats, scales, opacities, sh, selected, n, cam, st, means2d, radii, records, rect,
@@ -238,7 +256,7 @@ cudaError_t launch_project_backward(const float* means, const float* quats, cons
                                     float* g_quats, float* g_scales, float* g_opacities,
                                     float* g_sh, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
-  const size_t smem = (size_t)PB * st.sh_coeffs * 3 * sizeof(float);
+  const size_t smem = (size_t)PB * (st.sh_coeffs * 3 + 1) * sizeof(float);
   count_launches(1);
   project_backward_kernel<<<blocks_for(n, PB), PB, smem, s>>>(
       means, quats, scales, opacities, sh, n, cam, st, gxy, grec, g_means, g_quats, g_scales,
