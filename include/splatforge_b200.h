@@ -252,6 +252,52 @@ int sf_b200_depth_normals_backward(const float* depth, const float* K, int32_t w
                                    const float* grad_normals, float* grad_depth, float* workspace,
                                    void* stream);
 
+/* ---- GOF mesh extraction ---------------------------------------------------------
+ * The device stages of GOFExporter.export (src/splatforge/studio/exporters.py:20-102)
+ * and of marching_tetrahedra (src/splatforge/mesh/tetrahedra.py:34-109).  The caller
+ * deduplicates the grid points and triangulates them on the host (as the reference
+ * does), then runs, on one stream:
+ *   mesh_count  -> host reads slot_offsets[n_cells] (S) and face_offsets[n_cells] (F)
+ *   mesh_edges  -> host reads *n_edges (U, the unique crossing edges)
+ *   binary_steps x (mesh_midpoints, field(midpoints) -> values, mesh_bisect)
+ *   mesh_faces  -> host reads *n_kept
+ * Points and vertices are float64 [*,3]; cells int32 [n_cells,4] (16-byte aligned);
+ * values float64; inside and low_inside uint8 0/1.  n_edges and n_kept are DEVICE
+ * int64 scalars.  With equal field values the output equals the reference's:
+ * vertices [U,3] in ascending (low vertex, high vertex) edge order and faces [n_kept,3]
+ * in cell order, oriented away from the inside vertices, degenerate ones removed.
+ *
+ * mesh_grid_points: exporters.py:20-38 without the deduplication: seed Gaussian
+ *   chosen[i] -> points [n,9,3] (its centre, then the 8 corners of the extent-sigma box
+ *   in itertools.product((-1,1), repeat=3) order) and radius [n] = max scale * extent
+ *   (a float32 product).  scales are the activated (exponentiated) scales. */
+int sf_b200_mesh_grid_points(const float* means, const float* quats, const float* scales,
+                             const int32_t* chosen, int64_t n, double extent, double* points,
+                             double* radius, void* stream);
+int sf_b200_mesh_count_workspace_bytes(int64_t n_cells, size_t* bytes);
+int sf_b200_mesh_count(const double* values, int64_t n_points, const int32_t* cells, int64_t n_cells,
+                       double level, int32_t inside_greater, uint8_t* inside, int64_t* slot_offsets,
+                       int64_t* face_offsets, void* workspace, size_t workspace_bytes, void* stream);
+int sf_b200_mesh_edges_workspace_bytes(int64_t n_slots, size_t* bytes);
+/* edge_ids [S] (unique edge of each crossing slot), pairs [S,2], low/high [S,3] and
+ * low_inside [S]: the first U rows are the unique edges. */
+int sf_b200_mesh_edges(const double* points, int64_t n_points, const int32_t* cells, int64_t n_cells,
+                       const uint8_t* inside, const int64_t* slot_offsets, int64_t n_slots,
+                       int32_t* edge_ids, int32_t* pairs, double* low, double* high,
+                       uint8_t* low_inside, int64_t* n_edges, void* workspace,
+                       size_t workspace_bytes, void* stream);
+int sf_b200_mesh_midpoints(const double* low, const double* high, int64_t n_edges, double* midpoints,
+                           void* stream);
+int sf_b200_mesh_bisect(double* low, double* high, const uint8_t* low_inside, int64_t n_edges,
+                        const double* values, double level, int32_t inside_greater, void* stream);
+int sf_b200_mesh_faces_workspace_bytes(int64_t n_faces, size_t* bytes);
+int sf_b200_mesh_faces(const double* points, const int32_t* cells, int64_t n_cells,
+                       const uint8_t* inside, const int64_t* slot_offsets, const int32_t* edge_ids,
+                       const double* low, const double* high, int64_t n_edges,
+                       const int64_t* face_offsets, int64_t n_faces, double* vertices,
+                       int64_t* faces, int64_t* n_kept, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
 /* ---- raster forward (batched_renderer.py:169-338 + alpha_composite@3) -----------
  * One CTA per 16x16 tile.  Images are HWC float32: rgb/normals [H,W,3], the rest
  * [H,W].  pixel_state [H*W, SF_PIXEL_STATE_FLOATS] is kept for the backward pass.

@@ -7,7 +7,7 @@ anywhere in this package.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_float, c_int32, c_int64, c_size_t, c_uint8, c_void_p
+from ctypes import POINTER, c_double, c_float, c_int32, c_int64, c_size_t, c_uint8, c_void_p
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -103,6 +103,19 @@ _SIGNATURES = {
     "sf_b200_ray_peak": (ctypes.c_int, [P, P, c_int64, P, P, c_int64, P, P, P, P]),
     "sf_b200_depth_normals": (ctypes.c_int, [P, P, c_int32, c_int32, P, P, P]),
     "sf_b200_depth_normals_backward": (ctypes.c_int, [P, P, c_int32, c_int32, P, P, P, P]),
+    "sf_b200_mesh_grid_points": (ctypes.c_int, [P, P, P, P, c_int64, c_double, P, P, P]),
+    "sf_b200_mesh_count_workspace_bytes": (ctypes.c_int, [c_int64, POINTER(c_size_t)]),
+    "sf_b200_mesh_count": (ctypes.c_int, [P, c_int64, P, c_int64, c_double, c_int32, P, P, P, P, c_size_t, P]),
+    "sf_b200_mesh_edges_workspace_bytes": (ctypes.c_int, [c_int64, POINTER(c_size_t)]),
+    "sf_b200_mesh_edges": (
+        ctypes.c_int, [P, c_int64, P, c_int64, P, P, c_int64, P, P, P, P, P, P, P, c_size_t, P]
+    ),
+    "sf_b200_mesh_midpoints": (ctypes.c_int, [P, P, c_int64, P, P]),
+    "sf_b200_mesh_bisect": (ctypes.c_int, [P, P, P, c_int64, P, c_double, c_int32, P]),
+    "sf_b200_mesh_faces_workspace_bytes": (ctypes.c_int, [c_int64, POINTER(c_size_t)]),
+    "sf_b200_mesh_faces": (
+        ctypes.c_int, [P, P, c_int64, P, P, P, P, P, c_int64, P, c_int64, P, P, P, P, c_size_t, P]
+    ),
     "sf_b200_raster_forward": (
         ctypes.c_int,
         [P, c_int64, P, P, POINTER(Camera), POINTER(Settings)]

@@ -461,4 +461,105 @@ int sf_b200_alpha_composite_backward(const float* alphas, const float* colors, c
                      "alpha_composite_backward");
 }
 
+// ------------------------------------------------------------------ GOF mesh extraction
+int sf_b200_mesh_grid_points(const float* means, const float* quats, const float* scales, const int32_t* chosen,
+                             int64_t n, double extent, double* points, double* radius, void* stream) {
+  if (n < 0) return fail(SF_ERR_ARGUMENT, "mesh_grid_points: negative size");
+  if (n > 0 && (!means || !quats || !scales || !chosen || !points || !radius))
+    return fail(SF_ERR_ARGUMENT, "mesh_grid_points: NULL buffer");
+  return cuda_status(sf::launch_grid_points(means, quats, scales, chosen, n, extent, points, radius,
+                                            as_stream(stream)),
+                     "mesh_grid_points");
+}
+
+int sf_b200_mesh_count_workspace_bytes(int64_t n_cells, size_t* bytes) {
+  if (n_cells < 0 || !bytes) return fail(SF_ERR_ARGUMENT, "mesh_count_workspace_bytes: bad arguments");
+  *bytes = sf::mesh_count_workspace_bytes(n_cells);
+  return SF_OK;
+}
+
+int sf_b200_mesh_count(const double* values, int64_t n_points, const int32_t* cells, int64_t n_cells, double level,
+                       int32_t inside_greater, uint8_t* inside, int64_t* slot_offsets, int64_t* face_offsets,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  if (n_points < 0 || n_cells < 0 || n_points > 0x7fffffffLL)
+    return fail(SF_ERR_ARGUMENT, "mesh_count: sizes must be non-negative and points fit 32-bit indices");
+  if (!slot_offsets || !face_offsets || (n_points > 0 && (!values || !inside)) ||
+      (n_cells > 0 && (!cells || !inside || !workspace)))
+    return fail(SF_ERR_ARGUMENT, "mesh_count: NULL buffer");
+  if (reinterpret_cast<uintptr_t>(cells) % 16) return fail(SF_ERR_ARGUMENT, "mesh_count: cells must be 16-byte aligned");
+  if (workspace_bytes < sf::mesh_count_workspace_bytes(n_cells))
+    return fail(SF_ERR_CAPACITY, "mesh_count: workspace of %zu bytes, %zu needed", workspace_bytes,
+                sf::mesh_count_workspace_bytes(n_cells));
+  return cuda_status(sf::mesh_count(values, n_points, cells, n_cells, level, inside_greater != 0, inside, slot_offsets,
+                                    face_offsets, workspace, workspace_bytes, as_stream(stream)),
+                     "mesh_count");
+}
+
+int sf_b200_mesh_edges_workspace_bytes(int64_t n_slots, size_t* bytes) {
+  if (n_slots < 0 || !bytes) return fail(SF_ERR_ARGUMENT, "mesh_edges_workspace_bytes: bad arguments");
+  if (n_slots > 0x7fffffffLL) return fail(SF_ERR_CAPACITY, "mesh_edges: %lld crossing slots exceed 32-bit indices",
+                                          (long long)n_slots);
+  *bytes = sf::mesh_edges_workspace_bytes(n_slots);
+  return SF_OK;
+}
+
+int sf_b200_mesh_edges(const double* points, int64_t n_points, const int32_t* cells, int64_t n_cells,
+                       const uint8_t* inside, const int64_t* slot_offsets, int64_t n_slots, int32_t* edge_ids,
+                       int32_t* pairs, double* low, double* high, uint8_t* low_inside, int64_t* n_edges,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  if (n_points < 0 || n_cells < 0 || n_slots < 0 || !n_edges) return fail(SF_ERR_ARGUMENT, "mesh_edges: bad arguments");
+  if (n_slots > 0x7fffffffLL || n_points > 0x7fffffffLL)
+    return fail(SF_ERR_CAPACITY, "mesh_edges: sizes exceed 32-bit indices");
+  if (n_slots > 0 && (!points || !cells || !inside || !slot_offsets || !edge_ids || !pairs || !low || !high ||
+                      !low_inside || !workspace))
+    return fail(SF_ERR_ARGUMENT, "mesh_edges: NULL buffer");
+  if (reinterpret_cast<uintptr_t>(cells) % 16) return fail(SF_ERR_ARGUMENT, "mesh_edges: cells must be 16-byte aligned");
+  if (workspace_bytes < sf::mesh_edges_workspace_bytes(n_slots))
+    return fail(SF_ERR_CAPACITY, "mesh_edges: workspace of %zu bytes, %zu needed", workspace_bytes,
+                sf::mesh_edges_workspace_bytes(n_slots));
+  return cuda_status(sf::mesh_edges(points, n_points, cells, n_cells, inside, slot_offsets, n_slots, edge_ids, pairs,
+                                    low, high, low_inside, n_edges, workspace, workspace_bytes, as_stream(stream)),
+                     "mesh_edges");
+}
+
+int sf_b200_mesh_midpoints(const double* low, const double* high, int64_t n_edges, double* midpoints, void* stream) {
+  if (n_edges < 0) return fail(SF_ERR_ARGUMENT, "mesh_midpoints: negative size");
+  if (n_edges > 0 && (!low || !high || !midpoints)) return fail(SF_ERR_ARGUMENT, "mesh_midpoints: NULL buffer");
+  return cuda_status(sf::mesh_midpoints(low, high, n_edges, midpoints, as_stream(stream)), "mesh_midpoints");
+}
+
+int sf_b200_mesh_bisect(double* low, double* high, const uint8_t* low_inside, int64_t n_edges, const double* values,
+                        double level, int32_t inside_greater, void* stream) {
+  if (n_edges < 0) return fail(SF_ERR_ARGUMENT, "mesh_bisect: negative size");
+  if (n_edges > 0 && (!low || !high || !low_inside || !values)) return fail(SF_ERR_ARGUMENT, "mesh_bisect: NULL buffer");
+  return cuda_status(sf::mesh_bisect(low, high, low_inside, n_edges, values, level, inside_greater != 0,
+                                     as_stream(stream)),
+                     "mesh_bisect");
+}
+
+int sf_b200_mesh_faces_workspace_bytes(int64_t n_faces, size_t* bytes) {
+  if (n_faces < 0 || !bytes) return fail(SF_ERR_ARGUMENT, "mesh_faces_workspace_bytes: bad arguments");
+  *bytes = sf::mesh_faces_workspace_bytes(n_faces);
+  return SF_OK;
+}
+
+int sf_b200_mesh_faces(const double* points, const int32_t* cells, int64_t n_cells, const uint8_t* inside,
+                       const int64_t* slot_offsets, const int32_t* edge_ids, const double* low, const double* high,
+                       int64_t n_edges, const int64_t* face_offsets, int64_t n_faces, double* vertices,
+                       int64_t* faces, int64_t* n_kept, void* workspace, size_t workspace_bytes, void* stream) {
+  if (n_cells < 0 || n_edges < 0 || n_faces < 0 || !n_kept) return fail(SF_ERR_ARGUMENT, "mesh_faces: bad arguments");
+  if (n_edges > 0 && (!low || !high || !vertices)) return fail(SF_ERR_ARGUMENT, "mesh_faces: NULL buffer");
+  if (n_faces > 0 && (!points || !cells || !inside || !slot_offsets || !edge_ids || !face_offsets || !faces ||
+                      !workspace))
+    return fail(SF_ERR_ARGUMENT, "mesh_faces: NULL buffer");
+  if (reinterpret_cast<uintptr_t>(cells) % 16) return fail(SF_ERR_ARGUMENT, "mesh_faces: cells must be 16-byte aligned");
+  if (workspace_bytes < sf::mesh_faces_workspace_bytes(n_faces))
+    return fail(SF_ERR_CAPACITY, "mesh_faces: workspace of %zu bytes, %zu needed", workspace_bytes,
+                sf::mesh_faces_workspace_bytes(n_faces));
+  return cuda_status(sf::mesh_faces(points, cells, n_cells, inside, slot_offsets, edge_ids, low, high, n_edges,
+                                    face_offsets, n_faces, vertices, faces, n_kept, workspace, workspace_bytes,
+                                    as_stream(stream)),
+                     "mesh_faces");
+}
+
 }  // extern "C"

@@ -141,4 +141,25 @@ cudaError_t scan_counts(const int32_t* in, int64_t n, int64_t* out, void* ws, si
                         cudaStream_t s);
 size_t scan_workspace_bytes(int64_t n);
 
+// GOF mesh extraction (meshing.cu)
+cudaError_t launch_grid_points(const float* means, const float* quats, const float* scales, const int32_t* chosen,
+                               int64_t n, double extent, double* points, double* radius, cudaStream_t s);
+size_t mesh_count_workspace_bytes(int64_t n_cells);
+cudaError_t mesh_count(const double* values, int64_t n_points, const int32_t* cells, int64_t n_cells, double level,
+                       int greater, uint8_t* inside, int64_t* slot_off, int64_t* face_off, void* ws,
+                       size_t ws_bytes, cudaStream_t s);
+size_t mesh_edges_workspace_bytes(int64_t n_slots);
+cudaError_t mesh_edges(const double* points, int64_t n_points, const int32_t* cells, int64_t n_cells,
+                       const uint8_t* inside, const int64_t* slot_off, int64_t n_slots, int32_t* edge_uid,
+                       int32_t* pairs, double* low, double* high, uint8_t* low_inside, int64_t* n_unique,
+                       void* ws, size_t ws_bytes, cudaStream_t s);
+cudaError_t mesh_midpoints(const double* low, const double* high, int64_t n_edges, double* mid, cudaStream_t s);
+cudaError_t mesh_bisect(double* low, double* high, const uint8_t* low_inside, int64_t n_edges, const double* values,
+                        double level, int greater, cudaStream_t s);
+size_t mesh_faces_workspace_bytes(int64_t n_faces);
+cudaError_t mesh_faces(const double* points, const int32_t* cells, int64_t n_cells, const uint8_t* inside,
+                       const int64_t* slot_off, const int32_t* edge_uid, const double* low, const double* high,
+                       int64_t n_edges, const int64_t* face_off, int64_t n_faces, double* vertices, int64_t* faces,
+                       int64_t* n_kept, void* ws, size_t ws_bytes, cudaStream_t s);
+
 }  // namespace sf

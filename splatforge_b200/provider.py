@@ -166,3 +166,14 @@ def register_renderer(registry=None, name="b200"):
         from splatforge.studio.renderers import renderers as registry
     registry.register(name, b200_factory)
     return registry
+
+
+def register_exporter(registry=None, name="b200-gof"):
+    """Add the device GOF exporter to a ``ComponentRegistry`` (default: Studio's
+    ``exporters``, src/splatforge/studio/exporters.py:264-266)."""
+    if registry is None:
+        from splatforge.studio.exporters import exporters as registry
+    from .meshing import B200GOFExporter
+
+    registry.register(name, B200GOFExporter)
+    return registry

@@ -16,6 +16,10 @@ Fixtures (all float32 unless noted):
                        random cases: bounds in, CSR tile lists out (int64).
 * ``geometry.npz``  -- pixel_rays@1, ray_peak@1, depth_normals@1 (with the depth
                        adjoint of a seeded loss on the normals).
+* ``mesh.npz``      -- marching_tetrahedra on an analytic plane (the reference's own
+                       test case) and sphere, and the GOF exporter's gaussian_grid
+                       (with and without max_gaussians) plus the level set of the
+                       opacity field of a 300-Gaussian scene (float64 grid).
 * ``ops.npz``       -- covariance@1, sh_color@1 (deg 0..3), pixel_rays@1,
                        ray_peak@1, alpha_composite@3 (all profiles, with input
                        gradients), opacity_field@1.
@@ -188,6 +192,70 @@ def geometry_cases():
     np.savez_compressed(HERE / "geometry.npz", **out)
 
 
+def mesh_cases():
+    """marching_tetrahedra on analytic fields, and the GOF exporter's extraction
+    (gaussian_grid, opacity_field@1 at every grid and bisection point,
+    marching_tetrahedra) of a 300-Gaussian surface scene seen from 4 origins."""
+    from types import SimpleNamespace
+
+    from splatforge.gaussian import SurfaceOperators
+    from splatforge.mesh.tetrahedra import marching_tetrahedra, triangulate
+    from splatforge.studio.exporters import gaussian_grid
+    from splatforge_b200 import scenes
+
+    out = {}
+    # the reference's analytic-plane case (tests/integration/test_surface_studio.py:108-128)
+    cube = np.asarray([[x, y, z] for x in (-1.0, 1.0) for y in (-1.0, 1.0) for z in (-1.0, 1.0)])
+
+    def plane(p):
+        return p[:, 2] - 0.25
+
+    cells = triangulate(cube)
+    v, f = marching_tetrahedra(cube, cells, plane(cube), plane, binary_steps=12, inside_greater=False)
+    out.update({"plane/points": cube, "plane/cells": cells, "plane/vertices": v, "plane/faces": f})
+
+    # a sphere level set over a radius-filtered Delaunay grid of seeded points
+    rng = np.random.default_rng(5)
+    pts = rng.uniform(-1.0, 1.0, (400, 3))
+    radii = rng.uniform(0.3, 0.6, 400)
+
+    def sphere(p):
+        return np.sqrt((p * p).sum(-1)) - 0.55
+
+    cells = triangulate(pts, radii)
+    v, f = marching_tetrahedra(pts, cells, sphere(pts), sphere, level=0.0, binary_steps=8, inside_greater=False)
+    out.update({"sphere/points": pts, "sphere/radii": radii, "sphere/cells": cells, "sphere/vertices": v,
+                "sphere/faces": f})
+
+    # GOF extraction
+    params = scenes.surfaces(300, seed=4)
+    view = scenes.activated(params)
+    model = SimpleNamespace(means=view.means, quats=view.quats, scales=view.scales, opacities=view.opacities,
+                            device=torch.device("cpu"))
+    ops = SurfaceOperators()
+    inverse = torch.linalg.inv(ops("gaussian.covariance@1", view.quats, view.scales))
+    g = torch.Generator().manual_seed(17)
+    d = torch.randn(4, 3, generator=g)
+    origins = 3.0 * d / d.norm(dim=-1, keepdim=True)
+
+    def field(coordinates):
+        sample = torch.as_tensor(coordinates, dtype=torch.float32)
+        return ops("gaussian.opacity_field@1", sample, view.means, inverse, view.opacities, origins,
+                   gaussian_chunk=512).numpy()
+
+    for tag, cap in (("gof", None), ("gof_cap", 120)):
+        config = SimpleNamespace(seed_opacity_min=0.05, max_gaussians=cap, tetra_extent=3.0)
+        points, cells, seeds = gaussian_grid(model, config)
+        out.update({f"{tag}/points": points, f"{tag}/cells": cells, f"{tag}/seeds": np.int64(seeds)})
+    points, cells = out["gof/points"], out["gof/cells"]
+    values = field(points)
+    v, f = marching_tetrahedra(points, cells, values, field, level=0.5, binary_steps=8, inside_greater=True)
+    out.update({"gof/means": view.means.numpy(), "gof/quats": view.quats.numpy(), "gof/scales": view.scales.numpy(),
+                "gof/opacities": view.opacities.numpy(), "gof/inverse": inverse.numpy(),
+                "gof/origins": origins.numpy(), "gof/values": values, "gof/vertices": v, "gof/faces": f})
+    np.savez_compressed(HERE / "mesh.npz", **out)
+
+
 CHANNELS = ("rgb", "alpha", "depth", "normals", "distortion_l1", "distortion_l2",
             "median_depth", "ray_color", "ambiguity_mask")
 
@@ -292,13 +360,15 @@ def render_cases():
 
 if __name__ == "__main__":
     _setup(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
-    which = sys.argv[2:] or ["binning", "ops", "geometry", "render"]
+    which = sys.argv[2:] or ["binning", "ops", "geometry", "mesh", "render"]
     if "binning" in which:
         binning_cases()
     if "ops" in which:
         op_cases()
     if "geometry" in which:
         geometry_cases()
+    if "mesh" in which:
+        mesh_cases()
     if "render" in which:
         render_cases()
     for f in sorted(HERE.glob("*.npz")):

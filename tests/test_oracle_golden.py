@@ -149,3 +149,63 @@ def test_geometry_ops_match_reference_fixture(golden):
     np.testing.assert_allclose(normals.detach().numpy(), f["dn/normals"], atol=1e-6)
     (gd,) = torch.autograd.grad((normals * torch.from_numpy(f["dn/up"])).sum(), depth)
     np.testing.assert_allclose(gd.numpy(), f["dn/gdepth"], rtol=1e-4, atol=1e-5)
+
+
+def test_mesh_oracle_matches_reference_marching_tetrahedra(golden):
+    """Analytic plane (the reference's own case) and sphere: same cells, vertices and
+    faces (order and orientation included) as tetrahedra.py produced."""
+    from oracle import meshing
+
+    f = golden("mesh")
+
+    def plane(p):
+        return p[:, 2] - 0.25
+
+    pts = f["plane/points"]
+    cells = meshing.triangulate(pts)
+    np.testing.assert_array_equal(cells, f["plane/cells"])
+    v, fc = meshing.marching_tetrahedra(pts, cells, plane(pts), plane, binary_steps=12, inside_greater=False)
+    np.testing.assert_array_equal(v, f["plane/vertices"])
+    np.testing.assert_array_equal(fc, f["plane/faces"])
+
+    def sphere(p):
+        return np.sqrt((p * p).sum(-1)) - 0.55
+
+    pts = f["sphere/points"]
+    cells = meshing.triangulate(pts, f["sphere/radii"])
+    np.testing.assert_array_equal(cells, f["sphere/cells"])
+    v, fc = meshing.marching_tetrahedra(pts, cells, sphere(pts), sphere, level=0.0, binary_steps=8,
+                                        inside_greater=False)
+    np.testing.assert_array_equal(v, f["sphere/vertices"])
+    np.testing.assert_array_equal(fc, f["sphere/faces"])
+
+
+@pytest.mark.parametrize("tag,cap", [("gof", None), ("gof_cap", 120)])
+def test_mesh_oracle_grid_matches_reference_gaussian_grid(golden, tag, cap):
+    from oracle import meshing
+
+    f = golden("mesh")
+    pts, radius, seeds = meshing.grid(f["gof/means"], f["gof/quats"], f["gof/scales"], f["gof/opacities"],
+                                      max_gaussians=cap)
+    assert seeds == int(f[f"{tag}/seeds"])
+    np.testing.assert_allclose(pts, f[f"{tag}/points"], rtol=0, atol=1e-12)
+    np.testing.assert_array_equal(meshing.triangulate(f[f"{tag}/points"], radius), f[f"{tag}/cells"])
+
+
+def test_mesh_oracle_gof_level_set_matches_reference(golden):
+    """The GOF extraction with the oracle's opacity field: the field at the grid points
+    within 1e-6, then the same vertices and faces."""
+    from oracle import meshing
+
+    f = golden("mesh")
+    args = [torch.from_numpy(f[f"gof/{k}"]) for k in ("means", "inverse", "opacities", "origins")]
+
+    def field(p):
+        return ops.opacity_field(torch.as_tensor(p, dtype=torch.float32), *args).numpy()
+
+    pts, cells = f["gof/points"], f["gof/cells"]
+    values = field(pts)
+    np.testing.assert_allclose(values, f["gof/values"], atol=1e-6)
+    v, fc = meshing.marching_tetrahedra(pts, cells, values, field, level=0.5, binary_steps=8, inside_greater=True)
+    np.testing.assert_array_equal(fc, f["gof/faces"])
+    np.testing.assert_array_equal(v, f["gof/vertices"])

@@ -112,3 +112,19 @@ def test_geometry_ops_and_the_culled_field_register():
                                    torch.randn(2, 3, device="meta"), policy=allowed)
     cand = [c for c in exp.candidates if c.implementation_id == culled][0]
     assert "host_synchronization_forbidden" not in cand.reasons
+
+
+def test_device_gof_exporter_registers():
+    """``b200-gof`` joins an exporter registry beside the reference's ``gof``
+    (exporters.py:264-266) and exposes the same ``export(pipeline, path, config)`` call."""
+    from splatforge.studio.exporters import GOFExporter
+
+    from splatforge_b200.meshing import B200GOFExporter
+
+    reg = ComponentRegistry("splatforge.exporters.test")
+    reg.register("gof", GOFExporter)
+    provider.register_exporter(reg)
+    assert reg.get("b200-gof") is B200GOFExporter
+    assert callable(reg.get("b200-gof")().export)
+    with pytest.raises(ValueError):
+        provider.register_exporter(reg)  # duplicate names raise (plugins.py:14-18)
