@@ -11,6 +11,8 @@ parallelism).  ``value`` = all ranks' rendered pixels / max-over-ranks step time
 ``--workload surfaces3m_views64`` runs the view-batched training step instead: 3M
 Gaussians, 8 views of 1600x1064 per GPU per step (8/16/32/64 views at 1/2/4/8 GPUs),
 gradients accumulated over the views, then one all-reduce of the [N,59] buffer.
+``--workload field2m_views32`` times the GOF opacity field (queries/s) and
+``--workload mesh100k_views32`` the GOF mesh extraction (tetrahedra/s).
 
     python bench.py [--gpus N --steps K --warmup W]          # B200 arm
     python bench.py --impl reference [...]                     # CPU arm (oracle port)
@@ -432,6 +434,173 @@ def field_cpu_baseline(host, budget_s=15.0):
                       f"{m.shape[0]} Gaussians; linear in queries and origins, scaled to {org.shape[0]} origins"}
 
 
+MESH_WORKLOADS = {"mesh100k_views32"}
+
+
+class MeshJob:
+    """GOF level-set extraction of the exporter (src/splatforge/studio/exporters.py:41-88)
+    on a fixed tetrahedral grid: the seed Gaussians' grid and its Delaunay cells are built
+    once (host Qhull, untimed); a step builds the culled field plan (every view's
+    candidate lists), evaluates the field at every grid point and runs marching
+    tetrahedra with 8 bisection steps (8 more field evaluations over the crossing edges)
+    to the vertices and faces."""
+
+    def __init__(self, workload, dev):
+        from splatforge_b200 import meshing, scenes
+
+        params, cams = scenes.workload(workload, seed=0)
+        view = scenes.activated(params)
+        self.n = params.means.shape[0]
+        self.host = {"means": view.means.contiguous().pin_memory(), "quats": view.quats.contiguous().pin_memory(),
+                     "scales": view.scales.contiguous().pin_memory(),
+                     "opac": view.opacities.contiguous().pin_memory(),
+                     "Q": scenes.inverse_covariances(params).contiguous().pin_memory(),
+                     "origins": torch.stack([c.origin for c in cams]).contiguous().pin_memory()}
+        self.d = {k: v.to(dev) for k, v in self.host.items()}
+        t0 = time.perf_counter()
+        points, cells, self.seeds = meshing.gaussian_grid(self.d["means"], self.d["quats"], self.d["scales"],
+                                                          self.d["opac"])
+        self.grid_seconds = time.perf_counter() - t0
+        self.points_host, self.cells_host = points, cells
+        self.points = torch.as_tensor(points, device=dev)
+        self.cells = torch.as_tensor(cells, device=dev).to(torch.int32)
+        self.queries = 0
+        self.meshing = meshing
+
+    def field(self, coordinates):
+        self.queries += coordinates.shape[0]
+        return self.plan(coordinates.to(torch.float32).contiguous())
+
+    def step(self):
+        from splatforge_b200 import ops
+
+        d = self.d
+        self.plan = ops.OpacityFieldPlan(d["means"], d["Q"], d["opac"], d["origins"])
+        return self.meshing.marching_tetrahedra(self.points, self.cells, self.field(self.points), self.field,
+                                                level=0.5, binary_steps=8)
+
+
+def run_mesh(args):
+    """Replicas: every rank extracts the same level set (the extraction's bisection
+    steps depend on each other's results, so the path does not shard); value = ranks x
+    tetrahedra / max-over-ranks step time."""
+    import torch.distributed as dist
+
+    from splatforge_b200 import distributed, rasterizer
+
+    rank, world, local = distributed.init_from_env(backend="nccl", timeout_s=600)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    job = MeshJob(args.workload, dev)
+    for _ in range(args.warmup):
+        verts, faces = job.step()
+    torch.cuda.synchronize()
+    launches0 = rasterizer.kernel_launches()
+    job.queries = 0
+    clocks = ClockSampler(local).start() if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        verts, faces = job.step()
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop() if clocks else None
+    launches = rasterizer.kernel_launches() - launches0
+    queries = job.queries // args.steps
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    n_cells = job.cells.shape[0]
+
+    # end to end: the scene and the grid from pinned host memory, the mesh back to the host
+    pts_pinned = job.points.cpu().pin_memory()
+    cells_pinned = job.cells.cpu().pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in job.host.values()) + pts_pinned.numel() * 8 + cells_pinned.numel() * 4
+    d2h = 0
+    if world > 1:
+        dist.barrier()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    for _ in range(args.steps):
+        for k, v in job.host.items():
+            job.d[k].copy_(v, non_blocking=True)
+        job.points.copy_(pts_pinned, non_blocking=True)
+        job.cells.copy_(cells_pinned, non_blocking=True)
+        verts, faces = job.step()
+        vh, fh = verts.cpu(), faces.cpu()
+        d2h = vh.numel() * 8 + fh.numel() * 8
+    a1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([a0.elapsed_time(a1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    ems = float(te.item())
+    result = None
+    if rank == 0:
+        result = {
+            "metric": "GOF mesh extraction tetrahedra/s (100k Gaussians, 32 views, 8 bisection steps)",
+            "value": round(n_cells * world / (ms * 1e-3), 1), "unit": "tetrahedra/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64 (grid, bisection) / f32 (field)",
+            "data": "synthetic (seeded surface-sampled scene, exporter grid)",
+            "config": {"workload": f"{args.workload}: {job.n} Gaussians ({job.seeds} seeds), "
+                                   f"{len(job.points_host)} grid points, {n_cells} tetrahedra, "
+                                   f"{job.d['origins'].shape[0]} origins, level 0.5",
+                       "parallelism": f"{world} replicas" if world > 1 else "single GPU",
+                       "field_queries_per_step": int(queries), "vertices": int(verts.shape[0]),
+                       "faces": int(faces.shape[0]),
+                       "untimed_setup": f"grid points (device) + dedup and Delaunay (host Qhull) "
+                                        f"{job.grid_seconds:.1f} s"},
+            "gpu_launches": int(launches), "clocks": clk,
+            "e2e": {"value": round(n_cells * world / (ems * 1e-3), 1), "unit": "tetrahedra/s",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": round(ems, 3)},
+            "roofline": None,
+            "cpu_baseline": mesh_cpu_baseline(job) if world == 1 and not args.no_cpu_baseline else None,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def mesh_cpu_baseline(job, field_budget_s=10.0):
+    """The oracle on the host cores: its marching tetrahedra over the full grid, timed
+    with the field values replayed from the device run (the oracle's bisection points
+    are the device's, bit for bit), plus the oracle field's measured cost per query
+    times the queries one extraction evaluates."""
+    import numpy as np
+
+    from oracle import meshing as oracle_meshing
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    recorded = []
+
+    def record(c):
+        v = job.field(c)
+        recorded.append(v.double().cpu().numpy())
+        return v
+
+    job.meshing.marching_tetrahedra(job.points, job.cells, record(job.points), record, level=0.5, binary_steps=8)
+    replay = iter(recorded[1:])
+    t0 = time.perf_counter()
+    oracle_meshing.marching_tetrahedra(job.points_host, job.cells_host, recorded[0], lambda p: next(replay),
+                                       level=0.5, binary_steps=8)
+    marching_s = time.perf_counter() - t0
+    n_queries = sum(len(r) for r in recorded)
+    field = field_cpu_baseline({"pts": job.points.float().cpu(), "means": job.host["means"], "Q": job.host["Q"],
+                                "opac": job.host["opac"], "origins": job.host["origins"]}, budget_s=field_budget_s)
+    field_s = n_queries / field["value"] if field["value"] else float("inf")
+    total = marching_s + field_s
+    return {"value": round(job.cells.shape[0] / total, 3), "unit": "tetrahedra/s", "cores": threads, "kind": "port",
+            "sample": f"oracle marching over all {job.cells.shape[0]} tetrahedra ({marching_s:.1f} s, field values "
+                      f"replayed) + oracle field at {field['value']:.2f} queries/s x {n_queries} queries "
+                      f"({field_s:.0f} s, extrapolated from {field['sample']})"}
+
+
 def settings_config(settings):
     from types import SimpleNamespace
 
@@ -569,12 +738,47 @@ def run_reference(args):
     }
 
 
+def run_reference_field(args):
+    """The reference arm of the field workload: the oracle field on the host cores, one
+    bounded (query, origin) sample per step; value = median rate."""
+    from splatforge_b200 import scenes
+
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return None
+    params, cams = scenes.workload(args.workload, seed=0)
+    view = scenes.activated(params)
+    host = {"pts": scenes.field_queries(params, 2_000_000, seed=0)[:4096], "means": view.means,
+            "Q": scenes.inverse_covariances(params), "opac": view.opacities,
+            "origins": torch.stack([c.origin for c in cams])}
+    for _ in range(args.warmup):
+        field_cpu_baseline(host, budget_s=0.5)
+    runs = [field_cpu_baseline(host, budget_s=5.0) for _ in range(args.steps)]
+    value = sorted(r["value"] for r in runs)[len(runs) // 2]
+    return {"impl": "reference", "metric": "GOF opacity-field queries/s (2M Gaussians, 32 views)", "value": value,
+            "unit": "queries/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 / value, 1) if value else None, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded surface-sampled scene)",
+            "config": {"workload": f"{args.workload}: {params.means.shape[0]} Gaussians, {len(cams)} origins"},
+            "cpu_baseline": {**runs[len(runs) // 2], "value": value},
+            "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.impl == "reference" and args.workload in FIELD_WORKLOADS:
+        res = run_reference_field(args)
+    elif args.impl == "reference" and args.workload in MESH_WORKLOADS:
+        res = None if dist_env()[0] else {
+            "impl": "reference",
+            "unavailable": "the oracle field would need days per extraction at this size on the host; the "
+                           "B200 line's cpu_baseline gives the oracle's marching time plus its sampled field cost"}
+    elif args.impl == "reference":
         res = run_reference(args)
     elif args.workload in FIELD_WORKLOADS:
         res = run_field(args)
+    elif args.workload in MESH_WORKLOADS:
+        res = run_mesh(args)
     else:
         res = run_b200(args)
     if res is not None:

@@ -235,6 +235,32 @@ int sf_b200_opacity_field_culled(const float* points, int64_t n_points, const fl
                                  size_t workspace_bytes, int64_t max_pairs, int64_t* pairs_needed,
                                  void* stream);
 
+/* A field plan for repeated evaluations against one Gaussian set and one origin set
+ * (the GOF exporter evaluates the grid and then every bisection step against the same
+ * scene, exporters.py:56-88): plan_build bins every view's Gaussians as
+ * sf_b200_opacity_field_culled does and keeps all views' candidate lists in `plan`
+ * (synchronises once per origin); plan_eval then evaluates a query set for all views
+ * with one sort of its (view, cell) keys and no host synchronisation.  The values equal
+ * sf_b200_opacity_field_culled's.  total_pairs and max_view_pairs size the lists: if
+ * the scene needs more (needed[0] = all views' pairs, needed[1] = the largest view's,
+ * host int64[2]) plan_build returns SF_ERR_CAPACITY and the caller retries.  plan_eval
+ * takes the plan's sizes and origins again, and n_points * n_origins < 2^31. */
+int sf_b200_opacity_field_plan_bytes(int64_t n_gaussians, int32_t n_origins, int32_t face_cells,
+                                     int64_t total_pairs, int64_t max_view_pairs, size_t* bytes);
+int sf_b200_opacity_field_plan_build(const float* means, const float* inverse_covariances,
+                                     const float* opacities, int64_t n_gaussians,
+                                     const float* origins, int32_t n_origins, float cutoff,
+                                     int32_t face_cells, void* plan, size_t plan_bytes,
+                                     int64_t total_pairs, int64_t max_view_pairs,
+                                     int64_t* needed, void* stream);
+int sf_b200_opacity_field_plan_query_bytes(int64_t n_points, int32_t n_origins, int32_t face_cells,
+                                           size_t* bytes);
+int sf_b200_opacity_field_plan_eval(const void* plan, int64_t n_gaussians, int32_t n_origins,
+                                    int32_t face_cells, int64_t total_pairs, int64_t max_view_pairs,
+                                    const float* origins, const float* points, int64_t n_points,
+                                    float* field, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
 /* ---- small geometry operators -------------------------------------------------
  * camera.pixel_rays@1 (reference.py:49-56): K [3,3] -> rays [height, width, 3].
  * gaussian.ray_peak@1 (reference.py:38-46): means [N,3], inverse_covariances [N,3,3],

@@ -99,6 +99,14 @@ _SIGNATURES = {
         ctypes.c_int,
         [P, c_int64, P, P, P, c_int64, P, c_int32, c_float, c_int32, P, P, c_size_t, c_int64, POINTER(c_int64), P],
     ),
+    "sf_b200_opacity_field_plan_bytes": (ctypes.c_int, [c_int64, c_int32, c_int32, c_int64, c_int64, POINTER(c_size_t)]),
+    "sf_b200_opacity_field_plan_build": (
+        ctypes.c_int, [P, P, P, c_int64, P, c_int32, c_float, c_int32, P, c_size_t, c_int64, c_int64, P, P]
+    ),
+    "sf_b200_opacity_field_plan_query_bytes": (ctypes.c_int, [c_int64, c_int32, c_int32, POINTER(c_size_t)]),
+    "sf_b200_opacity_field_plan_eval": (
+        ctypes.c_int, [P, c_int64, c_int32, c_int32, c_int64, c_int64, P, P, c_int64, P, P, c_size_t, P]
+    ),
     "sf_b200_pixel_rays": (ctypes.c_int, [P, c_int32, c_int32, P, P]),
     "sf_b200_ray_peak": (ctypes.c_int, [P, P, c_int64, P, P, c_int64, P, P, P, P]),
     "sf_b200_depth_normals": (ctypes.c_int, [P, P, c_int32, c_int32, P, P, P]),

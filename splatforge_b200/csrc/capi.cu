@@ -363,6 +363,72 @@ int sf_b200_opacity_field_culled(const float* points, int64_t n_points, const fl
   return SF_OK;
 }
 
+int sf_b200_opacity_field_plan_bytes(int64_t n_gaussians, int32_t n_origins, int32_t face_cells, int64_t total_pairs,
+                                     int64_t max_view_pairs, size_t* bytes) {
+  if (n_gaussians < 0 || n_origins < 1 || face_cells < 1 || face_cells > 1024 || total_pairs < 0 ||
+      max_view_pairs < 0 || !bytes)
+    return fail(SF_ERR_ARGUMENT, "opacity_field_plan_bytes: bad arguments");
+  *bytes = sf::field_plan_bytes(n_gaussians, n_origins, face_cells, total_pairs, max_view_pairs);
+  return SF_OK;
+}
+
+int sf_b200_opacity_field_plan_build(const float* means, const float* inverse_covariances, const float* opacities,
+                                     int64_t n_gaussians, const float* origins, int32_t n_origins, float cutoff,
+                                     int32_t face_cells, void* plan, size_t plan_bytes, int64_t total_pairs,
+                                     int64_t max_view_pairs, int64_t* needed, void* stream) {
+  if (n_gaussians < 0 || total_pairs < 0 || max_view_pairs < 0 || !needed)
+    return fail(SF_ERR_ARGUMENT, "opacity_field_plan_build: bad arguments");
+  if (n_origins < 1) return fail(SF_ERR_ARGUMENT, "opacity_field_plan_build: requires at least one origin");
+  if (!(cutoff > 0.f && cutoff < 1.f)) return fail(SF_ERR_ARGUMENT, "opacity_field_plan_build: cutoff must be in (0, 1)");
+  if (face_cells < 1 || face_cells > 1024) return fail(SF_ERR_ARGUMENT, "opacity_field_plan_build: face_cells in 1..1024");
+  if (!origins || !plan || (n_gaussians > 0 && (!means || !inverse_covariances || !opacities)))
+    return fail(SF_ERR_ARGUMENT, "opacity_field_plan_build: NULL buffer");
+  if (n_gaussians > INT32_MAX || total_pairs > INT64_C(1) << 40 || max_view_pairs > ((int64_t)1 << 31))
+    return fail(SF_ERR_ARGUMENT, "opacity_field_plan_build: index range exceeded");
+  const size_t need = sf::field_plan_bytes(n_gaussians, n_origins, face_cells, total_pairs, max_view_pairs);
+  if (plan_bytes < need)
+    return fail(SF_ERR_CAPACITY, "opacity_field_plan_build: plan of %zu bytes, %zu needed", plan_bytes, need);
+  const int rc = cuda_status(sf::field_plan_build(means, inverse_covariances, opacities, n_gaussians, origins, n_origins,
+                                                  cutoff, face_cells, plan, plan_bytes, total_pairs, max_view_pairs,
+                                                  needed, as_stream(stream)),
+                             "opacity_field_plan_build");
+  if (rc != SF_OK) return rc;
+  if (needed[0] > total_pairs || needed[1] > max_view_pairs)
+    return fail(SF_ERR_CAPACITY, "opacity_field_plan_build: %lld candidate pairs (%lld in one view) exceed %lld (%lld)",
+                (long long)needed[0], (long long)needed[1], (long long)total_pairs, (long long)max_view_pairs);
+  return SF_OK;
+}
+
+int sf_b200_opacity_field_plan_query_bytes(int64_t n_points, int32_t n_origins, int32_t face_cells, size_t* bytes) {
+  if (n_points < 0 || n_origins < 1 || face_cells < 1 || face_cells > 1024 || !bytes)
+    return fail(SF_ERR_ARGUMENT, "opacity_field_plan_query_bytes: bad arguments");
+  if (n_points * n_origins > INT32_MAX)
+    return fail(SF_ERR_CAPACITY, "opacity_field_plan_query_bytes: %lld (query, origin) pairs exceed 2^31 - 1",
+                (long long)(n_points * n_origins));
+  *bytes = sf::field_plan_query_bytes(n_points, n_origins, face_cells);
+  return SF_OK;
+}
+
+int sf_b200_opacity_field_plan_eval(const void* plan, int64_t n_gaussians, int32_t n_origins, int32_t face_cells,
+                                    int64_t total_pairs, int64_t max_view_pairs, const float* origins,
+                                    const float* points, int64_t n_points, float* field, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  if (n_gaussians < 0 || n_points < 0 || n_origins < 1 || face_cells < 1 || face_cells > 1024 || total_pairs < 0 ||
+      max_view_pairs < 0)
+    return fail(SF_ERR_ARGUMENT, "opacity_field_plan_eval: bad arguments");
+  if (n_points * n_origins > INT32_MAX)
+    return fail(SF_ERR_CAPACITY, "opacity_field_plan_eval: %lld (query, origin) pairs exceed 2^31 - 1",
+                (long long)(n_points * n_origins));
+  if (n_points > 0 && (!plan || !origins || !points || !field || !workspace))
+    return fail(SF_ERR_ARGUMENT, "opacity_field_plan_eval: NULL buffer");
+  const size_t need = sf::field_plan_query_bytes(n_points, n_origins, face_cells);
+  if (workspace_bytes < need)
+    return fail(SF_ERR_CAPACITY, "opacity_field_plan_eval: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+  return cuda_status(sf::field_plan_eval(plan, n_gaussians, n_origins, face_cells, total_pairs, max_view_pairs, origins,
+                                         points, n_points, field, workspace, workspace_bytes, as_stream(stream)),
+                     "opacity_field_plan_eval");
+}
+
 int sf_b200_pixel_rays(const float* K, int32_t width, int32_t height, float* rays, void* stream) {
   if (width <= 0 || height <= 0) return fail(SF_ERR_ARGUMENT, "pixel_rays: width and height must be positive");
   if (!K || !rays) return fail(SF_ERR_ARGUMENT, "pixel_rays: NULL buffer");

@@ -12,6 +12,8 @@
 // of 1 for that view).
 #include <cuda_runtime.h>
 
+#include <vector>
+
 #include "sf_device.cuh"
 #include "sf_kernels.h"
 
@@ -299,6 +301,78 @@ __global__ void cfield_chunks_kernel(const int2* qranges, int ncells, int32_t* c
   chunks[c] = (r.y - r.x + CF_THREADS - 1) / CF_THREADS;
 }
 
+// One (cell, chunk) work item: queries qidx[q0 .. min(q0 + CF_THREADS, q1)) walk the
+// cell's front-to-back candidates cell_ids[cr.x .. cr.y) after the view's global list.
+// Every barrier below is taken by the whole CTA (cr is uniform), so a CTA can run work
+// items one after another.
+//
+// The field is the minimum over views and a view's 1 - T only grows along the walk, so
+// a query stops as soon as 1 - T reaches the smallest value another view has already
+// stored for it (M, re-read per staged batch): what it then stores cannot lower the
+// minimum, and the view that attains the minimum is never stopped before reaching it.
+// The stored minimum is the same, bit for bit, as without this stop.
+__device__ __forceinline__ void field_chunk(const float* pts, const int32_t* qidx, int q0, int q1, float ox,
+                                            float oy, float oz, const float* rec, const float* near,
+                                            const int32_t* cell_ids, int2 cr, const int32_t* global_ids,
+                                            int64_t n_global, uint32_t* out, float4* s_g, float4* s_c,
+                                            float* s_near) {
+  const int tid = threadIdx.x;
+  const int qi = q0 + tid < q1 ? qidx[q0 + tid] : -1;
+  const volatile uint32_t* cur = reinterpret_cast<const volatile uint32_t*>(out);
+  float dx = 0.f, dy = 0.f, dz = 0.f, dist = 0.f, T = 1.f, M = 0.f;
+  bool stop = qi < 0;
+  if (!stop) {
+    M = __uint_as_float(cur[qi]);
+    dx = pts[(int64_t)qi * 3] - ox; dy = pts[(int64_t)qi * 3 + 1] - oy; dz = pts[(int64_t)qi * 3 + 2] - oz;
+    dist = sqrtf(dx * dx + dy * dy + dz * dz);
+    const float inv = 1.f / fmaxf(dist, 1e-12f);
+    dx *= inv; dy *= inv; dz *= inv;
+    for (int64_t k = 0; k < n_global && T >= 1e-7f && 1.f - T < M; ++k) {
+      const float4* g4 = reinterpret_cast<const float4*>(rec + (int64_t)global_ids[k] * CF_REC);
+      const float4 a = g4[0], b = g4[1], c = g4[2];
+      const float g[10] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y};
+      T *= 1.f - field_contribution(g, ox, oy, oz, dx, dy, dz, dist);
+    }
+    stop = T < 1e-7f || 1.f - T >= M;
+  }
+  for (int c0 = cr.x; c0 < cr.y; c0 += CF_THREADS) {
+    if (!stop) {
+      M = fminf(M, __uint_as_float(cur[qi]));
+      stop = 1.f - T >= M;
+    }
+    if (__syncthreads_count(stop) == CF_THREADS) break;
+    const int nc = min(CF_THREADS, cr.y - c0);
+    if (tid < nc) {
+      const int id = cell_ids[c0 + tid];
+      const float4* g4 = reinterpret_cast<const float4*>(rec + (int64_t)id * CF_REC);
+      const float4 a = g4[0];
+      s_g[tid * 3] = a;
+      s_g[tid * 3 + 1] = g4[1];
+      s_g[tid * 3 + 2] = g4[2];
+      s_near[tid] = near[id];
+      const float cx = a.x - ox, cy = a.y - oy, cz = a.z - oz;
+      s_c[tid] = make_float4(cx, cy, cz, cx * cx + cy * cy + cz * cz);
+    }
+    __syncthreads();
+    if (!stop) {
+      for (int k = 0; k < nc; ++k) {
+        // sorted front to back: this and every later ball start beyond the query
+        if (s_near[k] > dist) { stop = true; break; }
+        const float* g = reinterpret_cast<const float*>(&s_g[k * 3]);
+        // the ray misses the ball (squared distance of the mean from the ray's line
+        // above R^2, with a margin for the rounding of the difference): skip
+        const float4 c = s_c[k];
+        const float cd = c.x * dx + c.y * dy + c.z * dz;
+        const float R = g[10];
+        if (c.w - cd * cd > R * R * 1.002f + 1e-6f * c.w) continue;
+        T *= 1.f - field_contribution(g, ox, oy, oz, dx, dy, dz, dist);
+        if (T < 1e-7f || 1.f - T >= M) { stop = true; break; }
+      }
+    }
+  }
+  if (qi >= 0) atomicMin(out + qi, __float_as_uint(fmaxf(1.f - T, 0.f)));
+}
+
 // One CTA per (cell, chunk of CF_THREADS queries): work item w belongs to the cell c
 // with chunk_off[c] <= w < chunk_off[c + 1] (binary search), so a cell holding many
 // queries (a plane seen edge-on) spreads over many SMs.
@@ -316,60 +390,72 @@ __global__ void __launch_bounds__(CF_THREADS) cfield_cell_kernel(
     const int mid = (lo + hi + 1) >> 1;
     if (chunk_off[mid] <= w) lo = mid; else hi = mid - 1;
   }
-  const int cell = lo;
-  const int2 qr = qranges[cell];
-  const int2 cr = cell_ranges[cell];
-  const int tid = threadIdx.x;
-  {
-    const int q0 = qr.x + (int)(w - chunk_off[cell]) * CF_THREADS;
-    const int qi = q0 + tid < qr.y ? qidx[q0 + tid] : -1;
-    float dx = 0.f, dy = 0.f, dz = 0.f, dist = 0.f, T = 1.f;
-    bool stop = qi < 0;
-    if (!stop) {
-      dx = pts[(int64_t)qi * 3] - ox; dy = pts[(int64_t)qi * 3 + 1] - oy; dz = pts[(int64_t)qi * 3 + 2] - oz;
-      dist = sqrtf(dx * dx + dy * dy + dz * dz);
-      const float inv = 1.f / fmaxf(dist, 1e-12f);
-      dx *= inv; dy *= inv; dz *= inv;
-      for (int64_t k = 0; k < n_global && T >= 1e-7f; ++k) {
-        const float4* g4 = reinterpret_cast<const float4*>(rec + (int64_t)global_ids[k] * CF_REC);
-        const float4 a = g4[0], b = g4[1], c = g4[2];
-        const float g[10] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y};
-        T *= 1.f - field_contribution(g, ox, oy, oz, dx, dy, dz, dist);
-      }
-      stop = T < 1e-7f;
-    }
-    for (int c0 = cr.x; c0 < cr.y; c0 += CF_THREADS) {
-      if (__syncthreads_count(stop) == CF_THREADS) break;
-      const int nc = min(CF_THREADS, cr.y - c0);
-      if (tid < nc) {
-        const int id = cell_ids[c0 + tid];
-        const float4* g4 = reinterpret_cast<const float4*>(rec + (int64_t)id * CF_REC);
-        const float4 a = g4[0];
-        s_g[tid * 3] = a;
-        s_g[tid * 3 + 1] = g4[1];
-        s_g[tid * 3 + 2] = g4[2];
-        s_near[tid] = near[id];
-        const float cx = a.x - ox, cy = a.y - oy, cz = a.z - oz;
-        s_c[tid] = make_float4(cx, cy, cz, cx * cx + cy * cy + cz * cz);
-      }
-      __syncthreads();
-      if (!stop) {
-        for (int k = 0; k < nc; ++k) {
-          // sorted front to back: this and every later ball start beyond the query
-          if (s_near[k] > dist) { stop = true; break; }
-          const float* g = reinterpret_cast<const float*>(&s_g[k * 3]);
-          // the ray misses the ball (squared distance of the mean from the ray's line
-          // above R^2, with a margin for the rounding of the difference): skip
-          const float4 c = s_c[k];
-          const float cd = c.x * dx + c.y * dy + c.z * dz;
-          const float R = g[10];
-          if (c.w - cd * cd > R * R * 1.002f + 1e-6f * c.w) continue;
-          T *= 1.f - field_contribution(g, ox, oy, oz, dx, dy, dz, dist);
-          if (T < 1e-7f) { stop = true; break; }
-        }
-      }
-    }
-    if (qi >= 0) atomicMin(out + qi, __float_as_uint(fmaxf(1.f - T, 0.f)));
+  const int2 qr = qranges[lo];
+  field_chunk(pts, qidx, qr.x + (int)(w - chunk_off[lo]) * CF_THREADS, qr.y, ox, oy, oz, rec, near, cell_ids,
+              cell_ranges[lo], global_ids, n_global, out, s_g, s_c, s_near);
+}
+
+// ------------------------------------------------------------------ field plan
+// A plan holds every view's candidate lists (built once per Gaussian set and origin
+// set); an evaluation sorts its queries by (view, cell) in one pass and hands out
+// (view, cell, chunk) work items from a queue.
+
+// query i of view v: key v * (ncells + 1) + cell, ncells for a query at the origin
+// (whose field is 0 for that view, set here)
+__global__ void cfield_plan_qcell_kernel(const float* pts, int64_t np, const float* origins, int nc, int F,
+                                         uint32_t* qkey, int32_t* qidx, uint32_t* out) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= np * nc) return;
+  const int v = (int)(j / np);
+  const int64_t i = j - (int64_t)v * np;
+  const float dx = pts[i * 3] - origins[v * 3], dy = pts[i * 3 + 1] - origins[v * 3 + 1],
+              dz = pts[i * 3 + 2] - origins[v * 3 + 2];
+  const bool at_origin = !(dx * dx + dy * dy + dz * dz > 0.f);
+  const uint32_t cells = (uint32_t)(6 * F * F);
+  qkey[j] = (uint32_t)v * (cells + 1) + (at_origin ? cells : (uint32_t)cube_cell(dx, dy, dz, F));
+  qidx[j] = (int32_t)i;
+  if (at_origin) atomicMin(out + i, 0u);
+}
+
+// chunks of every (view, cell) key; the at-origin key of each view has none
+__global__ void cfield_plan_chunks_kernel(const int2* qranges, int64_t nkeys, int per_view, int32_t* chunks) {
+  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= nkeys) return;
+  const int2 r = qranges[k];
+  chunks[k] = (k % per_view == per_view - 1) ? 0 : (r.y - r.x + CF_THREADS - 1) / CF_THREADS;
+}
+
+// work item list: item chunk_off[k] + j is (key k, chunk j)
+__global__ void cfield_plan_items_kernel(const int64_t* chunk_off, int64_t nkeys, int32_t* item_key) {
+  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= nkeys) return;
+  for (int64_t w = chunk_off[k]; w < chunk_off[k + 1]; ++w) item_key[w] = (int32_t)k;
+}
+
+__global__ void __launch_bounds__(CF_THREADS) cfield_plan_kernel(
+    const float* pts, const int32_t* qidx, const int2* qranges, const int64_t* chunk_off, const int32_t* item_key,
+    int64_t nkeys, int per_view, const float* origins, const float* rec, const float* near, int64_t ng,
+    const int32_t* vals, const int2* cell_ranges, const int64_t* view_info, const int32_t* gids,
+    unsigned long long* queue, uint32_t* out) {
+  __shared__ float4 s_g[CF_THREADS * 3];
+  __shared__ float4 s_c[CF_THREADS];
+  __shared__ float s_near[CF_THREADS];
+  __shared__ long long s_w;
+  const long long total = chunk_off[nkeys];
+  const int ncells = per_view - 1;
+  for (;;) {
+    if (threadIdx.x == 0) s_w = (long long)atomicAdd(queue, 1ull);
+    __syncthreads();
+    const long long w = s_w;
+    __syncthreads();
+    if (w >= total) break;
+    const int k = item_key[w];
+    const int v = k / per_view, cell = k - v * per_view;
+    const int2 qr = qranges[k];
+    const int64_t base = view_info[v * 2], n_global = view_info[v * 2 + 1];
+    field_chunk(pts, qidx, qr.x + (int)(w - chunk_off[k]) * CF_THREADS, qr.y, origins[v * 3], origins[v * 3 + 1],
+                origins[v * 3 + 2], rec, near + (int64_t)v * ng, vals + base,
+                cell_ranges[(int64_t)v * ncells + cell], gids + (int64_t)v * ng, n_global, out, s_g, s_c, s_near);
   }
 }
 
@@ -546,6 +632,195 @@ cudaError_t launch_opacity_field_culled(const float* pts, int64_t np, const floa
   delete[] host_origins;
   if (pairs_needed) *pairs_needed = most;
   return e;
+}
+
+// ------------------------------------------------------------------ field plan
+namespace {
+
+struct PlanLayout {
+  float* rec; float* near; int32_t* gids; int32_t* ranges; int64_t* view_info; int32_t* vals;
+  // build scratch
+  int32_t* count; int32_t* gflag; int64_t* offs; int64_t* goffs; void* scan_ws; size_t scan_bytes;
+  uint32_t* dkey; int32_t* order; void* order_ws; size_t order_bytes; uint32_t* keys; void* sort_ws;
+  size_t sort_bytes;
+  size_t used;
+};
+
+PlanLayout plan_layout(void* base, int64_t ng, int nc, int F, int64_t total_pairs, int64_t max_view_pairs) {
+  PlanLayout L{};
+  char* p = reinterpret_cast<char*>(base);
+  size_t used = 0;
+  auto take = [&](size_t bytes) { char* r = p ? p + used : nullptr; used += aup(bytes); return r; };
+  const int64_t ncells = 6LL * F * F;
+  L.rec = reinterpret_cast<float*>(take((size_t)ng * CF_REC * sizeof(float)));
+  L.near = reinterpret_cast<float*>(take((size_t)nc * ng * sizeof(float)));
+  L.gids = reinterpret_cast<int32_t*>(take((size_t)nc * ng * sizeof(int32_t)));
+  L.ranges = reinterpret_cast<int32_t*>(take((size_t)nc * ncells * 2 * sizeof(int32_t)));
+  L.view_info = reinterpret_cast<int64_t*>(take((size_t)nc * 2 * sizeof(int64_t)));
+  L.vals = reinterpret_cast<int32_t*>(take((size_t)total_pairs * sizeof(int32_t)));
+  L.count = reinterpret_cast<int32_t*>(take((size_t)ng * sizeof(int32_t)));
+  L.gflag = reinterpret_cast<int32_t*>(take((size_t)ng * sizeof(int32_t)));
+  L.offs = reinterpret_cast<int64_t*>(take((size_t)(ng + 1) * sizeof(int64_t)));
+  L.goffs = reinterpret_cast<int64_t*>(take((size_t)(ng + 1) * sizeof(int64_t)));
+  L.scan_bytes = scan_workspace_bytes(ng);
+  L.scan_ws = take(L.scan_bytes);
+  L.dkey = reinterpret_cast<uint32_t*>(take((size_t)ng * sizeof(uint32_t)));
+  L.order = reinterpret_cast<int32_t*>(take((size_t)ng * sizeof(int32_t)));
+  L.order_bytes = bin_workspace_bytes(ng, 0, 0);
+  L.order_ws = take(L.order_bytes);
+  L.keys = reinterpret_cast<uint32_t*>(take((size_t)max_view_pairs * sizeof(uint32_t)));
+  L.sort_bytes = sort_pairs_workspace_bytes(max_view_pairs);
+  L.sort_ws = take(L.sort_bytes);
+  L.used = used;
+  return L;
+}
+
+struct PlanQueryLayout {
+  uint32_t* qkey; int32_t* qidx; void* sort_ws; size_t sort_bytes; int32_t* qranges; int32_t* chunks;
+  int64_t* chunk_off; void* scan_ws; size_t scan_bytes; int32_t* item_key; unsigned long long* queue;
+  size_t used;
+};
+
+PlanQueryLayout plan_query_layout(void* base, int64_t np, int nc, int F) {
+  PlanQueryLayout L{};
+  char* p = reinterpret_cast<char*>(base);
+  size_t used = 0;
+  auto take = [&](size_t bytes) { char* r = p ? p + used : nullptr; used += aup(bytes); return r; };
+  const int64_t n = np * nc, nkeys = (int64_t)nc * (6LL * F * F + 1);
+  L.qkey = reinterpret_cast<uint32_t*>(take((size_t)n * sizeof(uint32_t)));
+  L.qidx = reinterpret_cast<int32_t*>(take((size_t)n * sizeof(int32_t)));
+  L.sort_bytes = sort_pairs_workspace_bytes(n);
+  L.sort_ws = take(L.sort_bytes);
+  L.qranges = reinterpret_cast<int32_t*>(take((size_t)nkeys * 2 * sizeof(int32_t)));
+  L.chunks = reinterpret_cast<int32_t*>(take((size_t)nkeys * sizeof(int32_t)));
+  L.chunk_off = reinterpret_cast<int64_t*>(take((size_t)(nkeys + 1) * sizeof(int64_t)));
+  L.scan_bytes = scan_workspace_bytes(nkeys);
+  L.scan_ws = take(L.scan_bytes);
+  // at most one partial chunk per key beyond the full ones
+  L.item_key = reinterpret_cast<int32_t*>(take((size_t)((n + CF_THREADS - 1) / CF_THREADS + nkeys) * sizeof(int32_t)));
+  L.queue = reinterpret_cast<unsigned long long*>(take(sizeof(unsigned long long)));
+  L.used = used;
+  return L;
+}
+
+}  // namespace
+
+size_t field_plan_bytes(int64_t ng, int nc, int F, int64_t total_pairs, int64_t max_view_pairs) {
+  return plan_layout(nullptr, ng, nc, F, total_pairs, max_view_pairs).used;
+}
+
+size_t field_plan_query_bytes(int64_t np, int nc, int F) { return plan_query_layout(nullptr, np, nc, F).used; }
+
+cudaError_t field_plan_build(const float* means, const float* invcov, const float* op, int64_t ng,
+                             const float* origins, int nc, float cutoff, int F, void* plan, size_t plan_bytes,
+                             int64_t total_pairs, int64_t max_view_pairs, int64_t* needed, cudaStream_t s) {
+  const PlanLayout L = plan_layout(plan, ng, nc, F, total_pairs, max_view_pairs);
+  if (plan_bytes < L.used) return cudaErrorInvalidValue;
+  needed[0] = needed[1] = 0;
+  const int64_t ncells = 6LL * F * F;
+  std::vector<int64_t> info((size_t)nc * 2, 0);
+  cudaError_t e = cudaSuccess;
+  if (ng > 0) {
+    const unsigned gb = (unsigned)((ng + 255) / 256);
+    count_launches(1);
+    cfield_prep_kernel<<<gb, 256, 0, s>>>(means, invcov, op, ng, cutoff, L.rec);
+    e = cudaGetLastError();
+    std::vector<float> o((size_t)nc * 3);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(o.data(), origins, o.size() * sizeof(float), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    // first pass: candidate pairs of every view, so that undersized lists are reported
+    // before anything is written
+    int64_t sum = 0, most = 0;
+    for (int v = 0; v < nc && e == cudaSuccess; ++v) {
+      count_launches(1);
+      cfield_count_kernel<<<gb, 256, 0, s>>>(L.rec, ng, o[v * 3], o[v * 3 + 1], o[v * 3 + 2], F, L.count, L.gflag,
+                                             L.dkey, L.near + (int64_t)v * ng);
+      e = cudaGetLastError();
+      if (e == cudaSuccess) e = scan_counts(L.count, ng, L.offs, L.scan_ws, L.scan_bytes, s);
+      int64_t m = 0;
+      if (e == cudaSuccess) e = cudaMemcpyAsync(&m, L.offs + ng, sizeof(int64_t), cudaMemcpyDeviceToHost, s);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+      sum += m;
+      most = m > most ? m : most;
+    }
+    needed[0] = sum;
+    needed[1] = most;
+    if (e != cudaSuccess || sum > total_pairs || most > max_view_pairs) return e;
+    int64_t base = 0;
+    for (int v = 0; v < nc && e == cudaSuccess; ++v) {
+      float* near_v = L.near + (int64_t)v * ng;
+      count_launches(1);
+      cfield_count_kernel<<<gb, 256, 0, s>>>(L.rec, ng, o[v * 3], o[v * 3 + 1], o[v * 3 + 2], F, L.count, L.gflag,
+                                             L.dkey, near_v);
+      e = cudaGetLastError();
+      if (e == cudaSuccess) e = bin_order(L.count, L.dkey, ng, L.order, L.offs, L.order_ws, L.order_bytes, s);
+      if (e == cudaSuccess) e = scan_counts(L.gflag, ng, L.goffs, L.scan_ws, L.scan_bytes, s);
+      int64_t totals[2] = {0, 0};
+      if (e == cudaSuccess) e = cudaMemcpyAsync(&totals[0], L.offs + ng, sizeof(int64_t), cudaMemcpyDeviceToHost, s);
+      if (e == cudaSuccess) e = cudaMemcpyAsync(&totals[1], L.goffs + ng, sizeof(int64_t), cudaMemcpyDeviceToHost, s);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+      if (e != cudaSuccess) break;
+      const int64_t m = totals[0];
+      int32_t* vals_v = L.vals + base;
+      count_launches(1);
+      cfield_emit_kernel<<<gb, 256, 0, s>>>(L.rec, ng, o[v * 3], o[v * 3 + 1], o[v * 3 + 2], F, L.order, L.offs,
+                                            L.goffs, L.keys, vals_v, L.gids + (int64_t)v * ng);
+      e = cudaGetLastError();
+      if (e == cudaSuccess) e = sort_pairs(L.keys, vals_v, m, cube_bits(F), L.sort_ws, L.sort_bytes, s);
+      if (e == cudaSuccess) e = key_ranges(L.keys, m, ncells, L.ranges + (int64_t)v * ncells * 2, s);
+      info[(size_t)v * 2] = base;
+      info[(size_t)v * 2 + 1] = totals[1];
+      base += m;
+    }
+  } else {
+    e = cudaMemsetAsync(L.ranges, 0, (size_t)nc * ncells * 2 * sizeof(int32_t), s);
+  }
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(L.view_info, info.data(), info.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // `info` is host stack memory
+  return e;
+}
+
+cudaError_t field_plan_eval(const void* plan, int64_t ng, int nc, int F, int64_t total_pairs, int64_t max_view_pairs,
+                            const float* origins, const float* pts, int64_t np, float* out, void* ws, size_t ws_bytes,
+                            cudaStream_t s) {
+  const PlanLayout P = plan_layout(const_cast<void*>(plan), ng, nc, F, total_pairs, max_view_pairs);
+  const PlanQueryLayout Q = plan_query_layout(ws, np, nc, F);
+  if (ws_bytes < Q.used) return cudaErrorInvalidValue;
+  if (np == 0) return cudaSuccess;
+  uint32_t* o = reinterpret_cast<uint32_t*>(out);
+  count_launches(1);
+  field_init_kernel<<<(unsigned)((np + 255) / 256), 256, 0, s>>>(o, np);
+  const int64_t n = np * nc;
+  const int per_view = 6 * F * F + 1;
+  const int64_t nkeys = (int64_t)nc * per_view;
+  int qbits = 1;
+  while ((1LL << qbits) < nkeys) ++qbits;
+  count_launches(1);
+  cfield_plan_qcell_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(pts, np, origins, nc, F, Q.qkey, Q.qidx, o);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = sort_pairs(Q.qkey, Q.qidx, n, qbits, Q.sort_ws, Q.sort_bytes, s);
+  if (e == cudaSuccess) e = key_ranges(Q.qkey, n, nkeys, Q.qranges, s);
+  if (e != cudaSuccess) return e;
+  const unsigned kb = (unsigned)((nkeys + 255) / 256);
+  count_launches(1);
+  cfield_plan_chunks_kernel<<<kb, 256, 0, s>>>(reinterpret_cast<const int2*>(Q.qranges), nkeys, per_view, Q.chunks);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = scan_counts(Q.chunks, nkeys, Q.chunk_off, Q.scan_ws, Q.scan_bytes, s);
+  if (e != cudaSuccess) return e;
+  count_launches(1);
+  cfield_plan_items_kernel<<<kb, 256, 0, s>>>(Q.chunk_off, nkeys, Q.item_key);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaMemsetAsync(Q.queue, 0, sizeof(unsigned long long), s);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  count_launches(1);
+  cfield_plan_kernel<<<(unsigned)(sms * 6), CF_THREADS, 0, s>>>(
+      pts, Q.qidx, reinterpret_cast<const int2*>(Q.qranges), Q.chunk_off, Q.item_key, nkeys, per_view, origins, P.rec,
+      P.near, ng, P.vals, reinterpret_cast<const int2*>(P.ranges), P.view_info, P.gids, Q.queue, o);
+  return cudaGetLastError();
 }
 
 }  // namespace sf

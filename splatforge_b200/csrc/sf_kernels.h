@@ -117,6 +117,17 @@ cudaError_t launch_opacity_field(const float* pts, int64_t np, const float* mean
                                  const float* op, int64_t ng, const float* origins, int nc, float* out, void* ws,
                                  cudaStream_t s);
 
+// opacity field plan: every view's candidate lists built once, queries of all views
+// evaluated per call
+size_t field_plan_bytes(int64_t ng, int nc, int F, int64_t total_pairs, int64_t max_view_pairs);
+size_t field_plan_query_bytes(int64_t np, int nc, int F);
+cudaError_t field_plan_build(const float* means, const float* invcov, const float* op, int64_t ng,
+                             const float* origins, int nc, float cutoff, int F, void* plan, size_t plan_bytes,
+                             int64_t total_pairs, int64_t max_view_pairs, int64_t* needed, cudaStream_t s);
+cudaError_t field_plan_eval(const void* plan, int64_t ng, int nc, int F, int64_t total_pairs, int64_t max_view_pairs,
+                            const float* origins, const float* pts, int64_t np, float* out, void* ws, size_t ws_bytes,
+                            cudaStream_t s);
+
 // binning / sorting
 cudaError_t launch_bin_rects(const float* bounds, int64_t n, int width, int height, int tile,
                              float near_plane, float far_plane, int32_t* rect, int32_t* count,

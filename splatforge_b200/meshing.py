@@ -7,7 +7,7 @@ tetrahedra and shared-edge bisection (src/splatforge/mesh/tetrahedra.py:34-109),
 writes a PLY mesh.  Here:
 
 * on the device (libsf_b200.so): the grid points (``sf_b200_mesh_grid_points``), the
-  opacity field (``ops.opacity_field_culled``, or the brute-force ``ops.opacity_field``)
+  opacity field (a culled ``ops.OpacityFieldPlan``, or the brute-force ``ops.opacity_field``)
   and every marching stage (``sf_b200_mesh_count`` / ``_edges`` / ``_midpoints`` /
   ``_bisect`` / ``_faces``): inside flags, active cells, crossing-edge deduplication, the
   bisection updates and the oriented faces;
@@ -184,9 +184,10 @@ def gof_mesh(means, quats, scales, opacities, origins, *, inverse_covariances=No
     """The GOF exporter's extraction (exporters.py:41-88) on activated Gaussians
     (scales exponentiated, opacities after the sigmoid) and the training views' camera
     origins [V,3].  ``inverse_covariances`` defaults to inv(covariance(quats, scales)).
-    The field is the culled opacity field (``culled``) or the brute-force one; the
-    exporter's query and Gaussian chunking only bound the reference's memory and do not
-    change the field, so every evaluation covers all queries at once.  Returns
+    The field is the culled opacity field through one ``ops.OpacityFieldPlan`` for the
+    whole extraction (``culled``) or the brute-force one; the exporter's query and
+    Gaussian chunking only bound the reference's memory and do not change the field, so
+    every evaluation covers all queries at once.  Returns
     SimpleNamespace(vertices, faces, grid_vertices, tetrahedra, seeds)."""
     dev = _device_of(means)
     m, q, s, o, org = (t.detach().to(torch.float32).contiguous() for t in (means, quats, scales, opacities, origins))
@@ -196,7 +197,13 @@ def gof_mesh(means, quats, scales, opacities, origins, *, inverse_covariances=No
     inv = inverse_covariances.detach().to(torch.float32).contiguous()
     points, cells, seeds = gaussian_grid(m, q, s, o, seed_opacity_min=seed_opacity_min,
                                          max_gaussians=max_gaussians, tetra_extent=tetra_extent)
-    field_op = ops.opacity_field_culled if culled else ops.opacity_field
+    if culled:
+        plan = ops.OpacityFieldPlan(m, inv, o, org)
+
+        def field_op(p, *args):
+            return plan(p)
+    else:
+        field_op = ops.opacity_field
 
     def field(coordinates):
         # queries rounded to float32, as the reference's field converts them

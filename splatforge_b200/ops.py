@@ -216,6 +216,71 @@ def opacity_field_culled(points, means, inverse_covariances, opacities, origins,
         raise _lib.NativeError("opacity_field_culled: candidate lists did not fit after resizing")
 
 
+class OpacityFieldPlan:
+    """Repeated evaluations of ``gaussian.opacity_field@1`` against one Gaussian set and
+    one set of origins, as the GOF exporter makes them (the grid, then every bisection
+    step, src/splatforge/studio/exporters.py:56-88): every view's culled candidate lists
+    are built once (one host synchronisation per origin); each call then evaluates its
+    queries for all views at once, with no host synchronisation.  The values equal
+    ``opacity_field_culled``'s for the same ``cutoff`` and ``face_cells``."""
+
+    def __init__(self, means, inverse_covariances, opacities, origins, *, cutoff=FIELD_CUTOFF, face_cells=None):
+        dev = _require_cuda_f32("gaussian.opacity_field@1", means, inverse_covariances, opacities, origins)
+        if origins.shape[0] < 1:
+            raise ValueError("opacity field requires at least one origin")
+        self.device = dev
+        self.n = means.shape[0]
+        self.origins = origins.contiguous()
+        nc = self.origins.shape[0]
+        F = face_cells or FIELD_FACE_CELLS
+        total = most = 0
+        needed = (ctypes.c_int64 * 2)()
+        with torch.cuda.device(dev), torch.no_grad():
+            m, q, o = (t.contiguous() for t in (means, inverse_covariances, opacities))
+            for _ in range(8):
+                size = ctypes.c_size_t()
+                call("sf_b200_opacity_field_plan_bytes", self.n, nc, F, total, most, ctypes.byref(size))
+                plan = torch.empty((max(size.value, 1),), device=dev, dtype=torch.uint8)
+                status = _lib.lib().sf_b200_opacity_field_plan_build(
+                    _ptr(m), _ptr(q), _ptr(o), self.n, _ptr(self.origins), nc, ctypes.c_float(cutoff), F, _ptr(plan),
+                    plan.numel(), total, most, needed, _stream(dev))
+                if status == _lib.SF_OK:
+                    break
+                if status != _lib.SF_ERR_CAPACITY:
+                    raise _lib.NativeError(_lib.lib().sf_b200_last_error().decode())
+                if needed[1] > FIELD_PAIR_LIMIT and F > 8 and face_cells is None:
+                    # fewer, larger cells: pairs scale with the square of the face resolution
+                    F = max(8, int(F * 0.97 * (FIELD_PAIR_LIMIT / needed[1]) ** 0.5))
+                    total = most = 0
+                else:
+                    total, most = int(needed[0]), int(needed[1])
+            else:
+                raise _lib.NativeError("opacity field plan: candidate lists did not fit after resizing")
+        self.plan, self.face_cells, self.total_pairs, self.max_view_pairs = plan, F, total, most
+        self._ws = None
+
+    def __call__(self, points):
+        dev = _require_cuda_f32("gaussian.opacity_field@1", points, self.origins)
+        if dev != self.device:
+            raise ValueError("opacity field plan: points must be on the plan's device")
+        nc = self.origins.shape[0]
+        with torch.cuda.device(dev), torch.no_grad():
+            p = points.contiguous()
+            out = torch.empty((p.shape[0],), device=dev, dtype=torch.float32)
+            step = (2**31 - 1) // nc
+            for start in range(0, p.shape[0], step):
+                part = p[start:start + step]
+                size = ctypes.c_size_t()
+                call("sf_b200_opacity_field_plan_query_bytes", part.shape[0], nc, self.face_cells, ctypes.byref(size))
+                if self._ws is None or self._ws.numel() < size.value:
+                    self._ws = None
+                    self._ws = torch.empty((max(size.value, 1),), device=dev, dtype=torch.uint8)
+                call("sf_b200_opacity_field_plan_eval", _ptr(self.plan), self.n, nc, self.face_cells, self.total_pairs,
+                     self.max_view_pairs, _ptr(self.origins), _ptr(part), part.shape[0], _ptr(out[start:]),
+                     _ptr(self._ws), self._ws.numel(), _stream(dev))
+        return out
+
+
 # ---------------------------------------------------------------- small geometry ops
 def pixel_rays(K, *, width, height):
     """``camera.pixel_rays@1``: inv(K) (u + 0.5, v + 0.5, 1) as [height, width, 3]."""

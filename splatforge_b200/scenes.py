@@ -287,6 +287,9 @@ def workload(name: str, seed: int = 0):
         return surfaces(3_000_000, seed), orbit_cameras(
             64, 1600, 1064, 60.0, seed=seed, radius_range=(2.5, 4.0)
         )
+    if name == "mesh100k_views32":
+        # the GOF mesh-extraction workload: 100k Gaussians, 32 training-view origins
+        return surfaces(100_000, seed), orbit_cameras(32, 1280, 720, 60.0, radius=3.0, seed=seed)
     if name == "field2m_views32":
         # the GOF opacity-field workload: 2M Gaussians, 32 training-view origins
         return surfaces(2_000_000, seed), orbit_cameras(32, 1280, 720, 60.0, radius=3.0, seed=seed)

@@ -160,6 +160,30 @@ def test_opacity_field_culled_edge_cases_against_oracle():
     assert want[-2].item() == 0.0
 
 
+def test_opacity_field_plan_equals_the_culled_field():
+    """The plan (all views' lists built once, all views' queries in one pass) gives the
+    culled field's values bit for bit, on the 20k scene and on the edge cases (origin
+    inside a Gaussian's ball, a query at an origin, a Gaussian below the cutoff), and
+    stays valid across calls with different query sets."""
+    args = [t.to(DEV) for t in _field_case(20_000, 20_000, 6)]
+    plan = ops.OpacityFieldPlan(*args[1:])
+    assert torch.equal(plan(args[0]), ops.opacity_field_culled(*args))
+    part = args[0][::7].contiguous()
+    assert torch.equal(plan(part), ops.opacity_field_culled(part, *args[1:]))
+    pts, m, Q, o, org = _field_case(300, 400, 3, seed=4)
+    org = torch.cat((org, m[7:8] + 1e-3), 0)
+    pts = torch.cat((pts, org[1:2], m[7:8] + 2e-3), 0)
+    o = o.clone()
+    o[11] = 5e-8
+    d = [t.to(DEV) for t in (pts, m, Q, o, org)]
+    for cells in (1, 16, 128):
+        got = ops.OpacityFieldPlan(*d[1:], face_cells=cells)(d[0])
+        assert torch.equal(got, ops.opacity_field_culled(*d, face_cells=cells)), cells
+    assert got[-2].item() == 0.0
+    empty = ops.OpacityFieldPlan(d[1][:0], d[2][:0], d[3][:0], d[4])
+    assert torch.equal(empty(d[0]), ops.opacity_field(d[0], d[1][:0], d[2][:0], d[3][:0], d[4]))
+
+
 def test_opacity_field_culled_reference_fixture(golden):
     f = golden("ops")
     out = ops.opacity_field_culled(*(T(f[f"field/{k}"]) for k in ("p", "m", "Q", "o", "origins")))
