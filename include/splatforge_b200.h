@@ -278,6 +278,41 @@ int sf_b200_depth_normals_backward(const float* depth, const float* K, int32_t w
                                    const float* grad_normals, float* grad_depth, float* workspace,
                                    void* stream);
 
+/* ---- training-step operations --------------------------------------------------
+ * matching.patch_zncc@1 (reference.py:225-236): a, b, mask [rows, S] (mask 0/1) ->
+ *   correlation [rows] and valid [rows] (uint8); the backward maps grad_correlation
+ *   [rows] to grad_a, grad_b [rows, S] (the mask is not differentiated).
+ * densify_observe (studio/densification.py:18-43): where radii[i] > 0,
+ *   gradient[i] += |(grad2d[i,0] * scale_x, grad2d[i,1] * scale_y)| and
+ *   observations[i] += 1 (both accumulators updated in place).
+ * normal_consistency (studio/losses.py:9-12, 45-53): depth [H,W], K [3,3], alpha [H,W],
+ *   mask [H,W], and either normal_numerator [H,W,3] (loss term alpha - n_num . n_depth) or
+ *   normals [H,W,3] (1 - n . n_depth; pass NULL for the other) -> loss (device float) and
+ *   count (device int64) of the pixels where the depth normal is valid, alpha > 0.1 and
+ *   mask > 0.  The backward takes the device scalar grad_loss, the same inputs and the
+ *   same workspace (which keeps the depth normals between the calls) and writes
+ *   grad_depth [H,W], grad_alpha [H,W] (zero in the normals case), grad_vector [H,W,3]
+ *   (for whichever of normal_numerator / normals was given), plus a grad_normals [H,W,3]
+ *   scratch.  Each may be NULL except grad_depth and grad_normals. */
+int sf_b200_patch_zncc(const float* a, const float* b, const float* mask, int64_t rows, int32_t samples,
+                       float epsilon, float* correlation, uint8_t* valid, void* stream);
+int sf_b200_patch_zncc_backward(const float* a, const float* b, const float* mask, int64_t rows,
+                                int32_t samples, float epsilon, const float* grad_correlation,
+                                float* grad_a, float* grad_b, void* stream);
+int sf_b200_densify_observe(const float* grad2d, const float* radii, int64_t n, float scale_x,
+                            float scale_y, float* gradient, float* observations, void* stream);
+int sf_b200_normal_consistency_workspace_bytes(int32_t width, int32_t height, size_t* bytes);
+int sf_b200_normal_consistency(const float* depth, const float* K, int32_t width, int32_t height,
+                               const float* alpha, const float* normal_numerator, const float* normals,
+                               const float* mask, float* loss, int64_t* count, void* workspace,
+                               size_t workspace_bytes, void* stream);
+int sf_b200_normal_consistency_backward(const float* depth, const float* K, int32_t width, int32_t height,
+                                        const float* alpha, const float* normal_numerator,
+                                        const float* normals, const float* mask, const float* grad_loss,
+                                        const int64_t* count, float* grad_depth, float* grad_alpha,
+                                        float* grad_vector, float* grad_normals, void* workspace,
+                                        size_t workspace_bytes, void* stream);
+
 /* ---- GOF mesh extraction ---------------------------------------------------------
  * The device stages of GOFExporter.export (src/splatforge/studio/exporters.py:20-102)
  * and of marching_tetrahedra (src/splatforge/mesh/tetrahedra.py:34-109).  The caller

@@ -217,3 +217,40 @@ def opacity_field(points, means, inverse_covariances, opacities, origins, *, gau
             trans = trans * (1 - c).prod(0)
         out = torch.minimum(out, 1 - trans)
     return out
+
+
+def patch_zncc(a, b, mask, epsilon=1e-8):
+    """``matching.patch_zncc@1`` (reference.py:225-236): masked, zero-mean correlation of
+    patch pairs over the last axis; a patch needs >= 2 valid samples and both variances
+    above epsilon, else it reads 0 and is invalid.  Returns (correlation, valid)."""
+    n = mask.sum(-1)
+    count = n.clamp_min(1)
+    ca = a - (a * mask).sum(-1, keepdim=True) / count[..., None]
+    cb = b - (b * mask).sum(-1, keepdim=True) / count[..., None]
+    va = (mask * ca * ca).sum(-1)
+    vb = (mask * cb * cb).sum(-1)
+    ok = (n >= 2) & (va > epsilon) & (vb > epsilon)
+    r = (mask * ca * cb).sum(-1) / torch.sqrt((va * vb).clamp_min(epsilon * epsilon))
+    return torch.where(ok, r.clamp(-1, 1), torch.zeros_like(r)), ok
+
+
+def normal_consistency(depth, K, alpha, vector, mask, numerator=True):
+    """The normal-consistency loss (studio/losses.py:45-53) on [H,W] depth/alpha/mask and
+    an [H,W,3] normal numerator (term alpha - v . n) or unit normals (term 1 - v . n):
+    the mean of the term over pixels whose depth normal n is valid, alpha > 0.1 and
+    mask > 0 (losses.py:9-12), divided by max(count, 1)."""
+    n, valid = depth_normals(depth, K)
+    keep = valid & (alpha > 0.1) & (mask > 0)
+    dot = (vector * n).sum(-1)
+    term = (alpha - dot) if numerator else (1 - dot)
+    return torch.where(keep, term, torch.zeros_like(term)).sum() / keep.sum().clamp_min(1)
+
+
+def densify_observe(gradient, observations, grad2d, radii, scale=(1.0, 1.0)):
+    """GaussianDensifier.observe's update (studio/densification.py:18-43): where the
+    projected radius is positive, add the norm of the scaled 2D gradient and count one
+    observation.  Updates the accumulators in place."""
+    seen = radii.reshape(-1) > 0
+    g = grad2d.reshape(-1, 2) * grad2d.new_tensor(scale)
+    gradient += torch.where(seen, torch.linalg.vector_norm(g, dim=-1), torch.zeros_like(gradient))
+    observations += seen.to(observations.dtype)

@@ -111,6 +111,14 @@ _SIGNATURES = {
     "sf_b200_ray_peak": (ctypes.c_int, [P, P, c_int64, P, P, c_int64, P, P, P, P]),
     "sf_b200_depth_normals": (ctypes.c_int, [P, P, c_int32, c_int32, P, P, P]),
     "sf_b200_depth_normals_backward": (ctypes.c_int, [P, P, c_int32, c_int32, P, P, P, P]),
+    "sf_b200_patch_zncc": (ctypes.c_int, [P, P, P, c_int64, c_int32, c_float, P, P, P]),
+    "sf_b200_patch_zncc_backward": (ctypes.c_int, [P, P, P, c_int64, c_int32, c_float, P, P, P, P]),
+    "sf_b200_densify_observe": (ctypes.c_int, [P, P, c_int64, c_float, c_float, P, P, P]),
+    "sf_b200_normal_consistency_workspace_bytes": (ctypes.c_int, [c_int32, c_int32, POINTER(c_size_t)]),
+    "sf_b200_normal_consistency": (ctypes.c_int, [P, P, c_int32, c_int32, P, P, P, P, P, P, P, c_size_t, P]),
+    "sf_b200_normal_consistency_backward": (
+        ctypes.c_int, [P, P, c_int32, c_int32, P, P, P, P, P, P, P, P, P, P, P, c_size_t, P]
+    ),
     "sf_b200_mesh_grid_points": (ctypes.c_int, [P, P, P, P, c_int64, c_double, P, P, P]),
     "sf_b200_mesh_count_workspace_bytes": (ctypes.c_int, [c_int64, POINTER(c_size_t)]),
     "sf_b200_mesh_count": (ctypes.c_int, [P, c_int64, P, c_int64, c_double, c_int32, P, P, P, P, c_size_t, P]),

@@ -23,7 +23,7 @@ CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 LIB = PKG / "libsf_b200.so"
 HOSTCHECK = PKG / "libsf_b200_hostcheck.so"
-CUDA_SOURCES = ("preprocess.cu", "binning.cu", "raster.cu", "composite.cu", "opacity_field.cu", "geometry.cu", "meshing.cu", "capi.cu",
+CUDA_SOURCES = ("preprocess.cu", "binning.cu", "raster.cu", "composite.cu", "opacity_field.cu", "geometry.cu", "meshing.cu", "training.cu", "capi.cu",
                 "binning_static.cu")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

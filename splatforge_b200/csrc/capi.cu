@@ -527,6 +527,84 @@ int sf_b200_alpha_composite_backward(const float* alphas, const float* colors, c
                      "alpha_composite_backward");
 }
 
+// ------------------------------------------------------------------ training-step operations
+int sf_b200_patch_zncc(const float* a, const float* b, const float* mask, int64_t rows, int32_t samples, float epsilon,
+                       float* correlation, uint8_t* valid, void* stream) {
+  if (rows < 0 || samples < 0) return fail(SF_ERR_ARGUMENT, "patch_zncc: negative size");
+  if (rows > 0 && (!a || !b || !mask || !correlation || !valid)) return fail(SF_ERR_ARGUMENT, "patch_zncc: NULL buffer");
+  return cuda_status(sf::launch_patch_zncc(a, b, mask, rows, samples, epsilon, correlation, valid, as_stream(stream)),
+                     "patch_zncc");
+}
+
+int sf_b200_patch_zncc_backward(const float* a, const float* b, const float* mask, int64_t rows, int32_t samples,
+                                float epsilon, const float* grad_correlation, float* grad_a, float* grad_b,
+                                void* stream) {
+  if (rows < 0 || samples < 0) return fail(SF_ERR_ARGUMENT, "patch_zncc_backward: negative size");
+  if (rows > 0 && (!a || !b || !mask || !grad_correlation || !grad_a || !grad_b))
+    return fail(SF_ERR_ARGUMENT, "patch_zncc_backward: NULL buffer");
+  return cuda_status(sf::launch_patch_zncc_backward(a, b, mask, rows, samples, epsilon, grad_correlation, grad_a,
+                                                    grad_b, as_stream(stream)),
+                     "patch_zncc_backward");
+}
+
+int sf_b200_densify_observe(const float* grad2d, const float* radii, int64_t n, float scale_x, float scale_y,
+                            float* gradient, float* observations, void* stream) {
+  if (n < 0) return fail(SF_ERR_ARGUMENT, "densify_observe: negative size");
+  if (n > 0 && (!grad2d || !radii || !gradient || !observations))
+    return fail(SF_ERR_ARGUMENT, "densify_observe: NULL buffer");
+  return cuda_status(sf::launch_densify_observe(grad2d, radii, n, scale_x, scale_y, gradient, observations,
+                                                as_stream(stream)),
+                     "densify_observe");
+}
+
+int sf_b200_normal_consistency_workspace_bytes(int32_t width, int32_t height, size_t* bytes) {
+  if (width < 0 || height < 0 || !bytes) return fail(SF_ERR_ARGUMENT, "normal_consistency_workspace_bytes: bad arguments");
+  *bytes = sf::normal_consistency_workspace_bytes(width, height);
+  return SF_OK;
+}
+
+static int nc_check(const char* what, const float* depth, const float* K, int32_t width, int32_t height,
+                    const float* alpha, const float* numer, const float* normals, const float* mask, size_t ws_bytes,
+                    const void* ws) {
+  if (width < 0 || height < 0) return fail(SF_ERR_ARGUMENT, "%s: negative size", what);
+  if ((numer == nullptr) == (normals == nullptr))
+    return fail(SF_ERR_ARGUMENT, "%s: pass exactly one of normal_numerator and normals", what);
+  if (!K || !ws || ((int64_t)width * height > 0 && (!depth || !alpha || !mask)))
+    return fail(SF_ERR_ARGUMENT, "%s: NULL buffer", what);
+  if (ws_bytes < sf::normal_consistency_workspace_bytes(width, height))
+    return fail(SF_ERR_CAPACITY, "%s: workspace of %zu bytes, %zu needed", what, ws_bytes,
+                sf::normal_consistency_workspace_bytes(width, height));
+  return SF_OK;
+}
+
+int sf_b200_normal_consistency(const float* depth, const float* K, int32_t width, int32_t height, const float* alpha,
+                               const float* normal_numerator, const float* normals, const float* mask, float* loss,
+                               int64_t* count, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = nc_check("normal_consistency", depth, K, width, height, alpha, normal_numerator, normals, mask,
+                    workspace_bytes, workspace);
+  if (rc != SF_OK) return rc;
+  if (!loss || !count) return fail(SF_ERR_ARGUMENT, "normal_consistency: NULL buffer");
+  return cuda_status(sf::normal_consistency(depth, K, width, height, alpha, normal_numerator, normals, mask, loss,
+                                            count, workspace, as_stream(stream)),
+                     "normal_consistency");
+}
+
+int sf_b200_normal_consistency_backward(const float* depth, const float* K, int32_t width, int32_t height,
+                                        const float* alpha, const float* normal_numerator, const float* normals,
+                                        const float* mask, const float* grad_loss, const int64_t* count,
+                                        float* grad_depth, float* grad_alpha, float* grad_vector, float* grad_normals,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = nc_check("normal_consistency_backward", depth, K, width, height, alpha, normal_numerator, normals, mask,
+                    workspace_bytes, workspace);
+  if (rc != SF_OK) return rc;
+  if ((int64_t)width * height > 0 && (!grad_loss || !count || !grad_depth || !grad_normals))
+    return fail(SF_ERR_ARGUMENT, "normal_consistency_backward: NULL buffer");
+  return cuda_status(sf::normal_consistency_backward(depth, K, width, height, alpha, normal_numerator, normals, mask,
+                                                     grad_loss, count, grad_depth, grad_alpha, grad_vector,
+                                                     grad_normals, workspace, as_stream(stream)),
+                     "normal_consistency_backward");
+}
+
 // ------------------------------------------------------------------ GOF mesh extraction
 int sf_b200_mesh_grid_points(const float* means, const float* quats, const float* scales, const int32_t* chosen,
                              int64_t n, double extent, double* points, double* radius, void* stream) {

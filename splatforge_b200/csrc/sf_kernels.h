@@ -173,4 +173,20 @@ cudaError_t mesh_faces(const double* points, const int32_t* cells, int64_t n_cel
                        int64_t n_edges, const int64_t* face_off, int64_t n_faces, double* vertices, int64_t* faces,
                        int64_t* n_kept, void* ws, size_t ws_bytes, cudaStream_t s);
 
+// training-step operations (training.cu)
+cudaError_t launch_patch_zncc(const float* a, const float* b, const float* m, int64_t rows, int S, float eps,
+                              float* corr, uint8_t* valid, cudaStream_t s);
+cudaError_t launch_patch_zncc_backward(const float* a, const float* b, const float* m, int64_t rows, int S, float eps,
+                                       const float* g_corr, float* ga, float* gb, cudaStream_t s);
+cudaError_t launch_densify_observe(const float* grad2d, const float* radii, int64_t n, float sx, float sy,
+                                   float* gradient, float* observations, cudaStream_t s);
+size_t normal_consistency_workspace_bytes(int W, int H);
+cudaError_t normal_consistency(const float* depth, const float* K, int W, int H, const float* alpha,
+                               const float* numer, const float* unit, const float* mask, float* loss, int64_t* count,
+                               void* ws, cudaStream_t s);
+cudaError_t normal_consistency_backward(const float* depth, const float* K, int W, int H, const float* alpha,
+                                        const float* numer, const float* unit, const float* mask, const float* g_loss,
+                                        const int64_t* count, float* g_depth, float* g_alpha, float* g_vec,
+                                        float* g_normals, void* ws, cudaStream_t s);
+
 }  // namespace sf

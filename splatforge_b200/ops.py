@@ -10,6 +10,7 @@ what the Torch provider's function returns:
                                                      splat.alpha_composite@3 (reference.py:182-186)
 * ``opacity_field(points, means, inverse_covariances, opacities, origins, *, gaussian_chunk)``
                                                      gaussian.opacity_field@1 (reference.py:194-222)
+* ``patch_zncc(a, b, mask, *, epsilon)``             matching.patch_zncc@1 (reference.py:225-236)
 
 They accept CUDA float32 tensors only and raise ``ValueError`` otherwise, like the
 reference's CUDA composite provider (cuda_composite.py:79-85); nothing falls back
@@ -279,6 +280,50 @@ class OpacityFieldPlan:
                      self.max_view_pairs, _ptr(self.origins), _ptr(part), part.shape[0], _ptr(out[start:]),
                      _ptr(self._ws), self._ws.numel(), _stream(dev))
         return out
+
+
+# ---------------------------------------------------------------- matching.patch_zncc@1
+class _PatchZncc(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, b, mask, epsilon):
+        dev = a.device
+        S = a.shape[-1]
+        rows = a.numel() // S if S else 0
+        a2, b2, m2 = (t.contiguous().reshape(rows, S) for t in (a, b, mask))
+        corr = torch.empty((rows,), device=dev, dtype=torch.float32)
+        valid = torch.empty((rows,), device=dev, dtype=torch.uint8)
+        with torch.cuda.device(dev):
+            call("sf_b200_patch_zncc", _ptr(a2), _ptr(b2), _ptr(m2), rows, S, ctypes.c_float(epsilon), _ptr(corr),
+                 _ptr(valid), _stream(dev))
+        ctx.save_for_backward(a2, b2, m2)
+        ctx.shape, ctx.epsilon = a.shape, epsilon
+        ctx.mark_non_differentiable(valid)
+        return corr.reshape(a.shape[:-1]), valid.bool().reshape(a.shape[:-1])
+
+    @staticmethod
+    def backward(ctx, g_corr, g_valid):
+        a2, b2, m2 = ctx.saved_tensors
+        rows, S = a2.shape
+        if g_corr is None:
+            return None, None, None, None
+        dev = a2.device
+        g = g_corr.contiguous().reshape(rows).float()
+        ga = torch.empty_like(a2)
+        gb = torch.empty_like(b2)
+        with torch.cuda.device(dev):
+            call("sf_b200_patch_zncc_backward", _ptr(a2), _ptr(b2), _ptr(m2), rows, S, ctypes.c_float(ctx.epsilon),
+                 _ptr(g), _ptr(ga), _ptr(gb), _stream(dev))
+        return ga.reshape(ctx.shape), gb.reshape(ctx.shape), None, None
+
+
+def patch_zncc(a, b, mask, *, epsilon=1e-8):
+    """``matching.patch_zncc@1``: masked zero-mean normalised cross-correlation of patch
+    pairs a, b [..., S] with a 0/1 mask [..., S] -> (correlation [...], valid [...] bool);
+    differentiable in a and b (reference.py:225-236).  The mask is not differentiated."""
+    _require_cuda_f32("matching.patch_zncc@1", a, b, mask)
+    if a.ndim < 1 or a.shape != b.shape or a.shape != mask.shape:
+        raise ValueError("patch_zncc: a, b and mask must share one shape [..., S]")
+    return _PatchZncc.apply(a, b, mask, float(epsilon))
 
 
 # ---------------------------------------------------------------- small geometry ops

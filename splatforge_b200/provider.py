@@ -48,6 +48,8 @@ _OPS = {
                             "sm100a-float32-forward", False, ("geometry.cu",)),
     "geometry.depth_normals@1": ("splatforge_b200.native_cuda.depth_normals.v1", ops.depth_normals,
                                  "sf_b200_depth_normals", "sm100a-float32", True, ("geometry.cu",)),
+    "matching.patch_zncc@1": ("splatforge_b200.native_cuda.patch_zncc.v1", ops.patch_zncc, "sf_b200_patch_zncc",
+                              "sm100a-float32", True, ("training.cu", "sf_device.cuh")),
 }
 
 # Additional implementations of an operator already listed above, selected explicitly

@@ -20,6 +20,9 @@ Fixtures (all float32 unless noted):
                        test case) and sphere, and the GOF exporter's gaussian_grid
                        (with and without max_gaussians) plus the level set of the
                        opacity field of a 300-Gaussian scene (float64 grid).
+* ``training.npz``  -- matching.patch_zncc@1 (with its a/b adjoints), the
+                       normal-consistency loss (numerator and unit-normal forms, with
+                       input gradients) and GaussianDensifier.observe statistics.
 * ``ops.npz``       -- covariance@1, sh_color@1 (deg 0..3), pixel_rays@1,
                        ray_peak@1, alpha_composite@3 (all profiles, with input
                        gradients), opacity_field@1.
@@ -256,6 +259,83 @@ def mesh_cases():
     np.savez_compressed(HERE / "mesh.npz", **out)
 
 
+def training_cases():
+    """matching.patch_zncc@1 (forward and the a/b adjoints of a seeded linear loss, with
+    short, constant, perfectly correlated and anti-correlated patches), the
+    normal-consistency loss with and without a normal numerator (value and input
+    gradients), and GaussianDensifier.observe in pixel and NDC gradient space."""
+    from types import SimpleNamespace
+
+    from splatforge.gaussian import SurfaceOperators
+    from splatforge.studio.densification import GaussianDensifier
+    from splatforge.studio.losses import normal_consistency
+
+    ops = SurfaceOperators()
+    out = {}
+    g = torch.Generator().manual_seed(23)
+    rows, S = 40, 49
+    a = torch.rand(rows, S, generator=g)
+    b = 0.6 * a + 0.4 * torch.rand(rows, S, generator=g)
+    m = (torch.rand(rows, S, generator=g) > 0.2).float()
+    m[0] = 0.0
+    m[1, 1:] = 0.0           # one sample: invalid
+    a[2] = 0.5               # constant: zero variance
+    b[3] = 2.0 * a[3] + 1.0  # perfectly correlated
+    b[4] = -a[4]             # anti-correlated
+    a.requires_grad_()
+    b.requires_grad_()
+    corr, valid = ops("matching.patch_zncc@1", a, b, m)
+    up = torch.randn(rows, generator=g)
+    ga, gb = torch.autograd.grad((corr * up).sum(), (a, b))
+    out.update({"zncc/a": a.detach().numpy(), "zncc/b": b.detach().numpy(), "zncc/m": m.numpy(),
+                "zncc/corr": corr.detach().numpy(), "zncc/valid": valid.numpy(), "zncc/up": up.numpy(),
+                "zncc/ga": ga.numpy(), "zncc/gb": gb.numpy()})
+
+    H, W = 29, 41
+    yy, xx = torch.meshgrid(torch.arange(H, dtype=torch.float32), torch.arange(W, dtype=torch.float32), indexing="ij")
+    depth = 2.0 + 0.3 * torch.sin(xx / 6.0) + 0.2 * torch.cos(yy / 4.0) + 0.05 * torch.rand(H, W, generator=g)
+    depth[7, 11] = 0.0
+    alpha = torch.rand(H, W, generator=g)
+    nnum = torch.randn(H, W, 3, generator=g) * 0.5
+    normals = torch.nn.functional.normalize(torch.randn(H, W, 3, generator=g), dim=-1)
+    mask = (torch.rand(H, W, generator=g) > 0.1).float()
+    K = torch.tensor([[50.0, 0.0, 20.0], [0.0, 48.0, 14.5], [0.0, 0.0, 1.0]])
+    camera = SimpleNamespace(K=K)
+    out.update({"nc/depth": depth.numpy(), "nc/alpha": alpha.numpy(), "nc/nnum": nnum.numpy(),
+                "nc/normals": normals.numpy(), "nc/mask": mask.numpy(), "nc/K": K.numpy()})
+    for tag, numerator in (("num", True), ("unit", False)):
+        d = depth.clone().unsqueeze(-1).requires_grad_()
+        al = alpha.clone().unsqueeze(-1).requires_grad_()
+        v = (nnum if numerator else normals).clone().requires_grad_()
+        output = SimpleNamespace(depth=d, alpha=al, normals=v if not numerator else normals,
+                                 normal_numerator=v if numerator else None)
+        loss = normal_consistency(output, camera, ops, mask.unsqueeze(-1))
+        gd, gal, gv = torch.autograd.grad(loss, (d, al, v), allow_unused=True)
+        gal = torch.zeros_like(al) if gal is None else gal
+        out.update({f"nc/{tag}/loss": loss.detach().numpy(), f"nc/{tag}/gdepth": gd.squeeze(-1).numpy(),
+                    f"nc/{tag}/galpha": gal.squeeze(-1).numpy(), f"nc/{tag}/gvec": gv.numpy()})
+
+    n = 500
+    grad = torch.randn(n, 2, generator=g)
+    absgrad = grad.abs() + torch.rand(n, 2, generator=g)
+    radii = torch.where(torch.rand(n, generator=g) > 0.3, torch.rand(n, generator=g) * 10, torch.zeros(n))
+    out.update({"dens/grad": grad.numpy(), "dens/absgrad": absgrad.numpy(), "dens/radii": radii.numpy()})
+    for space in ("pixel", "ndc"):
+        for absolute in (False, True):
+            config = SimpleNamespace(absolute_gradients=absolute, gradient_space=space)
+            model = SimpleNamespace(count=n, device=torch.device("cpu"))
+            dens = GaussianDensifier(config, model)
+            projected = torch.zeros(n, 2)
+            projected.grad = grad
+            projected.absgrad = absgrad
+            output = SimpleNamespace(projected_means=projected, projected_radii=radii, rgb=torch.zeros(24, 40, 3))
+            dens.observe(output, model)
+            dens.observe(output, model)
+            key = f"dens/{space}/{'abs' if absolute else 'grad'}"
+            out.update({f"{key}/gradient": dens.gradient.numpy(), f"{key}/observations": dens.observations.numpy()})
+    np.savez_compressed(HERE / "training.npz", **out)
+
+
 CHANNELS = ("rgb", "alpha", "depth", "normals", "distortion_l1", "distortion_l2",
             "median_depth", "ray_color", "ambiguity_mask")
 
@@ -360,7 +440,7 @@ def render_cases():
 
 if __name__ == "__main__":
     _setup(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
-    which = sys.argv[2:] or ["binning", "ops", "geometry", "mesh", "render"]
+    which = sys.argv[2:] or ["binning", "ops", "geometry", "mesh", "training", "render"]
     if "binning" in which:
         binning_cases()
     if "ops" in which:
@@ -369,6 +449,8 @@ if __name__ == "__main__":
         geometry_cases()
     if "mesh" in which:
         mesh_cases()
+    if "training" in which:
+        training_cases()
     if "render" in which:
         render_cases()
     for f in sorted(HERE.glob("*.npz")):

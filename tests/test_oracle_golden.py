@@ -209,3 +209,37 @@ def test_mesh_oracle_gof_level_set_matches_reference(golden):
     v, fc = meshing.marching_tetrahedra(pts, cells, values, field, level=0.5, binary_steps=8, inside_greater=True)
     np.testing.assert_array_equal(fc, f["gof/faces"])
     np.testing.assert_array_equal(v, f["gof/vertices"])
+
+
+def test_training_ops_oracle_matches_reference(golden):
+    """patch_zncc (values and a/b gradients), the normal-consistency loss (both forms,
+    with depth/alpha/vector gradients) and the densifier statistics against the
+    reference's outputs."""
+    f = golden("training")
+    a = torch.from_numpy(f["zncc/a"]).requires_grad_()
+    b = torch.from_numpy(f["zncc/b"]).requires_grad_()
+    corr, valid = ops.patch_zncc(a, b, torch.from_numpy(f["zncc/m"]))
+    np.testing.assert_array_equal(valid.numpy(), f["zncc/valid"])
+    np.testing.assert_allclose(corr.detach().numpy(), f["zncc/corr"], atol=1e-6)
+    ga, gb = torch.autograd.grad((corr * torch.from_numpy(f["zncc/up"])).sum(), (a, b))
+    np.testing.assert_allclose(ga.numpy(), f["zncc/ga"], atol=1e-5)
+    np.testing.assert_allclose(gb.numpy(), f["zncc/gb"], atol=1e-5)
+    K = torch.from_numpy(f["nc/K"])
+    for tag, numerator in (("num", True), ("unit", False)):
+        d = torch.from_numpy(f["nc/depth"]).requires_grad_()
+        al = torch.from_numpy(f["nc/alpha"]).requires_grad_()
+        v = torch.from_numpy(f["nc/nnum" if numerator else "nc/normals"]).requires_grad_()
+        loss = ops.normal_consistency(d, K, al, v, torch.from_numpy(f["nc/mask"]), numerator)
+        np.testing.assert_allclose(loss.item(), f[f"nc/{tag}/loss"], rtol=1e-6)
+        gd, gal, gv = torch.autograd.grad(loss, (d, al, v), allow_unused=True)
+        np.testing.assert_allclose(gd.numpy(), f[f"nc/{tag}/gdepth"], rtol=1e-4, atol=1e-7)
+        np.testing.assert_allclose(torch.zeros_like(al) if gal is None else gal, f[f"nc/{tag}/galpha"], atol=1e-9)
+        np.testing.assert_allclose(gv.numpy(), f[f"nc/{tag}/gvec"], atol=1e-9)
+    grad, absgrad, radii = (torch.from_numpy(f[f"dens/{k}"]) for k in ("grad", "absgrad", "radii"))
+    for space, scale in (("pixel", (1.0, 1.0)), ("ndc", (20.0, 12.0))):
+        for kind, g2 in (("grad", grad), ("abs", absgrad)):
+            acc, obs = torch.zeros(len(radii)), torch.zeros(len(radii))
+            for _ in range(2):
+                ops.densify_observe(acc, obs, g2, radii, scale)
+            np.testing.assert_allclose(acc.numpy(), f[f"dens/{space}/{kind}/gradient"], rtol=1e-6)
+            np.testing.assert_array_equal(obs.numpy(), f[f"dens/{space}/{kind}/observations"])
