@@ -23,6 +23,13 @@ namespace {
 
 constexpr int REC4 = SF_RECORD_FLOATS / 4;  // float4 per record
 constexpr int ACC = 24;                      // accumulator floats per batch slot (20 + absgrad 2 + pad)
+// The backward's per-batch accumulator covers record slots [BASE, 24) of each Gaussian:
+// GOF never produces adjoints for slots 0-3 (xy and the 2D conic), so its accumulator
+// starts at slot 4 and is 20 floats (5 float4) wide; the other modes use all 24.
+template <int MODE> struct AccWindow {
+  static constexpr int BASE = MODE == SF_MODE_GOF ? 4 : 0;
+  static constexpr int N = ACC - BASE;
+};
 
 // first slot of a pixel's contiguous L1 sample run (fixed capacity or CSR); ptid is
 // the row-major index of the pixel inside its tile
@@ -587,7 +594,8 @@ template <int MODE, int DIST>
 __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const RasterBwdArgs a) {
   __shared__ float4 s_rec[TILE_PIXELS * REC4];
   __shared__ int s_id[TILE_PIXELS];
-  __shared__ float s_acc[TILE_PIXELS * ACC];
+  constexpr int AB = AccWindow<MODE>::BASE, AN = AccWindow<MODE>::N;
+  __shared__ float s_acc[TILE_PIXELS * AN];
   __shared__ int s_max;
   constexpr int NV = SampleLayout<MODE>::NV;
   const int tile = blockIdx.x;
@@ -666,7 +674,7 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
       if (comp == 0) s_id[slot] = id;
       s_rec[q] = __ldg(reinterpret_cast<const float4*>(a.records) + (int64_t)id * REC4 + comp);
     }
-    for (int q = tid; q < n_in * ACC; q += TILE_PIXELS) s_acc[q] = 0.f;
+    for (int q = tid; q < n_in * AN; q += TILE_PIXELS) s_acc[q] = 0.f;
     __syncthreads();
     for (int g = ((n_in + 31) >> 5) - 1; g >= 0; --g) {
      unsigned m = warp_cull(s_rec, n_in, g, lane, wx0, wx1, wy0, wy1, ext2);
@@ -722,18 +730,18 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
         const float r = reduce16_transposed(v16, lane);
         const int qi = lane >> 1;
         if ((lane & 1) == 0 && qi < NV && qi < 16 && r != 0.f)
-          atomicAdd(&s_acc[j * ACC + SampleLayout<MODE>::slot(qi)], r);
+          atomicAdd(&s_acc[j * AN + SampleLayout<MODE>::slot(qi) - AB], r);
 #pragma unroll
         for (int q = 16; q < NV; ++q) {
           const float t = warp_sum(vals[q]);
-          if (lane == 2 * (q - 16) + 1 && t != 0.f) atomicAdd(&s_acc[j * ACC + SampleLayout<MODE>::slot(q)], t);
+          if (lane == 2 * (q - 16) + 1 && t != 0.f) atomicAdd(&s_acc[j * AN + SampleLayout<MODE>::slot(q) - AB], t);
         }
       }
      }
     }
     __syncthreads();
-    for (int q = tid; q < n_in * (ACC / 4); q += TILE_PIXELS) {
-      const int slot = q / (ACC / 4), c4 = q - slot * (ACC / 4);
+    for (int q = tid; q < n_in * (AN / 4); q += TILE_PIXELS) {
+      const int slot = q / (AN / 4), c4 = q - slot * (AN / 4) + AB / 4;
       const float4 val = reinterpret_cast<const float4*>(s_acc)[q];
       if (val.x == 0.f && val.y == 0.f && val.z == 0.f && val.w == 0.f) continue;
       const int id = s_id[slot];
