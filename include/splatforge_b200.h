@@ -294,6 +294,20 @@ int sf_b200_depth_normals_backward(const float* depth, const float* K, int32_t w
  *   grad_depth [H,W], grad_alpha [H,W] (zero in the normals case), grad_vector [H,W,3]
  *   (for whichever of normal_numerator / normals was given), plus a grad_normals [H,W,3]
  *   scratch.  Each may be NULL except grad_depth and grad_normals. */
+/* gaussian.sh_ambiguity@1 (reference.py:116-117): coefficients [N,K,3] -> [N], the sum of
+ * squares outside the DC band; the backward maps grad [N] to grad_coefficients [N,K,3].
+ * gaussian.ray_color_variance@2 (reference.py:189-191), and @1 with batches = 1
+ * (reference.py:120-122): weights [B,N,P], colors [B,N,3], composite [B,P,3] -> [B,P],
+ * sum_n w |c - composite|^2 with weights and composite detached; the backward maps
+ * grad [B,P] to grad_colors [B,N,3]. */
+int sf_b200_sh_ambiguity(const float* coefficients, int64_t n, int32_t k, float* out, void* stream);
+int sf_b200_sh_ambiguity_backward(const float* coefficients, int64_t n, int32_t k, const float* grad,
+                                  float* grad_coefficients, void* stream);
+int sf_b200_ray_color_variance(const float* weights, const float* colors, const float* composite,
+                               int64_t batches, int64_t n, int64_t pixels, float* out, void* stream);
+int sf_b200_ray_color_variance_backward(const float* weights, const float* colors, const float* composite,
+                                        const float* grad, int64_t batches, int64_t n, int64_t pixels,
+                                        float* grad_colors, void* stream);
 int sf_b200_patch_zncc(const float* a, const float* b, const float* mask, int64_t rows, int32_t samples,
                        float epsilon, float* correlation, uint8_t* valid, void* stream);
 int sf_b200_patch_zncc_backward(const float* a, const float* b, const float* mask, int64_t rows,

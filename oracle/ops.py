@@ -254,3 +254,15 @@ def densify_observe(gradient, observations, grad2d, radii, scale=(1.0, 1.0)):
     g = grad2d.reshape(-1, 2) * grad2d.new_tensor(scale)
     gradient += torch.where(seen, torch.linalg.vector_norm(g, dim=-1), torch.zeros_like(gradient))
     observations += seen.to(observations.dtype)
+
+
+def sh_ambiguity(coefficients):
+    """``gaussian.sh_ambiguity@1`` (reference.py:116-117): squared norm outside the DC band."""
+    return (coefficients[:, 1:] * coefficients[:, 1:]).sum((1, 2))
+
+
+def ray_color_variance_batch(weights, colors, composite):
+    """``gaussian.ray_color_variance@2`` (reference.py:189-191): per batch and pixel,
+    sum_n stopgrad(w) |c_n - stopgrad(composite)|^2."""
+    diff = colors[:, :, None, :] - composite.detach()[:, None, :, :]
+    return (weights.detach() * (diff * diff).sum(-1)).sum(1)

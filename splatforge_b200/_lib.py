@@ -111,6 +111,10 @@ _SIGNATURES = {
     "sf_b200_ray_peak": (ctypes.c_int, [P, P, c_int64, P, P, c_int64, P, P, P, P]),
     "sf_b200_depth_normals": (ctypes.c_int, [P, P, c_int32, c_int32, P, P, P]),
     "sf_b200_depth_normals_backward": (ctypes.c_int, [P, P, c_int32, c_int32, P, P, P, P]),
+    "sf_b200_sh_ambiguity": (ctypes.c_int, [P, c_int64, c_int32, P, P]),
+    "sf_b200_sh_ambiguity_backward": (ctypes.c_int, [P, c_int64, c_int32, P, P, P]),
+    "sf_b200_ray_color_variance": (ctypes.c_int, [P, P, P, c_int64, c_int64, c_int64, P, P]),
+    "sf_b200_ray_color_variance_backward": (ctypes.c_int, [P, P, P, P, c_int64, c_int64, c_int64, P, P]),
     "sf_b200_patch_zncc": (ctypes.c_int, [P, P, P, c_int64, c_int32, c_float, P, P, P]),
     "sf_b200_patch_zncc_backward": (ctypes.c_int, [P, P, P, c_int64, c_int32, c_float, P, P, P, P]),
     "sf_b200_densify_observe": (ctypes.c_int, [P, P, c_int64, c_float, c_float, P, P, P]),

@@ -528,6 +528,42 @@ int sf_b200_alpha_composite_backward(const float* alphas, const float* colors, c
 }
 
 // ------------------------------------------------------------------ training-step operations
+int sf_b200_sh_ambiguity(const float* coefficients, int64_t n, int32_t k, float* out, void* stream) {
+  if (n < 0 || k < 1) return fail(SF_ERR_ARGUMENT, "sh_ambiguity: bad sizes");
+  if (n > 0 && (!coefficients || !out)) return fail(SF_ERR_ARGUMENT, "sh_ambiguity: NULL buffer");
+  return cuda_status(sf::launch_sh_ambiguity(coefficients, n, k, out, as_stream(stream)), "sh_ambiguity");
+}
+
+int sf_b200_sh_ambiguity_backward(const float* coefficients, int64_t n, int32_t k, const float* grad,
+                                  float* grad_coefficients, void* stream) {
+  if (n < 0 || k < 1) return fail(SF_ERR_ARGUMENT, "sh_ambiguity_backward: bad sizes");
+  if (n > 0 && (!coefficients || !grad || !grad_coefficients))
+    return fail(SF_ERR_ARGUMENT, "sh_ambiguity_backward: NULL buffer");
+  return cuda_status(sf::launch_sh_ambiguity_backward(coefficients, n, k, grad, grad_coefficients, as_stream(stream)),
+                     "sh_ambiguity_backward");
+}
+
+int sf_b200_ray_color_variance(const float* weights, const float* colors, const float* composite, int64_t batches,
+                               int64_t n, int64_t pixels, float* out, void* stream) {
+  if (batches < 0 || n < 0 || pixels < 0) return fail(SF_ERR_ARGUMENT, "ray_color_variance: negative size");
+  if (batches * pixels > 0 && (!composite || !out || (n > 0 && (!weights || !colors))))
+    return fail(SF_ERR_ARGUMENT, "ray_color_variance: NULL buffer");
+  return cuda_status(sf::launch_ray_color_variance(weights, colors, composite, batches, n, pixels, out,
+                                                   as_stream(stream)),
+                     "ray_color_variance");
+}
+
+int sf_b200_ray_color_variance_backward(const float* weights, const float* colors, const float* composite,
+                                        const float* grad, int64_t batches, int64_t n, int64_t pixels,
+                                        float* grad_colors, void* stream) {
+  if (batches < 0 || n < 0 || pixels < 0) return fail(SF_ERR_ARGUMENT, "ray_color_variance_backward: negative size");
+  if (batches * n > 0 && (!weights || !colors || !grad_colors || (pixels > 0 && (!composite || !grad))))
+    return fail(SF_ERR_ARGUMENT, "ray_color_variance_backward: NULL buffer");
+  return cuda_status(sf::launch_ray_color_variance_backward(weights, colors, composite, grad, batches, n, pixels,
+                                                            grad_colors, as_stream(stream)),
+                     "ray_color_variance_backward");
+}
+
 int sf_b200_patch_zncc(const float* a, const float* b, const float* mask, int64_t rows, int32_t samples, float epsilon,
                        float* correlation, uint8_t* valid, void* stream) {
   if (rows < 0 || samples < 0) return fail(SF_ERR_ARGUMENT, "patch_zncc: negative size");

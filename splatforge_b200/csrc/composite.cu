@@ -266,4 +266,68 @@ cudaError_t launch_composite_backward(const float* al, const float* col, const f
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------ ray colour variance
+// gaussian.ray_color_variance@1/@2 (reference.py:120-122, 189-191): per batch b and pixel
+// p, sum_n w[b,n,p] |c[b,n] - composite[b,p]|^2 with the weights and the composite
+// detached; the adjoint reaches the colours only: g_c[b,n] = 2 sum_p g[b,p] w[b,n,p]
+// (c[b,n] - composite[b,p]).
+namespace {
+__global__ void ray_color_variance_kernel(const float* w, const float* c, const float* comp, int64_t B, int64_t N,
+                                          int64_t P, float* out) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= B * P) return;
+  const int64_t b = j / P, p = j - b * P;
+  const float r0 = comp[j * 3], r1 = comp[j * 3 + 1], r2 = comp[j * 3 + 2];
+  float acc = 0.f;
+  for (int64_t n = 0; n < N; ++n) {
+    const float* cn = c + (b * N + n) * 3;
+    const float e0 = cn[0] - r0, e1 = cn[1] - r1, e2 = cn[2] - r2;
+    acc += w[(b * N + n) * P + p] * (e0 * e0 + e1 * e1 + e2 * e2);
+  }
+  out[j] = acc;
+}
+
+// one warp per (b, n)
+__global__ void ray_color_variance_backward_kernel(const float* w, const float* c, const float* comp, const float* g,
+                                                   int64_t B, int64_t N, int64_t P, float* g_c) {
+  const int64_t k = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (k >= B * N) return;
+  const int64_t b = k / N;
+  const float c0 = c[k * 3], c1 = c[k * 3 + 1], c2 = c[k * 3 + 2];
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+  for (int64_t p = lane; p < P; p += 32) {
+    const float s = 2.f * g[b * P + p] * w[k * P + p];
+    const float* r = comp + (b * P + p) * 3;
+    a0 += s * (c0 - r[0]);
+    a1 += s * (c1 - r[1]);
+    a2 += s * (c2 - r[2]);
+  }
+  a0 = warp_sum(a0);
+  a1 = warp_sum(a1);
+  a2 = warp_sum(a2);
+  if (lane == 0) {
+    g_c[k * 3] = a0;
+    g_c[k * 3 + 1] = a1;
+    g_c[k * 3 + 2] = a2;
+  }
+}
+}  // namespace
+
+cudaError_t launch_ray_color_variance(const float* w, const float* c, const float* comp, int64_t B, int64_t N,
+                                      int64_t P, float* out, cudaStream_t s) {
+  if (B * P == 0) return cudaSuccess;
+  count_launches(1);
+  ray_color_variance_kernel<<<(unsigned)((B * P + 255) / 256), 256, 0, s>>>(w, c, comp, B, N, P, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ray_color_variance_backward(const float* w, const float* c, const float* comp, const float* g,
+                                               int64_t B, int64_t N, int64_t P, float* g_c, cudaStream_t s) {
+  if (B * N == 0) return cudaSuccess;
+  count_launches(1);
+  ray_color_variance_backward_kernel<<<(unsigned)((B * N + 7) / 8), 256, 0, s>>>(w, c, comp, g, B, N, P, g_c);
+  return cudaGetLastError();
+}
+
 }  // namespace sf

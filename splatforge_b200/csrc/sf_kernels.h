@@ -189,4 +189,13 @@ cudaError_t normal_consistency_backward(const float* depth, const float* K, int 
                                         const int64_t* count, float* g_depth, float* g_alpha, float* g_vec,
                                         float* g_normals, void* ws, cudaStream_t s);
 
+// gaussian.sh_ambiguity@1 (training.cu), gaussian.ray_color_variance@1/@2 (composite.cu)
+cudaError_t launch_sh_ambiguity(const float* coeffs, int64_t n, int K, float* out, cudaStream_t s);
+cudaError_t launch_sh_ambiguity_backward(const float* coeffs, int64_t n, int K, const float* g, float* g_coeffs,
+                                         cudaStream_t s);
+cudaError_t launch_ray_color_variance(const float* w, const float* c, const float* comp, int64_t B, int64_t N,
+                                      int64_t P, float* out, cudaStream_t s);
+cudaError_t launch_ray_color_variance_backward(const float* w, const float* c, const float* comp, const float* g,
+                                               int64_t B, int64_t N, int64_t P, float* g_c, cudaStream_t s);
+
 }  // namespace sf

@@ -6,6 +6,8 @@
 // * the densifier's statistics (src/splatforge/studio/densification.py:18-43): per
 //   Gaussian, the norm of its (optionally NDC-scaled) projected-mean gradient added to the
 //   accumulator where its radius is positive, and the visibility count.
+// * gaussian.sh_ambiguity@1 (reference.py:116-117), the AmbiSuR method's per-Gaussian
+//   score (src/splatforge/studio/methods/ambisur.py:25).
 // * the normal-consistency loss (src/splatforge/studio/losses.py:9-12, 45-53): depth normals
 //   (geometry.depth_normals@1, geometry.cu), masked by validity, alpha > 0.1 and the caller's
 //   mask, against the rendered normal numerator (alpha - n_num . n_depth) or unit normal
@@ -194,7 +196,45 @@ __global__ void nc_backward_kernel(const float* normals, const uint8_t* valid, c
   }
 }
 
+// --------------------------------------------------------------------------- SH ambiguity
+// gaussian.sh_ambiguity@1 (reference.py:116-117): sum of squares of every band but the DC
+// one, per Gaussian; the adjoint is 2 c g outside the DC band.  One warp per Gaussian.
+__global__ void sh_ambiguity_kernel(const float* coeffs, int64_t n, int K, float* out) {
+  const int64_t i = (int64_t)blockIdx.x * TR_WARPS + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  const float* c = coeffs + i * K * 3;
+  float acc = 0.f;
+  for (int k = 3 + lane; k < K * 3; k += 32) acc += c[k] * c[k];
+  acc = warp_sum(acc);
+  if (lane == 0) out[i] = acc;
+}
+
+__global__ void sh_ambiguity_backward_kernel(const float* coeffs, int64_t total, int K, const float* g,
+                                             float* g_coeffs) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= total) return;
+  const int64_t i = j / (K * 3);
+  g_coeffs[j] = (j - i * K * 3) < 3 ? 0.f : 2.f * coeffs[j] * g[i];
+}
+
 }  // namespace
+
+cudaError_t launch_sh_ambiguity(const float* coeffs, int64_t n, int K, float* out, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  count_launches(1);
+  sh_ambiguity_kernel<<<(unsigned)((n + TR_WARPS - 1) / TR_WARPS), TR_THREADS, 0, s>>>(coeffs, n, K, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sh_ambiguity_backward(const float* coeffs, int64_t n, int K, const float* g, float* g_coeffs,
+                                         cudaStream_t s) {
+  const int64_t total = n * K * 3;
+  if (total == 0) return cudaSuccess;
+  count_launches(1);
+  sh_ambiguity_backward_kernel<<<blocks_of(total), TR_THREADS, 0, s>>>(coeffs, total, K, g, g_coeffs);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_patch_zncc(const float* a, const float* b, const float* m, int64_t rows, int S, float eps,
                               float* corr, uint8_t* valid, cudaStream_t s) {

@@ -11,6 +11,9 @@ what the Torch provider's function returns:
 * ``opacity_field(points, means, inverse_covariances, opacities, origins, *, gaussian_chunk)``
                                                      gaussian.opacity_field@1 (reference.py:194-222)
 * ``patch_zncc(a, b, mask, *, epsilon)``             matching.patch_zncc@1 (reference.py:225-236)
+* ``sh_ambiguity(coefficients)``                     gaussian.sh_ambiguity@1 (reference.py:116-117)
+* ``ray_color_variance(w, c, composite)`` / ``ray_color_variance_batch(...)``
+                                                     gaussian.ray_color_variance@1/@2 (reference.py:120-122, 189-191)
 
 They accept CUDA float32 tensors only and raise ``ValueError`` otherwise, like the
 reference's CUDA composite provider (cuda_composite.py:79-85); nothing falls back
@@ -280,6 +283,78 @@ class OpacityFieldPlan:
                      self.max_view_pairs, _ptr(self.origins), _ptr(part), part.shape[0], _ptr(out[start:]),
                      _ptr(self._ws), self._ws.numel(), _stream(dev))
         return out
+
+
+# ---------------------------------------------------------------- gaussian.sh_ambiguity@1
+class _ShAmbiguity(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, coeffs):
+        dev = coeffs.device
+        c = coeffs.contiguous()
+        n, K = c.shape[0], c.shape[1]
+        out = torch.empty((n,), device=dev, dtype=torch.float32)
+        with torch.cuda.device(dev):
+            call("sf_b200_sh_ambiguity", _ptr(c), n, K, _ptr(out), _stream(dev))
+        ctx.save_for_backward(c)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        (c,) = ctx.saved_tensors
+        dev = c.device
+        gc = torch.empty_like(c)
+        gg = g.contiguous().float()
+        with torch.cuda.device(dev):
+            call("sf_b200_sh_ambiguity_backward", _ptr(c), c.shape[0], c.shape[1], _ptr(gg), _ptr(gc), _stream(dev))
+        return gc
+
+
+def sh_ambiguity(coefficients):
+    """``gaussian.sh_ambiguity@1``: squared norm of the SH coefficients [N,K,3] outside
+    the DC band -> [N] (reference.py:116-117); differentiable."""
+    _require_cuda_f32("gaussian.sh_ambiguity@1", coefficients)
+    return _ShAmbiguity.apply(coefficients)
+
+
+# ---------------------------------------------------------------- gaussian.ray_color_variance@1/@2
+class _RayColorVariance(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, weights, colors, composite):
+        dev = colors.device
+        w, c, r = (t.detach().contiguous() for t in (weights, colors, composite))
+        B, N, P = w.shape
+        out = torch.empty((B, P), device=dev, dtype=torch.float32)
+        with torch.cuda.device(dev):
+            call("sf_b200_ray_color_variance", _ptr(w), _ptr(c), _ptr(r), B, N, P, _ptr(out), _stream(dev))
+        ctx.save_for_backward(w, c, r)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        w, c, r = ctx.saved_tensors
+        dev = c.device
+        B, N, P = w.shape
+        gc = torch.empty_like(c)
+        gg = g.contiguous().float()
+        with torch.cuda.device(dev):
+            call("sf_b200_ray_color_variance_backward", _ptr(w), _ptr(c), _ptr(r), _ptr(gg), B, N, P, _ptr(gc),
+                 _stream(dev))
+        return None, gc, None
+
+
+def ray_color_variance_batch(weights, colors, composite):
+    """``gaussian.ray_color_variance@2``: weights [B,N,P], colors [B,N,3], composite [B,P,3]
+    -> [B,P] = sum_n stopgrad(w) |c - stopgrad(composite)|^2; only the colours receive
+    gradients (reference.py:189-191)."""
+    _require_cuda_f32("gaussian.ray_color_variance@2", weights, colors, composite)
+    return _RayColorVariance.apply(weights, colors, composite)
+
+
+def ray_color_variance(weights, colors, composite):
+    """``gaussian.ray_color_variance@1``: the single-batch form, weights [N,P], colors
+    [N,3], composite [P,3] -> [P] (reference.py:120-122)."""
+    _require_cuda_f32("gaussian.ray_color_variance@1", weights, colors, composite)
+    return _RayColorVariance.apply(weights[None], colors[None], composite[None])[0]
 
 
 # ---------------------------------------------------------------- matching.patch_zncc@1

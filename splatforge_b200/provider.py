@@ -50,6 +50,14 @@ _OPS = {
                                  "sf_b200_depth_normals", "sm100a-float32", True, ("geometry.cu",)),
     "matching.patch_zncc@1": ("splatforge_b200.native_cuda.patch_zncc.v1", ops.patch_zncc, "sf_b200_patch_zncc",
                               "sm100a-float32", True, ("training.cu", "sf_device.cuh")),
+    "gaussian.sh_ambiguity@1": ("splatforge_b200.native_cuda.sh_ambiguity.v1", ops.sh_ambiguity,
+                                "sf_b200_sh_ambiguity", "sm100a-float32", True, ("training.cu", "sf_device.cuh")),
+    "gaussian.ray_color_variance@1": ("splatforge_b200.native_cuda.ray_color_variance.v1", ops.ray_color_variance,
+                                      "sf_b200_ray_color_variance", "sm100a-float32", True,
+                                      ("composite.cu", "sf_device.cuh")),
+    "gaussian.ray_color_variance@2": ("splatforge_b200.native_cuda.ray_color_variance.v2",
+                                      ops.ray_color_variance_batch, "sf_b200_ray_color_variance",
+                                      "sm100a-float32-batched", True, ("composite.cu", "sf_device.cuh")),
 }
 
 # Additional implementations of an operator already listed above, selected explicitly

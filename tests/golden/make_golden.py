@@ -20,6 +20,8 @@ Fixtures (all float32 unless noted):
                        test case) and sphere, and the GOF exporter's gaussian_grid
                        (with and without max_gaussians) plus the level set of the
                        opacity field of a 300-Gaussian scene (float64 grid).
+* ``ops_extra.npz`` -- gaussian.sh_ambiguity@1 and gaussian.ray_color_variance@1/@2 with
+                       the adjoints of seeded linear losses.
 * ``training.npz``  -- matching.patch_zncc@1 (with its a/b adjoints), the
                        normal-consistency loss (numerator and unit-normal forms, with
                        input gradients) and GaussianDensifier.observe statistics.
@@ -259,6 +261,36 @@ def mesh_cases():
     np.savez_compressed(HERE / "mesh.npz", **out)
 
 
+def extra_op_cases():
+    """gaussian.sh_ambiguity@1 and gaussian.ray_color_variance@1/@2 with the adjoints of
+    seeded linear losses."""
+    from splatforge.gaussian import SurfaceOperators
+
+    ops = SurfaceOperators()
+    g = torch.Generator().manual_seed(31)
+    out = {}
+    sh = torch.randn(57, 16, 3, generator=g).requires_grad_()
+    amb = ops("gaussian.sh_ambiguity@1", sh)
+    up = torch.randn(57, generator=g)
+    (gsh,) = torch.autograd.grad((amb * up).sum(), sh)
+    out.update({"amb/sh": sh.detach().numpy(), "amb/out": amb.detach().numpy(), "amb/up": up.numpy(),
+                "amb/gsh": gsh.numpy()})
+    B, N, P = 3, 37, 256
+    w = torch.rand(B, N, P, generator=g) * 0.1
+    c = torch.rand(B, N, 3, generator=g).requires_grad_()
+    r = torch.rand(B, P, 3, generator=g)
+    var = ops("gaussian.ray_color_variance@2", w, c, r)
+    upv = torch.randn(B, P, generator=g)
+    (gc,) = torch.autograd.grad((var * upv).sum(), c)
+    c1 = c.detach()[0].clone().requires_grad_()
+    var1 = ops("gaussian.ray_color_variance@1", w[0], c1, r[0])
+    (gc1,) = torch.autograd.grad((var1 * upv[0]).sum(), c1)
+    out.update({"rcv/w": w.numpy(), "rcv/c": c.detach().numpy(), "rcv/r": r.numpy(), "rcv/out": var.detach().numpy(),
+                "rcv/up": upv.numpy(), "rcv/gc": gc.numpy(), "rcv/out1": var1.detach().numpy(),
+                "rcv/gc1": gc1.numpy()})
+    np.savez_compressed(HERE / "ops_extra.npz", **out)
+
+
 def training_cases():
     """matching.patch_zncc@1 (forward and the a/b adjoints of a seeded linear loss, with
     short, constant, perfectly correlated and anti-correlated patches), the
@@ -440,7 +472,7 @@ def render_cases():
 
 if __name__ == "__main__":
     _setup(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
-    which = sys.argv[2:] or ["binning", "ops", "geometry", "mesh", "training", "render"]
+    which = sys.argv[2:] or ["binning", "ops", "extra", "geometry", "mesh", "training", "render"]
     if "binning" in which:
         binning_cases()
     if "ops" in which:
@@ -451,6 +483,8 @@ if __name__ == "__main__":
         mesh_cases()
     if "training" in which:
         training_cases()
+    if "extra" in which:
+        extra_op_cases()
     if "render" in which:
         render_cases()
     for f in sorted(HERE.glob("*.npz")):

@@ -116,3 +116,24 @@ def test_densify_observe_matches_reference(golden, space, absolute):
     np.testing.assert_array_equal(dens.observations.cpu().numpy(), f[f"{key}/observations"])
     with pytest.raises(ValueError, match="do not match"):
         training.observe(dens, out, SimpleNamespace(count=n + 1))
+
+
+def test_sh_ambiguity_and_ray_color_variance_match_reference(golden):
+    """gaussian.sh_ambiguity@1 and gaussian.ray_color_variance@1/@2 (values and the
+    adjoints of seeded linear losses) against the reference."""
+    f = golden("ops_extra")
+    sh = T(f["amb/sh"]).requires_grad_()
+    amb = ops.sh_ambiguity(sh)
+    np.testing.assert_allclose(amb.detach().cpu().numpy(), f["amb/out"], rtol=1e-5)
+    (g,) = torch.autograd.grad((amb * T(f["amb/up"])).sum(), sh)
+    np.testing.assert_allclose(g.cpu().numpy(), f["amb/gsh"], rtol=1e-5, atol=1e-7)
+    c = T(f["rcv/c"]).requires_grad_()
+    var = ops.ray_color_variance_batch(T(f["rcv/w"]), c, T(f["rcv/r"]))
+    np.testing.assert_allclose(var.detach().cpu().numpy(), f["rcv/out"], rtol=1e-5, atol=1e-6)
+    (gc,) = torch.autograd.grad((var * T(f["rcv/up"])).sum(), c)
+    np.testing.assert_allclose(gc.cpu().numpy(), f["rcv/gc"], rtol=1e-4, atol=1e-5)
+    c1 = T(f["rcv/c"][0]).requires_grad_()
+    var1 = ops.ray_color_variance(T(f["rcv/w"][0]), c1, T(f["rcv/r"][0]))
+    np.testing.assert_allclose(var1.detach().cpu().numpy(), f["rcv/out1"], rtol=1e-5, atol=1e-6)
+    (gc1,) = torch.autograd.grad((var1 * T(f["rcv/up"][0])).sum(), c1)
+    np.testing.assert_allclose(gc1.cpu().numpy(), f["rcv/gc1"], rtol=1e-4, atol=1e-5)

@@ -243,3 +243,18 @@ def test_training_ops_oracle_matches_reference(golden):
                 ops.densify_observe(acc, obs, g2, radii, scale)
             np.testing.assert_allclose(acc.numpy(), f[f"dens/{space}/{kind}/gradient"], rtol=1e-6)
             np.testing.assert_array_equal(obs.numpy(), f[f"dens/{space}/{kind}/observations"])
+
+
+def test_extra_ops_oracle_matches_reference(golden):
+    f = golden("ops_extra")
+    sh = torch.from_numpy(f["amb/sh"]).requires_grad_()
+    amb = ops.sh_ambiguity(sh)
+    np.testing.assert_allclose(amb.detach().numpy(), f["amb/out"], rtol=1e-6)
+    (g,) = torch.autograd.grad((amb * torch.from_numpy(f["amb/up"])).sum(), sh)
+    np.testing.assert_allclose(g.numpy(), f["amb/gsh"], rtol=1e-6)
+    c = torch.from_numpy(f["rcv/c"]).requires_grad_()
+    var = ops.ray_color_variance_batch(torch.from_numpy(f["rcv/w"]), c, torch.from_numpy(f["rcv/r"]))
+    np.testing.assert_allclose(var.detach().numpy(), f["rcv/out"], rtol=1e-5, atol=1e-6)
+    (gc,) = torch.autograd.grad((var * torch.from_numpy(f["rcv/up"])).sum(), c)
+    np.testing.assert_allclose(gc.numpy(), f["rcv/gc"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(var.detach().numpy()[0], f["rcv/out1"], rtol=1e-5, atol=1e-6)
