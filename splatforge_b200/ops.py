@@ -145,6 +145,22 @@ def alpha_composite_selected(alphas, colors, depths, normals, *, distortions):
         return _Composite.apply(alphas, colors, depths, normals, _lib.DISTORTIONS[distortions])
 
 
+def alpha_composite_batch(alphas, colors, depths, normals):
+    """``splat.alpha_composite@2``: the batched composite with both distortion terms
+    (reference.py:151-179), the @3 kernel with distortions "both"."""
+    dev = _require_cuda_f32("splat.alpha_composite@2", alphas, colors, depths, normals)
+    with torch.cuda.device(dev):
+        return _Composite.apply(alphas, colors, depths, normals, _lib.DISTORTIONS["both"])
+
+
+def alpha_composite(alphas, colors, depths, normals):
+    """``splat.alpha_composite@1``: one front-to-back composite, alphas [N,P], colors
+    [N,3], depths [N,P], normals [N,P,3] (reference.py:125-148); the same 8-tuple without
+    the batch axis."""
+    outs = alpha_composite_batch(alphas[None], colors[None], depths[None], normals[None])
+    return tuple(o[0] for o in outs)
+
+
 # ---------------------------------------------------------------- gaussian.opacity_field@1
 # Two implementations: ``opacity_field`` evaluates every (point, Gaussian, origin)
 # triple and never synchronises; ``opacity_field_culled`` walks per-view candidate

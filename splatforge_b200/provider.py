@@ -40,6 +40,12 @@ _OPS = {
     "splat.alpha_composite@3": ("splatforge_b200.native_cuda.alpha_composite.v3", ops.alpha_composite_selected,
                                 "sf_b200_alpha_composite_forward", "sm100a-float32-selected", True,
                                 ("composite.cu", "sf_device.cuh")),
+    "splat.alpha_composite@2": ("splatforge_b200.native_cuda.alpha_composite.v2", ops.alpha_composite_batch,
+                                "sf_b200_alpha_composite_forward", "sm100a-float32-batched", True,
+                                ("composite.cu", "sf_device.cuh")),
+    "splat.alpha_composite@1": ("splatforge_b200.native_cuda.alpha_composite.v1", ops.alpha_composite,
+                                "sf_b200_alpha_composite_forward", "sm100a-float32", True,
+                                ("composite.cu", "sf_device.cuh")),
     "gaussian.opacity_field@1": ("splatforge_b200.native_cuda.opacity_field.v1", ops.opacity_field,
                                  "sf_b200_opacity_field", "sm100a-float32-forward", False, ("opacity_field.cu",)),
     "camera.pixel_rays@1": ("splatforge_b200.native_cuda.pixel_rays.v1", ops.pixel_rays, "sf_b200_pixel_rays",

@@ -20,8 +20,8 @@ Fixtures (all float32 unless noted):
                        test case) and sphere, and the GOF exporter's gaussian_grid
                        (with and without max_gaussians) plus the level set of the
                        opacity field of a 300-Gaussian scene (float64 grid).
-* ``ops_extra.npz`` -- gaussian.sh_ambiguity@1 and gaussian.ray_color_variance@1/@2 with
-                       the adjoints of seeded linear losses.
+* ``ops_extra.npz`` -- gaussian.sh_ambiguity@1, gaussian.ray_color_variance@1/@2 and
+                       splat.alpha_composite@1 with the adjoints of seeded linear losses.
 * ``training.npz``  -- matching.patch_zncc@1 (with its a/b adjoints), the
                        normal-consistency loss (numerator and unit-normal forms, with
                        input gradients) and GaussianDensifier.observe statistics.
@@ -288,6 +288,20 @@ def extra_op_cases():
     out.update({"rcv/w": w.numpy(), "rcv/c": c.detach().numpy(), "rcv/r": r.numpy(), "rcv/out": var.detach().numpy(),
                 "rcv/up": upv.numpy(), "rcv/gc": gc.numpy(), "rcv/out1": var1.detach().numpy(),
                 "rcv/gc1": gc1.numpy()})
+    # splat.alpha_composite@1 (TorchRenderer's unbatched composite) with input gradients
+    N, P = 23, 64
+    al = (torch.rand(N, P, generator=g) * 0.9).requires_grad_()
+    col = torch.rand(N, 3, generator=g).requires_grad_()
+    dep = (1 + torch.rand(N, P, generator=g) * 3).requires_grad_()
+    nrm = torch.randn(N, P, 3, generator=g).requires_grad_()
+    res = ops("splat.alpha_composite@1", al, col, dep, nrm)
+    ups = [torch.randn(r.shape, generator=g) for r in res]
+    grads = torch.autograd.grad(sum((r * u).sum() for r, u in zip(res, ups)), (al, col, dep, nrm))
+    out.update({"c1/a": al.detach().numpy(), "c1/c": col.detach().numpy(), "c1/d": dep.detach().numpy(),
+                "c1/n": nrm.detach().numpy()})
+    out.update({f"c1/out{i}": r.detach().numpy() for i, r in enumerate(res)})
+    out.update({f"c1/up{i}": u.numpy() for i, u in enumerate(ups)})
+    out.update({f"c1/g{k}": gr.numpy() for k, gr in zip("acdn", grads)})
     np.savez_compressed(HERE / "ops_extra.npz", **out)
 
 

@@ -137,3 +137,21 @@ def test_sh_ambiguity_and_ray_color_variance_match_reference(golden):
     np.testing.assert_allclose(var1.detach().cpu().numpy(), f["rcv/out1"], rtol=1e-5, atol=1e-6)
     (gc1,) = torch.autograd.grad((var1 * T(f["rcv/up"][0])).sum(), c1)
     np.testing.assert_allclose(gc1.cpu().numpy(), f["rcv/gc1"], rtol=1e-4, atol=1e-5)
+
+
+def test_alpha_composite_v1_and_v2_runners_match_reference(golden):
+    """splat.alpha_composite@1 (TorchRenderer's unbatched call) against the reference, and
+    @2 against the ops fixture's batched case with both distortions."""
+    f = golden("ops_extra")
+    ins = [T(f[f"c1/{k}"]).requires_grad_() for k in "acdn"]
+    res = ops.alpha_composite(*ins)
+    assert len(res) == 8
+    for i, r in enumerate(res):
+        np.testing.assert_allclose(r.detach().cpu().numpy(), f[f"c1/out{i}"], atol=1e-5)
+    loss = sum((r * T(f[f"c1/up{i}"])).sum() for i, r in enumerate(res))
+    for k, gr in zip("acdn", torch.autograd.grad(loss, ins)):
+        np.testing.assert_allclose(gr.cpu().numpy(), f[f"c1/g{k}"], atol=1e-4)
+    g = golden("ops")
+    ins = [T(g[f"comp/{k}"]) for k in "acdn"]
+    for i, r in enumerate(ops.alpha_composite_batch(*ins)):
+        np.testing.assert_allclose(r.cpu().numpy(), g[f"comp/both/out{i}"], atol=1e-5)

@@ -258,3 +258,15 @@ def test_extra_ops_oracle_matches_reference(golden):
     (gc,) = torch.autograd.grad((var * torch.from_numpy(f["rcv/up"])).sum(), c)
     np.testing.assert_allclose(gc.numpy(), f["rcv/gc"], rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(var.detach().numpy()[0], f["rcv/out1"], rtol=1e-5, atol=1e-6)
+
+
+def test_unbatched_composite_oracle_matches_reference(golden):
+    """splat.alpha_composite@1 is the batched composite (both distortions) on one batch."""
+    f = golden("ops_extra")
+    ins = [torch.from_numpy(f[f"c1/{k}"])[None].requires_grad_() for k in "acdn"]
+    res = ops.alpha_composite_batch(*ins, distortions="both")
+    for i, r in enumerate(res):
+        np.testing.assert_allclose(r[0].detach().numpy(), f[f"c1/out{i}"], atol=1e-6)
+    loss = sum((r[0] * torch.from_numpy(f[f"c1/up{i}"])).sum() for i, r in enumerate(res))
+    for k, gr in zip("acdn", torch.autograd.grad(loss, ins)):
+        np.testing.assert_allclose(gr[0].numpy(), f[f"c1/g{k}"], atol=2e-5)

@@ -89,7 +89,8 @@ def test_geometry_ops_and_the_culled_field_register():
     runtime = create_surface_runtime(implementations=provider.implementations(), capabilities=provider.capabilities())
     sel = provider.selection()
     for op in ("camera.pixel_rays@1", "gaussian.ray_peak@1", "geometry.depth_normals@1", "matching.patch_zncc@1",
-               "gaussian.sh_ambiguity@1", "gaussian.ray_color_variance@1", "gaussian.ray_color_variance@2"):
+               "gaussian.sh_ambiguity@1", "gaussian.ray_color_variance@1", "gaussian.ray_color_variance@2",
+               "splat.alpha_composite@1", "splat.alpha_composite@2"):
         impl = runtime.implementations.get(sel[op])
         assert impl is not None and str(impl.manifest.op_key) == op
     assert runtime.implementations.get(sel["geometry.depth_normals@1"]).manifest.eligibility.backward is True
