@@ -40,7 +40,7 @@ def _check(fix, out, p, v, profile):
         if ch == "median_depth":
             assert (np.abs(got - want) > 1e-4).mean() <= 0.002, ch
             continue
-        # the north-star bar (1e-4 absolute); L2 is a difference of moments that amplifies
+        # the image bar (1e-4 absolute); L2 is a difference of moments that amplifies
         # the rounding of the reference's LAPACK 2x2 inverse and eigenvalue
         atol = 2e-4 if ch == "distortion_l2" else 1e-4
         rtol = 1e-4 if ch.startswith("distortion") or ch == "depth" else 0.0
