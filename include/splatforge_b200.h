@@ -167,9 +167,14 @@ int sf_b200_bin_emit(const int32_t* order, const int64_t* offsets, const int32_t
  * MB, held on every GPU that loads the library until exit); n is limited to
  * SF_B200_STATIC_MAX_GAUSSIANS and larger counts return SF_ERR_CAPACITY.  Calls share
  * that array: calls whose kernels overlap on the GPU race and must be serialised by
- * the caller.  The first call on a device resolves the array's device address; make
- * it before any stream capture.  Nothing is allocated or freed. */
+ * the caller.  The first call in each CUDA context resolves the array's device address
+ * in that context; make it before any stream capture, and do not use the entry point
+ * across a cudaDeviceReset in one process.  `stream` must belong to the current device
+ * (SF_ERR_ARGUMENT otherwise).  Nothing is allocated or freed. */
 #define SF_B200_STATIC_MAX_GAUSSIANS 1048576
+/* bytes of the static array (checked against the ordering workspace of
+ * SF_B200_STATIC_MAX_GAUSSIANS Gaussians, sf_b200_bin_workspace_bytes) */
+#define SF_B200_STATIC_SCRATCH_BYTES (21u << 20)
 int sf_b200_bin_order_static(const int32_t* tile_count, const uint32_t* depth_key, int64_t n,
                              int32_t* order, int64_t* offsets, void* stream);
 
@@ -234,6 +239,16 @@ int sf_b200_opacity_field_culled(const float* points, int64_t n_points, const fl
                                  float cutoff, int32_t face_cells, float* field, void* workspace,
                                  size_t workspace_bytes, int64_t max_pairs, int64_t* pairs_needed,
                                  void* stream);
+/* The same call, measured: *pairs_evaluated (a device int64, accumulated) receives the
+ * number of (query, candidate) pairs whose contribution was evaluated, and *query_ms
+ * (host, accumulated) the CUDA-event time of the per-view query kernels.  Used for
+ * the field's roofline; the values equal sf_b200_opacity_field_culled's. */
+int sf_b200_opacity_field_culled_stats(const float* points, int64_t n_points, const float* means,
+                                       const float* inverse_covariances, const float* opacities,
+                                       int64_t n_gaussians, const float* origins, int32_t n_origins,
+                                       float cutoff, int32_t face_cells, float* field, void* workspace,
+                                       size_t workspace_bytes, int64_t max_pairs, int64_t* pairs_needed,
+                                       int64_t* pairs_evaluated, float* query_ms, void* stream);
 
 /* A field plan for repeated evaluations against one Gaussian set and one origin set
  * (the GOF exporter evaluates the grid and then every bisection step against the same

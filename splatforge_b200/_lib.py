@@ -99,6 +99,11 @@ _SIGNATURES = {
         ctypes.c_int,
         [P, c_int64, P, P, P, c_int64, P, c_int32, c_float, c_int32, P, P, c_size_t, c_int64, POINTER(c_int64), P],
     ),
+    "sf_b200_opacity_field_culled_stats": (
+        ctypes.c_int,
+        [P, c_int64, P, P, P, c_int64, P, c_int32, c_float, c_int32, P, P, c_size_t, c_int64, POINTER(c_int64), P,
+         POINTER(c_float), P],
+    ),
     "sf_b200_opacity_field_plan_bytes": (ctypes.c_int, [c_int64, c_int32, c_int32, c_int64, c_int64, POINTER(c_size_t)]),
     "sf_b200_opacity_field_plan_build": (
         ctypes.c_int, [P, P, P, c_int64, P, c_int32, c_float, c_int32, P, c_size_t, c_int64, c_int64, P, P]

@@ -330,11 +330,11 @@ int sf_b200_opacity_field_culled_workspace_bytes(int64_t n_points, int64_t n_gau
   return SF_OK;
 }
 
-int sf_b200_opacity_field_culled(const float* points, int64_t n_points, const float* means,
+static int field_culled(const float* points, int64_t n_points, const float* means,
                                  const float* inverse_covariances, const float* opacities, int64_t n_gaussians,
                                  const float* origins, int32_t n_origins, float cutoff, int32_t face_cells,
                                  float* field, void* workspace, size_t workspace_bytes, int64_t max_pairs,
-                                 int64_t* pairs_needed, void* stream) {
+                                 int64_t* pairs_needed, void* stream, int64_t* pairs_evaluated, float* query_ms) {
   if (n_points < 0 || n_gaussians < 0 || max_pairs < 0) return fail(SF_ERR_ARGUMENT, "opacity_field_culled: negative size");
   if (n_origins < 1) return fail(SF_ERR_ARGUMENT, "opacity_field_culled: requires at least one origin");
   if (!(cutoff > 0.f && cutoff < 1.f)) return fail(SF_ERR_ARGUMENT, "opacity_field_culled: cutoff must be in (0, 1)");
@@ -353,7 +353,9 @@ int sf_b200_opacity_field_culled(const float* points, int64_t n_points, const fl
   const int rc = cuda_status(sf::launch_opacity_field_culled(points, n_points, means, inverse_covariances, opacities,
                                                              n_gaussians, origins, n_origins, cutoff, face_cells,
                                                              field, workspace, workspace_bytes, max_pairs, &most,
-                                                             as_stream(stream)),
+                                                             as_stream(stream),
+                                                             reinterpret_cast<unsigned long long*>(pairs_evaluated),
+                                                             query_ms),
                              "opacity_field_culled");
   if (pairs_needed) *pairs_needed = most;
   if (rc != SF_OK) return rc;
@@ -361,6 +363,28 @@ int sf_b200_opacity_field_culled(const float* points, int64_t n_points, const fl
     return fail(SF_ERR_CAPACITY, "opacity_field_culled: %lld candidate pairs in one view, max_pairs is %lld",
                 (long long)most, (long long)max_pairs);
   return SF_OK;
+}
+
+int sf_b200_opacity_field_culled(const float* points, int64_t n_points, const float* means,
+                                 const float* inverse_covariances, const float* opacities, int64_t n_gaussians,
+                                 const float* origins, int32_t n_origins, float cutoff, int32_t face_cells,
+                                 float* field, void* workspace, size_t workspace_bytes, int64_t max_pairs,
+                                 int64_t* pairs_needed, void* stream) {
+  return field_culled(points, n_points, means, inverse_covariances, opacities, n_gaussians, origins, n_origins,
+                      cutoff, face_cells, field, workspace, workspace_bytes, max_pairs, pairs_needed, stream,
+                      nullptr, nullptr);
+}
+
+int sf_b200_opacity_field_culled_stats(const float* points, int64_t n_points, const float* means,
+                                       const float* inverse_covariances, const float* opacities,
+                                       int64_t n_gaussians, const float* origins, int32_t n_origins, float cutoff,
+                                       int32_t face_cells, float* field, void* workspace, size_t workspace_bytes,
+                                       int64_t max_pairs, int64_t* pairs_needed, int64_t* pairs_evaluated,
+                                       float* query_ms, void* stream) {
+  if (!pairs_evaluated || !query_ms) return fail(SF_ERR_ARGUMENT, "opacity_field_culled_stats: NULL counter");
+  return field_culled(points, n_points, means, inverse_covariances, opacities, n_gaussians, origins, n_origins,
+                      cutoff, face_cells, field, workspace, workspace_bytes, max_pairs, pairs_needed, stream,
+                      pairs_evaluated, query_ms);
 }
 
 int sf_b200_opacity_field_plan_bytes(int64_t n_gaussians, int32_t n_origins, int32_t face_cells, int64_t total_pairs,

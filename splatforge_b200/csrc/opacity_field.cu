@@ -315,8 +315,9 @@ __device__ __forceinline__ void field_chunk(const float* pts, const int32_t* qid
                                             float oy, float oz, const float* rec, const float* near,
                                             const int32_t* cell_ids, int2 cr, const int32_t* global_ids,
                                             int64_t n_global, uint32_t* out, float4* s_g, float4* s_c,
-                                            float* s_near) {
+                                            float* s_near, unsigned long long* pair_counter) {
   const int tid = threadIdx.x;
+  unsigned evaluated = 0;  // (query, candidate) pairs taken through field_contribution
   const int qi = q0 + tid < q1 ? qidx[q0 + tid] : -1;
   const volatile uint32_t* cur = reinterpret_cast<const volatile uint32_t*>(out);
   float dx = 0.f, dy = 0.f, dz = 0.f, dist = 0.f, T = 1.f, M = 0.f;
@@ -332,6 +333,7 @@ __device__ __forceinline__ void field_chunk(const float* pts, const int32_t* qid
       const float4 a = g4[0], b = g4[1], c = g4[2];
       const float g[10] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y};
       T *= 1.f - field_contribution(g, ox, oy, oz, dx, dy, dz, dist);
+      ++evaluated;
     }
     stop = T < 1e-7f || 1.f - T >= M;
   }
@@ -366,11 +368,17 @@ __device__ __forceinline__ void field_chunk(const float* pts, const int32_t* qid
         const float R = g[10];
         if (c.w - cd * cd > R * R * 1.002f + 1e-6f * c.w) continue;
         T *= 1.f - field_contribution(g, ox, oy, oz, dx, dy, dz, dist);
+        ++evaluated;
         if (T < 1e-7f || 1.f - T >= M) { stop = true; break; }
       }
     }
   }
   if (qi >= 0) atomicMin(out + qi, __float_as_uint(fmaxf(1.f - T, 0.f)));
+  if (pair_counter) {  // uniform: one atomic per warp
+    unsigned long long v = evaluated;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((tid & 31) == 0 && v) atomicAdd(pair_counter, v);
+  }
 }
 
 // One CTA per (cell, chunk of CF_THREADS queries): work item w belongs to the cell c
@@ -379,7 +387,7 @@ __device__ __forceinline__ void field_chunk(const float* pts, const int32_t* qid
 __global__ void __launch_bounds__(CF_THREADS) cfield_cell_kernel(
     const float* pts, const int32_t* qidx, const int2* qranges, const int64_t* chunk_off, int ncells, float ox,
     float oy, float oz, const float* rec, const float* near, const int32_t* cell_ids, const int2* cell_ranges,
-    const int32_t* global_ids, int64_t n_global, uint32_t* out) {
+    const int32_t* global_ids, int64_t n_global, uint32_t* out, unsigned long long* pair_counter) {
   __shared__ float4 s_g[CF_THREADS * 3];
   __shared__ float4 s_c[CF_THREADS];  // mean - origin, |mean - origin|^2
   __shared__ float s_near[CF_THREADS];
@@ -392,7 +400,7 @@ __global__ void __launch_bounds__(CF_THREADS) cfield_cell_kernel(
   }
   const int2 qr = qranges[lo];
   field_chunk(pts, qidx, qr.x + (int)(w - chunk_off[lo]) * CF_THREADS, qr.y, ox, oy, oz, rec, near, cell_ids,
-              cell_ranges[lo], global_ids, n_global, out, s_g, s_c, s_near);
+              cell_ranges[lo], global_ids, n_global, out, s_g, s_c, s_near, pair_counter);
 }
 
 // ------------------------------------------------------------------ field plan
@@ -455,7 +463,8 @@ __global__ void __launch_bounds__(CF_THREADS) cfield_plan_kernel(
     const int64_t base = view_info[v * 2], n_global = view_info[v * 2 + 1];
     field_chunk(pts, qidx, qr.x + (int)(w - chunk_off[k]) * CF_THREADS, qr.y, origins[v * 3], origins[v * 3 + 1],
                 origins[v * 3 + 2], rec, near + (int64_t)v * ng, vals + base,
-                cell_ranges[(int64_t)v * ncells + cell], gids + (int64_t)v * ng, n_global, out, s_g, s_c, s_near);
+                cell_ranges[(int64_t)v * ncells + cell], gids + (int64_t)v * ng, n_global, out, s_g, s_c, s_near,
+                nullptr);
   }
 }
 
@@ -520,7 +529,8 @@ size_t field_culled_query_bytes(int64_t np, int F) {
 cudaError_t launch_opacity_field_culled(const float* pts, int64_t np, const float* means, const float* invcov,
                                         const float* op, int64_t ng, const float* origins, int nc, float cutoff,
                                         int F, float* out, void* ws, size_t ws_bytes, int64_t max_pairs,
-                                        int64_t* pairs_needed, cudaStream_t s) {
+                                        int64_t* pairs_needed, cudaStream_t s, unsigned long long* pair_counter,
+                                        float* query_ms) {
   if (ws_bytes < field_culled_workspace_bytes(ng, max_pairs, F) + field_culled_query_bytes(np, F))
     return cudaErrorInvalidValue;
   uint32_t* o = reinterpret_cast<uint32_t*>(out);
@@ -588,6 +598,12 @@ cudaError_t launch_opacity_field_culled(const float* pts, int64_t np, const floa
     if (pairs_needed) *pairs_needed = most;
     return e;
   }
+  // optional timing of the query kernels (CUDA events on the launching stream)
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  if (query_ms) {
+    if (e == cudaSuccess) e = cudaEventCreate(&ev[0]);
+    if (e == cudaSuccess) e = cudaEventCreate(&ev[1]);
+  }
   for (int v = 0; v < nc && e == cudaSuccess; ++v) {
     const float ox = host_origins[v * 3], oy = host_origins[v * 3 + 1], oz = host_origins[v * 3 + 2];
     count_launches(1);
@@ -623,11 +639,24 @@ cudaError_t launch_opacity_field_culled(const float* pts, int64_t np, const floa
     if (e != cudaSuccess) break;
     // at most one partial chunk per cell beyond the full ones
     const int64_t max_items = (np + CF_THREADS - 1) / CF_THREADS + ncells;
+    if (query_ms && e == cudaSuccess) e = cudaEventRecord(ev[0], s);
     count_launches(1);
     cfield_cell_kernel<<<(unsigned)max_items, CF_THREADS, 0, s>>>(
         pts, qidx, reinterpret_cast<const int2*>(qranges), chunk_off, ncells, ox, oy, oz, rec, near, vals,
-        reinterpret_cast<const int2*>(ranges), gids, n_global, o);
+        reinterpret_cast<const int2*>(ranges), gids, n_global, o, pair_counter);
     e = cudaGetLastError();
+    if (query_ms && e == cudaSuccess) {
+      // the next view's count read synchronizes the stream anyway
+      e = cudaEventRecord(ev[1], s);
+      if (e == cudaSuccess) e = cudaEventSynchronize(ev[1]);
+      float ms = 0.f;
+      if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, ev[0], ev[1]);
+      *query_ms += ms;
+    }
+  }
+  if (query_ms) {
+    cudaEventDestroy(ev[0]);
+    cudaEventDestroy(ev[1]);
   }
   delete[] host_origins;
   if (pairs_needed) *pairs_needed = most;

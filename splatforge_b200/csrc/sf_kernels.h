@@ -110,7 +110,8 @@ size_t field_culled_query_bytes(int64_t np, int F);
 cudaError_t launch_opacity_field_culled(const float* pts, int64_t np, const float* means, const float* invcov,
                                         const float* op, int64_t ng, const float* origins, int nc, float cutoff,
                                         int F, float* out, void* ws, size_t ws_bytes, int64_t max_pairs,
-                                        int64_t* pairs_needed, cudaStream_t s);
+                                        int64_t* pairs_needed, cudaStream_t s,
+                                        unsigned long long* pair_counter = nullptr, float* query_ms = nullptr);
 // gaussian.opacity_field@1
 size_t field_workspace_bytes(int64_t n);
 cudaError_t launch_opacity_field(const float* pts, int64_t np, const float* means, const float* invcov,

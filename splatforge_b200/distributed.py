@@ -60,7 +60,7 @@ class GradientAllReduce:
     The packed buffer is allocated once and reused every step.
     """
 
-    def __init__(self, params, *, group=None, average=False):
+    def __init__(self, params, *, group=None, average=False, timed=False):
         self.params = list(params)
         if len(self.params) != len(PARAM_ORDER):
             raise ValueError("expected means, log_scales, quats, opacity_logits, sh")
@@ -72,6 +72,10 @@ class GradientAllReduce:
         self.group = group
         self.average = average
         self.buffer = torch.empty((n, sum(self.widths)), device=self.params[0].device, dtype=torch.float32)
+        # with ``timed``: CUDA events (pack start, pack end, all-reduce end, unpack end)
+        # recorded on the current stream around every call
+        self.timed = timed
+        self.events = []
 
     @property
     def floats_per_gaussian(self):
@@ -101,8 +105,26 @@ class GradientAllReduce:
     def __call__(self):
         if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(self.group) == 1:
             return
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if self.timed else None
+        if ev:
+            ev[0].record()
         self.pack()
+        if ev:
+            ev[1].record()
         dist.all_reduce(self.buffer, op=dist.ReduceOp.SUM, group=self.group)
         if self.average:
             self.buffer /= dist.get_world_size(self.group)
+        if ev:
+            ev[2].record()
         self.unpack()
+        if ev:
+            ev[3].record()
+            self.events.append(ev)
+
+    def timings_ms(self):
+        """Median (pack, all-reduce, unpack) milliseconds over the timed calls (after a
+        synchronize), or None."""
+        if not self.events:
+            return None
+        cols = list(zip(*[(a.elapsed_time(b), b.elapsed_time(c), c.elapsed_time(d)) for a, b, c, d in self.events]))
+        return tuple(sorted(col)[len(col) // 2] for col in cols)

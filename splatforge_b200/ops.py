@@ -194,12 +194,14 @@ def opacity_field(points, means, inverse_covariances, opacities, origins, *, gau
 
 
 def opacity_field_culled(points, means, inverse_covariances, opacities, origins, *, gaussian_chunk=1024,
-                         cutoff=FIELD_CUTOFF, face_cells=None):
+                         cutoff=FIELD_CUTOFF, face_cells=None, stats=None):
     """The opacity field through per-view cube-map candidate lists: contributions at or
     below ``cutoff`` are dropped, everything else is evaluated as in the brute-force
     kernel.  The cube-map resolution (``face_cells``, default FIELD_FACE_CELLS, lowered
     when a view's candidate lists would exceed FIELD_PAIR_LIMIT) and the list capacity
-    are remembered per problem shape, and the workspace is kept per device."""
+    are remembered per problem shape, and the workspace is kept per device.  With a
+    ``stats`` dict, ``stats["pairs_evaluated"]`` and ``stats["query_ms"]`` accumulate the
+    evaluated (query, candidate) pairs and the query kernels' CUDA-event time."""
     dev = _require_cuda_f32("gaussian.opacity_field@1", points, means, inverse_covariances, opacities, origins)
     del gaussian_chunk
     if origins.shape[0] < 1:
@@ -219,11 +221,20 @@ def opacity_field_culled(points, means, inverse_covariances, opacities, origins,
                 _FIELD_WS.pop(dev.index, None)
                 ws = torch.empty((size.value,), device=dev, dtype=torch.uint8)
                 _FIELD_WS[dev.index] = ws
-            status = _lib.lib().sf_b200_opacity_field_culled(
-                _ptr(p), npts, _ptr(m), _ptr(q), _ptr(o), n, _ptr(org), org.shape[0], ctypes.c_float(cutoff),
-                cells, _ptr(out), _ptr(ws), ws.numel(), pairs, ctypes.byref(needed), _stream(dev))
+            args = (_ptr(p), npts, _ptr(m), _ptr(q), _ptr(o), n, _ptr(org), org.shape[0], ctypes.c_float(cutoff),
+                    cells, _ptr(out), _ptr(ws), ws.numel(), pairs, ctypes.byref(needed))
+            if stats is None:
+                status = _lib.lib().sf_b200_opacity_field_culled(*args, _stream(dev))
+            else:
+                counter = torch.zeros((1,), device=dev, dtype=torch.int64)
+                qms = ctypes.c_float(0.0)
+                status = _lib.lib().sf_b200_opacity_field_culled_stats(*args, _ptr(counter), ctypes.byref(qms),
+                                                                        _stream(dev))
             if status == _lib.SF_OK:
                 _FIELD_CFG[shape] = (cells, pairs)
+                if stats is not None:
+                    stats["pairs_evaluated"] = stats.get("pairs_evaluated", 0) + int(counter.item())
+                    stats["query_ms"] = stats.get("query_ms", 0.0) + float(qms.value)
                 return out
             if status != _lib.SF_ERR_CAPACITY or needed.value <= pairs:
                 raise _lib.NativeError(_lib.lib().sf_b200_last_error().decode())

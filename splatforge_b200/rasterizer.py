@@ -313,7 +313,9 @@ class _Raster(torch.autograd.Function):
             plan.stats["l1_max_samples"] = most
             plan.stats["l1_capacity"] = cap
             if plan.l1_capacity is None:
-                _L1_SEEN[key] = max(32, int(most * 1.2 + 31) // 32 * 32)
+                # the largest count seen for this size, with headroom (never shrinks, so
+                # a sequence of poses settles on one capacity)
+                _L1_SEEN[key] = max(_L1_SEEN.get(key, 0), int(most * 1.2 + 31) // 32 * 32)
             if most > cap:
                 # capacity exceeded somewhere: exact per-pixel (CSR) storage and a rerun
                 plan.stats["l1_rerun"] = True

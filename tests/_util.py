@@ -47,3 +47,19 @@ def median_mismatch_ok(got, want, tol, frac=0.002):
 
 def numpy(t):
     return t.detach().cpu().numpy() if isinstance(t, torch.Tensor) else np.asarray(t)
+
+
+def reference_source():
+    """A directory from which the reference package ``splatforge`` imports, or None:
+    the ``SPLATFORGE_SRC`` environment variable (the reference's ``src`` directory), else
+    the copy ``pip install --target baseline/_ref`` puts beside this repository."""
+    import os
+    from pathlib import Path
+
+    env = os.environ.get("SPLATFORGE_SRC")
+    candidates = [Path(env)] if env else []
+    candidates.append(Path(__file__).resolve().parent.parent / "baseline" / "_ref")
+    for c in candidates:
+        if (c / "splatforge").is_dir():
+            return c
+    return None

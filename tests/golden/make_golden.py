@@ -1,8 +1,9 @@
 """Generate golden fixtures by running SplatForge's own Torch provider.
 
-Run in a container where the reference source tree is present:
+Run where the reference source tree is present, giving its ``src`` directory as the
+first argument or in ``SPLATFORGE_SRC``:
 
-    python tests/golden/make_golden.py /root/reference/src
+    python tests/golden/make_golden.py <reference>/src [fixture ...]
 
 It imports the reference read-only (no files are written into it), evaluates
 its renderers, operators and tile binning on seeded synthetic inputs, and
@@ -40,6 +41,7 @@ Fixtures (all float32 unless noted):
 
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
@@ -485,7 +487,10 @@ def render_cases():
 
 
 if __name__ == "__main__":
-    _setup(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SPLATFORGE_SRC")
+    if not src:
+        raise SystemExit("usage: make_golden.py <reference src directory> [fixture ...] (or set SPLATFORGE_SRC)")
+    _setup(src)
     which = sys.argv[2:] or ["binning", "ops", "extra", "geometry", "mesh", "training", "render"]
     if "binning" in which:
         binning_cases()

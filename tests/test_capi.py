@@ -70,3 +70,15 @@ def test_rasterize_rejects_cpu_tensors_without_fallback():
     with pytest.raises(ValueError):
         RasterSettings(distortions="l3").struct(3, 16)
     del torch
+
+
+def test_static_scratch_covers_the_ordering_workspace_at_its_limit():
+    """The static array behind sf_b200_bin_order_static holds the ordering workspace of
+    the largest call it accepts (host arithmetic only, no device)."""
+    text = HEADER.read_text()
+    limit = int(re.search(r"#define SF_B200_STATIC_MAX_GAUSSIANS (\d+)", text).group(1))
+    m = re.search(r"#define SF_B200_STATIC_SCRATCH_BYTES \((\d+)u << (\d+)\)", text)
+    scratch = int(m.group(1)) << int(m.group(2))
+    size = ctypes.c_size_t()
+    assert _lib.lib().sf_b200_bin_workspace_bytes(limit, 0, 1, ctypes.byref(size)) == 0
+    assert size.value <= scratch, (size.value, scratch)

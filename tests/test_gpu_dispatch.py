@@ -1,0 +1,152 @@
+"""Dispatch through SplatForge's own operator runtime on CUDA tensors.
+
+``SurfaceOperators(runtime, implementations=provider.selection())`` is the call the
+reference's compositions make (src/splatforge/gaussian/ops.py:234-254); here it runs the
+B200 runners on device tensors and is compared, outputs and gradients, with the
+reference's own Torch provider (the default ``SurfaceOperators()``) on the same values
+on the CPU.  Skipped where the reference package is not importable (``SPLATFORGE_SRC``
+or the baseline/_ref install).
+"""
+
+from __future__ import annotations
+
+import sys
+
+import pytest
+import torch
+
+from tests._util import reference_source
+
+pytestmark = pytest.mark.gpu
+
+REF = reference_source()
+if REF is None:
+    pytest.skip("the SplatForge reference package is not importable", allow_module_level=True)
+if str(REF) not in sys.path:
+    sys.path.insert(0, str(REF))
+sys.dont_write_bytecode = True
+
+from splatforge.gaussian import SurfaceOperators  # noqa: E402
+
+from splatforge_b200 import provider  # noqa: E402
+from tests._util import rel_err  # noqa: E402
+
+DEV = "cuda"
+
+
+def _pair(*shapes, seed, positive=()):
+    """The same random leaves on the device and on the CPU."""
+    g = torch.Generator().manual_seed(seed)
+    cpu = []
+    for k, s in enumerate(shapes):
+        t = torch.randn(*s, generator=g)
+        if k in positive:
+            t = t.abs() + 0.1
+        cpu.append(t)
+    dev = [t.to(DEV).requires_grad_() for t in cpu]
+    cpu = [t.clone().requires_grad_() for t in cpu]
+    return dev, cpu
+
+
+def _compare(op, b200, ref, dev_in, cpu_in, *, atol, grad_rtol, diff=True, **attrs):
+    got = b200(op, *dev_in, **attrs)
+    want = ref(op, *cpu_in, **attrs)
+    got = got if isinstance(got, tuple) else (got,)
+    want = want if isinstance(want, tuple) else (want,)
+    assert len(got) == len(want)
+    for a, b in zip(got, want):
+        assert a.device.type == "cuda"
+        torch.testing.assert_close(a.detach().cpu(), b.detach(), atol=atol, rtol=1e-4, check_dtype=False)
+    if not diff:
+        return
+    g = torch.Generator().manual_seed(99)
+    ups = [torch.randn(b.shape, generator=g) if b.is_floating_point() else None for b in want]
+    pairs = [(a, b, u) for a, b, u in zip(got, want, ups) if u is not None and b.requires_grad]
+    gd = torch.autograd.grad(sum((a * u.to(DEV)).sum() for a, _, u in pairs), dev_in, allow_unused=True)
+    gc = torch.autograd.grad(sum((b * u).sum() for _, b, u in pairs), cpu_in, allow_unused=True)
+    for x, y in zip(gd, gc):
+        if y is None:
+            continue
+        assert x is not None
+        assert rel_err(x.cpu(), y) < grad_rtol
+
+
+@pytest.fixture(scope="module")
+def operators():
+    return provider.surface_operators(), SurfaceOperators()
+
+
+def test_covariance_and_sh_color_through_the_runtime(operators):
+    b200, ref = operators
+    dev, cpu = _pair((256, 4), (256, 3), seed=1, positive=(1,))
+    _compare("gaussian.covariance@1", b200, ref, dev, cpu, atol=1e-5, grad_rtol=1e-4)
+    dev, cpu = _pair((256, 16, 3), (256, 3), seed=2)
+    with torch.no_grad():
+        for d in (dev[1], cpu[1]):
+            d /= d.norm(dim=-1, keepdim=True)
+    _compare("gaussian.sh_color@1", b200, ref, dev, cpu, atol=1e-5, grad_rtol=1e-4, degree=3)
+
+
+@pytest.mark.parametrize("distortions", ["none", "l1", "l2", "both"])
+def test_alpha_composite_through_the_runtime(operators, distortions):
+    b200, ref = operators
+    g = torch.Generator().manual_seed(3)
+    a = torch.rand(3, 24, 40, generator=g) * 0.6
+    c = torch.rand(3, 24, 3, generator=g)
+    d = torch.rand(3, 24, 40, generator=g) * 3 + 1
+    n = torch.randn(3, 24, 40, 3, generator=g)
+    cpu = [t.clone().requires_grad_() for t in (a, c, d, n)]
+    dev = [t.to(DEV).requires_grad_() for t in (a, c, d, n)]
+    _compare("splat.alpha_composite@3", b200, ref, dev, cpu, atol=2e-5, grad_rtol=1e-3, distortions=distortions)
+
+
+def test_geometry_operators_through_the_runtime(operators):
+    b200, ref = operators
+    K = torch.tensor([[40.0, 0.0, 16.0], [0.0, 42.0, 12.0], [0.0, 0.0, 1.0]])
+    got = b200("camera.pixel_rays@1", K.to(DEV), width=32, height=24)
+    want = ref("camera.pixel_rays@1", K, width=32, height=24)
+    torch.testing.assert_close(got.cpu(), want, atol=1e-6, rtol=1e-6)
+
+    g = torch.Generator().manual_seed(4)
+    m = torch.randn(48, 3, generator=g)
+    A = torch.randn(48, 3, 3, generator=g)
+    Q = A @ A.transpose(-1, -2) + 0.5 * torch.eye(3)
+    o = torch.randn(20, 3, generator=g) * 3
+    dirs = torch.randn(20, 3, generator=g)
+    cpu = [t.clone().requires_grad_() for t in (m, Q, o, dirs)]
+    dev = [t.to(DEV).requires_grad_() for t in (m, Q, o, dirs)]
+    _compare("gaussian.ray_peak@1", b200, ref, dev, cpu, atol=2e-4, grad_rtol=1e-3)
+
+    depth = 2.0 + torch.rand(24, 32, generator=g)
+    cpu = [depth.clone().requires_grad_(), K.clone()]
+    dev = [depth.to(DEV).requires_grad_(), K.to(DEV)]
+    got = b200("geometry.depth_normals@1", *dev)
+    want = ref("geometry.depth_normals@1", *cpu)
+    torch.testing.assert_close(got[0].detach().cpu(), want[0].detach(), atol=1e-5, rtol=1e-4)
+    assert torch.equal(got[1].cpu(), want[1])
+    up = torch.randn(want[0].shape, generator=g)
+    (gd,) = torch.autograd.grad((got[0] * up.to(DEV)).sum(), dev[0])
+    (gc,) = torch.autograd.grad((want[0] * up).sum(), cpu[0])
+    assert rel_err(gd.cpu(), gc) < 1e-3
+
+
+def test_opacity_field_through_the_runtime(operators):
+    b200, ref = operators
+    g = torch.Generator().manual_seed(5)
+    n = 200
+    means = torch.rand(n, 3, generator=g) * 2 - 1
+    A = torch.randn(n, 3, 3, generator=g) * 0.1
+    Q = torch.linalg.inv(A @ A.transpose(-1, -2) + 0.01 * torch.eye(3))
+    op = torch.rand(n, generator=g) * 0.9
+    pts = torch.rand(500, 3, generator=g) * 2 - 1
+    org = torch.randn(6, 3, generator=g)
+    org = 3 * org / org.norm(dim=-1, keepdim=True)
+    got = b200("gaussian.opacity_field@1", *(t.to(DEV) for t in (pts, means, Q, op, org)))
+    want = ref("gaussian.opacity_field@1", pts, means, Q, op, org)
+    torch.testing.assert_close(got.cpu(), want, atol=2e-5, rtol=1e-4)
+
+
+def test_cpu_tensors_do_not_fall_back(operators):
+    b200, _ = operators
+    with pytest.raises(Exception):
+        b200("gaussian.covariance@1", torch.randn(4, 4), torch.rand(4, 3))

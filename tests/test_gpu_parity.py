@@ -108,7 +108,7 @@ CROPS = {
 
 
 @pytest.mark.parametrize("workload", list(CROPS))
-@pytest.mark.parametrize("mode", ["radegs", "gof"])
+@pytest.mark.parametrize("mode", ["radegs", "gof", "ambisur"])
 def test_surface_scene_crops(workload, mode):
     """Tile-aligned crops (principal point shifted by multiples of 16): same rays as
     the full frame for the covered pixels."""

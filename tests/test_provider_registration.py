@@ -1,21 +1,23 @@
 """Registration behind SplatForge's own core runtime and renderer registry (CPU).
 
-Uses the reference package from its source tree when it is present in this
-container (it is not shipped with this repository); skipped otherwise.  No device
-is needed: dispatch is metadata-only (src/splatforge/core/runtime.py:256-326).
+Uses the reference package where it is importable (``SPLATFORGE_SRC`` pointing at its
+``src`` directory, or the baseline/_ref install; it is not shipped with this
+repository); skipped otherwise.  No device is needed: dispatch is metadata-only
+(src/splatforge/core/runtime.py:256-326).
 """
 
 from __future__ import annotations
 
 import sys
-from pathlib import Path
 
 import pytest
 import torch
 
-REF = Path("/root/reference/src")
-if not (REF / "splatforge").is_dir():
-    pytest.skip("SplatForge source tree not present", allow_module_level=True)
+from tests._util import reference_source
+
+REF = reference_source()
+if REF is None:
+    pytest.skip("the SplatForge reference package is not importable", allow_module_level=True)
 sys.path.insert(0, str(REF))
 sys.dont_write_bytecode = True
 

@@ -68,6 +68,29 @@ def test_static_scratch_matches_allocating_entry_point_twice():
         torch.cuda.synchronize()
 
 
+def test_static_scratch_call_allocates_no_device_memory():
+    """After a first call (which resolves the array's address), a call changes neither
+    the device's free memory nor torch's allocated bytes."""
+    n = 1 << 20
+    count, key = _inputs(n, 3)
+    order = torch.empty((n,), device=DEV, dtype=torch.int32)
+    offsets = torch.empty((n + 1,), device=DEV, dtype=torch.int64)
+    stream = _stream(torch.device(DEV))
+
+    def call():
+        _lib.call("sf_b200_bin_order_static", _ptr(count), _ptr(key), n, _ptr(order), _ptr(offsets), stream)
+
+    call()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    alloc0 = torch.cuda.memory_allocated()
+    call()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert torch.cuda.memory_allocated() == alloc0
+
+
 def test_static_scratch_rejects_oversized_input():
     n = (1 << 20) + 1
     count = torch.zeros((n,), device=DEV, dtype=torch.int32)
