@@ -104,18 +104,48 @@ def _sqrt_rn(x):
     return x.double().sqrt().to(x.dtype) if x.dtype == torch.float32 else x.sqrt()
 
 
-def covariance_explicit(quats, scales):
-    """``gaussian.covariance@1`` (reference.py:15-35) as explicit float32 sums:
-    ``n = sqrt(((w^2 + x^2) + y^2) + z^2)``, the reference's rotation formula,
-    ``M = R diag(s*s)``, ``C_ij = (M_i0 R_j0 + M_i1 R_j1) + M_i2 R_j2``."""
+def rotation_explicit(quats):
+    """The rotation of ``rotation_matrix`` (reference.py:15-31) as explicit float32
+    operations: ``n = sqrt(((w^2 + x^2) + y^2) + z^2)`` and the reference's formula on
+    the normalised quaternion.  Returns nested lists R[i][j] of [N] tensors."""
     w, x, y, z = quats.unbind(-1)
     n = _sqrt_rn(((w * w + x * x) + y * y) + z * z).clamp_min(1e-12)
     w, x, y, z = w / n, x / n, y / n, z / n
-    R = [
+    return [
         [1 - 2 * (y * y + z * z), 2 * (x * y - w * z), 2 * (x * z + w * y)],
         [2 * (x * y + w * z), 1 - 2 * (x * x + z * z), 2 * (y * z - w * x)],
         [2 * (x * z - w * y), 2 * (y * z + w * x), 1 - 2 * (x * x + y * y)],
     ]
+
+
+def dot3_rn(a, b):
+    """``(a0 b0 + a1 b1) + a2 b2`` over the last dimension, each product and sum rounded
+    on its own."""
+    return (a[..., 0] * b[..., 0] + a[..., 1] * b[..., 1]) + a[..., 2] * b[..., 2]
+
+
+def ambisur_plane(view, camera, m):
+    """AmbiSuR camera-facing normal and plane distance (batched_renderer.py:96-108): the
+    rotation column of the smallest scale, turned into the camera frame, flipped to face
+    the camera, and its dot product with the camera-space mean, as explicit float32
+    sums (the per-pixel plane depth plane / (n . ray) is ill-conditioned at grazing
+    angles, so the kernels evaluate the same sequence)."""
+    axis = view.scales.detach().argmin(-1)
+    R = rotation_explicit(view.quats)
+    cols = torch.stack([torch.stack(row, -1) for row in R], -2)  # [N, 3, 3]
+    world = cols.gather(2, axis[:, None, None].expand(-1, 3, 1)).squeeze(-1)
+    Wc = camera.world_to_camera[:3, :3]
+    nc = torch.stack([dot3_rn(world, Wc[i].expand_as(world)) for i in range(3)], -1)
+    facing = dot3_rn(nc, m)
+    normals = torch.where(facing[:, None] > 0, -nc, nc)
+    return normals, dot3_rn(normals, m)
+
+
+def covariance_explicit(quats, scales):
+    """``gaussian.covariance@1`` (reference.py:15-35) as explicit float32 sums: the
+    rotation of ``rotation_explicit``, ``M = R diag(s*s)``,
+    ``C_ij = (M_i0 R_j0 + M_i1 R_j1) + M_i2 R_j2``."""
+    R = rotation_explicit(quats)
     s2 = [scales[:, k] * scales[:, k] for k in range(3)]
     M = [[R[i][k] * s2[k] for k in range(3)] for i in range(3)]
     C = [[(M[i][0] * R[j][0] + M[i][1] * R[j][1]) + M[i][2] * R[j][2] for j in range(3)] for i in range(3)]
@@ -201,11 +231,7 @@ def prepare(
         rn = torch.cat((gain, -torch.ones_like(gain[:, :1])), 1)
         normals = ops._unit((full.transpose(-1, -2) @ rn.unsqueeze(-1)).squeeze(-1))
     elif mode == "ambisur":
-        axis = view.scales.detach().argmin(-1)
-        world = ops.rotation_matrix(view.quats).gather(2, axis[:, None, None].expand(-1, 3, 1)).squeeze(-1)
-        normals = world @ camera.world_to_camera[:3, :3].T
-        normals = torch.where((normals * m).sum(-1, keepdim=True) > 0, -normals, normals)
-        plane = (normals * m).sum(-1)
+        normals, plane = ambisur_plane(view, camera, m)
     else:
         qinv = torch.linalg.inv(cov_cam)
     sel = (
@@ -352,7 +378,7 @@ def _tile_batch(ids, valid, trays, pix, camera, xy, conic, colors, ray_colors, o
                 + (gain[ids][:, :, None, :] * delta).sum(-1)
             ) / torch.linalg.vector_norm(trays, dim=-1)[:, None]
         else:
-            den = (pn * trays[:, None]).sum(-1)
+            den = dot3_rn(pn, trays[:, None].expand_as(pn))
             ok = den.abs() > 1e-8
             depth = plane[ids][:, :, None] / torch.where(ok, den, torch.ones_like(den))
             resp = torch.where(ok, resp, 0)

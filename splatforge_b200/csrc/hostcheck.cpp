@@ -76,7 +76,7 @@ int hc_project_forward(const float* means, const float* quats, const float* scal
       inv3_sym(p.Cc, rec + R_Q3);
     } else {
       AmbiExtras e;
-      ambi_extras(q, sc, p, *cam, e);
+      ambi_extras(sc, p, *cam, e);
       for (int k = 0; k < 3; ++k) rec[R_ANRM + k] = e.normal[k];
       rec[R_PLANE] = e.plane;
     }

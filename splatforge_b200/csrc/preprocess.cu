@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(PB) project_forward_kernel(
     inv3_sym(p.Cc, rec + R_Q3);
   } else {
     AmbiExtras e;
-    ambi_extras(q, sc, p, cam, e);
+    ambi_extras(sc, p, cam, e);
     rec[R_ANRM] = e.normal[0]; rec[R_ANRM + 1] = e.normal[1]; rec[R_ANRM + 2] = e.normal[2];
     rec[R_PLANE] = e.plane;
   }

@@ -306,7 +306,7 @@ SF_HD void project_backward(const float* mean, const float* quat, const float* s
     g_mc[2] += grec[R_Z];
   } else {
     AmbiExtras e;
-    ambi_extras(quat, scale, p, cam, e);
+    ambi_extras(scale, p, cam, e);
     float gpl = grec[R_PLANE];
     float gn[3];
     for (int k = 0; k < 3; ++k) {

@@ -475,29 +475,32 @@ SF_HD void rade_extras(const Projection& p, RadeExtras& e) {
 struct AmbiExtras {
   int axis;
   float sign;
-  float Rr[9];      // rotation from the F.normalize'd quaternion
   float normal[3];
   float plane;
 };
 
-SF_HD void ambi_extras(const float* quat, const float* scale, const Projection& p,
-                       const sf_camera& cam, AmbiExtras& e) {
+// (a0 b0 + a1 b1) + a2 b2 with every product and sum rounded on its own (no FMA)
+SF_HD float dot3_rn(float a0, float a1, float a2, float b0, float b1, float b2) {
+  return radd(radd(rmul(a0, b0), rmul(a1, b1)), rmul(a2, b2));
+}
+
+// The AmbiSuR plane (batched_renderer.py:96-108): the rotation's column of the smallest
+// scale, turned into the camera frame and flipped to face the camera, and its plane
+// distance.  The per-pixel plane depth plane / (n . ray) is ill-conditioned at grazing
+// angles, so every step here is an exact-rounding sequence on the projection's exact
+// rotation (the oracle performs the same sequence).
+SF_HD void ambi_extras(const float* scale, const Projection& p, const sf_camera& cam, AmbiExtras& e) {
   int a = 0;
   if (scale[1] < scale[a]) a = 1;
   if (scale[2] < scale[a]) a = 2;
   e.axis = a;
-  float qn[4];
-  float n = sqrtf(quat[0] * quat[0] + quat[1] * quat[1] + quat[2] * quat[2] + quat[3] * quat[3]);
-  n = fmaxr(n, 1e-12f);
-  for (int k = 0; k < 4; ++k) qn[k] = quat[k] / n;
-  quat_rotation(qn, e.Rr);
-  float w[3] = {e.Rr[0 * 3 + a], e.Rr[1 * 3 + a], e.Rr[2 * 3 + a]};
+  const float w0 = p.R[0 * 3 + a], w1 = p.R[1 * 3 + a], w2 = p.R[2 * 3 + a];
   float nc[3];
-  for (int i = 0; i < 3; ++i) nc[i] = w[0] * cam.R[i * 3 + 0] + w[1] * cam.R[i * 3 + 1] + w[2] * cam.R[i * 3 + 2];
-  float facing = nc[0] * p.mc[0] + nc[1] * p.mc[1] + nc[2] * p.mc[2];
+  for (int i = 0; i < 3; ++i) nc[i] = dot3_rn(w0, w1, w2, cam.R[i * 3 + 0], cam.R[i * 3 + 1], cam.R[i * 3 + 2]);
+  const float facing = dot3_rn(nc[0], nc[1], nc[2], p.mc[0], p.mc[1], p.mc[2]);
   e.sign = facing > 0.f ? -1.f : 1.f;
   for (int i = 0; i < 3; ++i) e.normal[i] = e.sign * nc[i];
-  e.plane = e.normal[0] * p.mc[0] + e.normal[1] * p.mc[1] + e.normal[2] * p.mc[2];
+  e.plane = dot3_rn(e.normal[0], e.normal[1], e.normal[2], p.mc[0], p.mc[1], p.mc[2]);
 }
 
 // ---------------------------------------------------------------- per-pixel geometry
@@ -628,9 +631,11 @@ SF_HD bool eval_sample(const float* rec, const PixelRay& pr, float ext2, float n
       s.n[0] = rec[R_NRM]; s.n[1] = rec[R_NRM + 1]; s.n[2] = rec[R_NRM + 2];
     } else {
       s.n[0] = rec[R_ANRM]; s.n[1] = rec[R_ANRM + 1]; s.n[2] = rec[R_ANRM + 2];
-      s.aden = dot3(s.n[0], s.n[1], s.n[2], pr.r[0], pr.r[1], pr.r[2]);
+      // exact rounding: n . ray is ill-conditioned at grazing angles, and the depth
+      // decides near/far membership
+      s.aden = dot3_rn(s.n[0], s.n[1], s.n[2], pr.r[0], pr.r[1], pr.r[2]);
       s.aok = fabsf(s.aden) > 1e-8f;
-      s.depth = rec[R_PLANE] * fast_rcp(s.aok ? s.aden : 1.f);
+      s.depth = rdiv(rec[R_PLANE], s.aok ? s.aden : 1.f);
       if (!s.aok) resp = 0.f;
     }
   }

@@ -113,9 +113,9 @@ def test_geometry_operators_through_the_runtime(operators):
     Q = A @ A.transpose(-1, -2) + 0.5 * torch.eye(3)
     o = torch.randn(20, 3, generator=g) * 3
     dirs = torch.randn(20, 3, generator=g)
-    cpu = [t.clone().requires_grad_() for t in (m, Q, o, dirs)]
-    dev = [t.to(DEV).requires_grad_() for t in (m, Q, o, dirs)]
-    _compare("gaussian.ray_peak@1", b200, ref, dev, cpu, atol=2e-4, grad_rtol=1e-3)
+    # forward-only implementation: the runtime refuses it for inputs that require grad
+    _compare("gaussian.ray_peak@1", b200, ref, [t.to(DEV) for t in (m, Q, o, dirs)], [m, Q, o, dirs], atol=2e-4,
+             grad_rtol=None, diff=False)
 
     depth = 2.0 + torch.rand(24, 32, generator=g)
     cpu = [depth.clone().requires_grad_(), K.clone()]

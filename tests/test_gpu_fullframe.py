@@ -6,7 +6,7 @@ batch at a time).
   all three modes with every output channel and every gradient.
 * The view-batched training step's shape: the 3M-Gaussian scene, 8 poses of 1600x1064
   rendered one after another into one accumulated gradient, against the sum of the
-  oracle's single-view gradients.  Tile-aligned 256x256 windows of the 8 poses keep
+  oracle's single-view gradients.  Tile-aligned 128x128 windows of the 8 poses keep
   the oracle's share of the run short; the kernels see the same rays as in the full
   frame.
 
@@ -53,7 +53,7 @@ def test_full_frame_million_gaussians_1080p(million_1080p, mode):
     t2 = time.perf_counter()
     want = {k: v.cpu() for k, v in want.items()}
     print(f"\n{mode}: {out['n_isect']} intersections; kernels {t1 - t0:.1f} s, device oracle {t2 - t1:.1f} s")
-    assert out["n_isect"] > 30_000_000
+    assert out["n_isect"] > (15_000_000 if mode == "ambisur" else 30_000_000)
     assert_images(got, want, mode, f"1080p/{mode}")
     assert_grads(ggrads, wgrads, f"1080p/{mode}")
 
@@ -61,7 +61,7 @@ def test_full_frame_million_gaussians_1080p(million_1080p, mode):
 def test_view_batched_step_accumulates_eight_views():
     params, cams = scenes.workload("surfaces3m_views64", seed=0)
     poses = cams[:8]
-    windows = [c.crop(672, 400, 256, 256) for c in poses]
+    windows = [c.crop(736, 464, 128, 128) for c in poses]
     settings = RasterSettings(mode="gof", distortions="l1")
     ups = [_ups(c, 900 + k) for k, c in enumerate(windows)]
 

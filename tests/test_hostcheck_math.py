@@ -101,6 +101,20 @@ def test_hostcheck_projection_bits_match_oracle():
     assert torch.equal(ex["records"][:, 4], conic[:, 1, 1])
 
 
+def test_hostcheck_ambisur_plane_bits_match_oracle():
+    """The AmbiSuR camera-facing normal and plane distance (records 11..14) are
+    bit-identical to the oracle's: the plane depth plane / (n . ray) amplifies any
+    rounding difference at grazing angles, so both evaluate the same exact sequence."""
+    params = scenes.surfaces(20_000, seed=5)
+    cam = scenes.orbit_cameras(1, 800, 800, 50.0, radius=3.0, seed=5)[0]
+    _, _, ex = hostcheck.render(params, cam, RasterSettings(mode="ambisur", distortions="none"))
+    view = scenes.activated(params)
+    m, _, _, _, _, _ = oracle_render.project(view, cam, 0.3, 0.01)
+    normals, plane = oracle_render.ambisur_plane(view, cam, m)
+    assert torch.equal(ex["records"][:, 11:14], normals)
+    assert torch.equal(ex["records"][:, 14], plane)
+
+
 def test_warp_cull_never_drops_a_passing_sample():
     """The culling predicate over an 8x4 block of pixel centres is conservative: every
     Gaussian that passes squared <= extent^2 (float32, the kernels' operation order) at
