@@ -122,7 +122,8 @@ int hc_raster_forward(const float* records, const int32_t* ids, const int32_t* r
       PixelRay pr;
       pixel_ray(*cam, u, v, pr);
       double Td = 1.0, Wd = 0.0;
-      float C[3] = {0, 0, 0}, D = 0, D2 = 0, N[3] = {0, 0, 0}, Dn = 0, A = 0, Scc = 0, med_depth = 0;
+      float C[3] = {0, 0, 0}, D = 0, N[3] = {0, 0, 0}, Dn = 0, A = 0, Scc = 0, med_depth = 0;
+      double L2d1 = 0.0, L2d2 = 0.0;
       int last = r0, med = -1, cnt = 0;
       for (int pos = r0; pos < r1; ++pos) {
         const float* rec = records + (int64_t)ids[pos] * SF_RECORD_FLOATS;
@@ -136,7 +137,11 @@ int hc_raster_forward(const float* records, const int32_t* ids, const int32_t* r
         const float* c = rec + R_RGB;
         for (int k = 0; k < 3; ++k) { C[k] += w * c[k]; N[k] += w * s.n[k]; }
         D += w * s.depth;
-        if (dist & SF_DIST_L2) D2 += w * s.depth * s.depth;
+        if (dist & SF_DIST_L2) {
+          const double wd = (double)w * (double)s.depth;
+          L2d1 += wd;
+          L2d2 += wd * (double)s.depth;
+        }
         A += w * rec[R_SEL];
         if (mode == SF_MODE_AMBISUR) { Dn += w * rec[R_PLANE]; Scc += w * (c[0] * c[0] + c[1] * c[1] + c[2] * c[2]); }
         Wd += (double)w;
@@ -162,14 +167,14 @@ int hc_raster_forward(const float* records, const int32_t* ids, const int32_t* r
       depth[pix] = Wf > 1e-8f ? expected : 0.f;
       const float nn = fmaxr(std::sqrt(N[0] * N[0] + N[1] * N[1] + N[2] * N[2]), 1e-12f);
       for (int k = 0; k < 3; ++k) normals[pix * 3 + k] = N[k] / nn;
-      const float raw_l2 = (dist & SF_DIST_L2) ? 2.f * (Wf * D2 - D * D) : 0.f;
+      const float raw_l2 = (dist & SF_DIST_L2) ? (float)(2.0 * (Wd * L2d2 - L2d1 * L2d1)) : 0.f;
       l2[pix] = fmaxr(raw_l2, 0.f);
       median[pix] = med >= 0 ? med_depth : 0.f;
       const float CC = C[0] * C[0] + C[1] * C[1] + C[2] * C[2];
       ray_color[pix] = mode == SF_MODE_AMBISUR ? Scc - 2.f * CC + CC * Wf : 0.f;
       amb[pix] = A;
       float* stt = state + pix * SF_PIXEL_STATE_FLOATS;
-      stt[PS_T] = (float)Td; stt[PS_W] = Wf; stt[PS_D] = D; stt[PS_D2] = D2;
+      stt[PS_T] = (float)Td; stt[PS_W] = Wf; stt[PS_D] = D; stt[PS_D2] = (float)L2d2;
       for (int k = 0; k < 3; ++k) { stt[PS_C + k] = C[k]; stt[PS_N + k] = N[k]; }
       stt[PS_DNUM] = Dn; stt[PS_L2] = raw_l2; stt[PS_LAST] = i2f(last); stt[PS_MEDIAN] = i2f(med);
       stt[PS_COUNT] = i2f(cnt);

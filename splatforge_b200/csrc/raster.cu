@@ -120,7 +120,10 @@ __global__ void __launch_bounds__(TILE_PIXELS, 4) raster_forward_kernel(const Ra
   const float ext2 = a.st.extent_sq, nearp = a.st.near_plane, farp = a.st.far_plane;
   const double t_stop = (double)a.st.t_stop;
   double Td = 1.0, Wd = 0.0;
-  float C0 = 0.f, C1 = 0.f, C2 = 0.f, D = 0.f, D2 = 0.f, N0 = 0.f, N1 = 0.f, N2 = 0.f;
+  float C0 = 0.f, C1 = 0.f, C2 = 0.f, D = 0.f, N0 = 0.f, N1 = 0.f, N2 = 0.f;
+  // L2 = 2 (W sum w d^2 - (sum w d)^2) cancels when the depths are large and close
+  // (AmbiSuR plane depths at grazing angles): its moments accumulate in double
+  double L2d1 = 0.0, L2d2 = 0.0;
   float Dn = 0.f, A = 0.f, Scc = 0.f, med_depth = 0.f;
   int last = rg.x, med = -1, cnt = 0, evaluated = 0;
   bool done = !inside;
@@ -162,7 +165,11 @@ __global__ void __launch_bounds__(TILE_PIXELS, 4) raster_forward_kernel(const Ra
         const float c0 = rec[R_RGB], c1 = rec[R_RGB + 1], c2 = rec[R_RGB + 2];
         C0 += w * c0; C1 += w * c1; C2 += w * c2;
         D += w * s.depth;
-        if (DIST & SF_DIST_L2) D2 += w * s.depth * s.depth;
+        if (DIST & SF_DIST_L2) {
+          const double wd = (double)w * (double)s.depth;
+          L2d1 += wd;
+          L2d2 += wd * (double)s.depth;
+        }
         N0 += w * s.n[0]; N1 += w * s.n[1]; N2 += w * s.n[2];
         A += w * rec[R_SEL];
         if (MODE == SF_MODE_AMBISUR) {
@@ -206,7 +213,7 @@ __global__ void __launch_bounds__(TILE_PIXELS, 4) raster_forward_kernel(const Ra
     a.normals[p3 + 0] = N0 / nn;
     a.normals[p3 + 1] = N1 / nn;
     a.normals[p3 + 2] = N2 / nn;
-    const float raw_l2 = (DIST & SF_DIST_L2) ? 2.f * (Wf * D2 - D * D) : 0.f;
+    const float raw_l2 = (DIST & SF_DIST_L2) ? (float)(2.0 * (Wd * L2d2 - L2d1 * L2d1)) : 0.f;
     a.l2[pix] = fmaxr(raw_l2, 0.f);
     if (!(DIST & SF_DIST_L1)) a.l1[pix] = 0.f;
     a.median[pix] = med >= 0 ? med_depth : 0.f;
@@ -217,7 +224,7 @@ __global__ void __launch_bounds__(TILE_PIXELS, 4) raster_forward_kernel(const Ra
     st[PS_T] = (float)Td;
     st[PS_W] = Wf;
     st[PS_D] = D;
-    st[PS_D2] = D2;
+    st[PS_D2] = (float)L2d2;
     st[PS_C] = C0; st[PS_C + 1] = C1; st[PS_C + 2] = C2;
     st[PS_N] = N0; st[PS_N + 1] = N1; st[PS_N + 2] = N2;
     st[PS_DNUM] = Dn;
@@ -364,19 +371,74 @@ __device__ __noinline__ float l1_sort_pixel(float* col_d, float* col_w, int64_t 
 // below about 4), the packed keys are exact, unique and order like (depth, index),
 // and the network needs no payload: unsigned min/max only.  Returns false (nothing
 // written) when the span does not fit; the caller then runs the 64-bit path.
+//
+// The pixel's depths and weights arrive in one round of 16-byte loads in blocked layout
+// (lane l holds samples l*I .. l*I+I-1); the weights are parked in the warp's slice of
+// shared memory (s_w) by compositing index, so that after the sort each lane reads the
+// weights of its sorted samples there instead of from global memory; the two factors
+// are assembled in s_w / s_o by compositing index and leave in blocked layout.  A float4
+// is loaded or stored only when it starts below n: runs start on 8-sample boundaries and
+// their room is a multiple of 8, so it never leaves the pixel's run.
+template <int I>
+__device__ __forceinline__ void l1_load_run(const float* col, int64_t base, int n, int lane, bool vec, float (&v)[I]) {
+#pragma unroll
+  for (int q = 0; q < I / 4; ++q) {
+    const int e0 = lane * I + 4 * q;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (e0 < n) {
+      if (vec) {
+        x = *reinterpret_cast<const float4*>(col + base + e0);
+      } else {
+        x.x = col[base + e0];
+        x.y = e0 + 1 < n ? col[base + e0 + 1] : 0.f;
+        x.z = e0 + 2 < n ? col[base + e0 + 2] : 0.f;
+        x.w = e0 + 3 < n ? col[base + e0 + 3] : 0.f;
+      }
+    }
+    v[4 * q] = x.x; v[4 * q + 1] = x.y; v[4 * q + 2] = x.z; v[4 * q + 3] = x.w;
+  }
+}
+
+template <int I>
+__device__ __forceinline__ void l1_store_run(float* col, int64_t base, int n, int lane, bool vec, const float* s) {
+#pragma unroll
+  for (int q = 0; q < I / 4; ++q) {
+    const int e0 = lane * I + 4 * q;
+    if (e0 >= n) continue;
+    const float4 x = *reinterpret_cast<const float4*>(s + e0);
+    if (vec && e0 + 4 <= n) {
+      *reinterpret_cast<float4*>(col + base + e0) = x;
+    } else {
+      col[base + e0] = x.x;
+      if (e0 + 1 < n) col[base + e0 + 1] = x.y;
+      if (e0 + 2 < n) col[base + e0 + 2] = x.z;
+      if (e0 + 3 < n) col[base + e0 + 3] = x.w;
+    }
+  }
+}
+
 template <int I>
 __device__ __forceinline__ bool l1_sort_pixel_packed(float* col_d, float* col_w, int64_t base, int n, int lane,
-                                                     float& raw_out) {
+                                                     bool vec, float* s_w, float* s_o, float& raw_out) {
   constexpr int NN = 32 * I;
   constexpr int LOGN = (NN == 128) ? 7 : (NN == 256 ? 8 : 9);
   static_assert(NN == (1 << LOGN), "power of two");
   uint32_t key[I];
   uint32_t lo = 0xffffffffu, hi = 0u;
+  {
+    float dv[I], wv[I];
+    l1_load_run<I>(col_d, base, n, lane, vec, dv);
+    l1_load_run<I>(col_w, base, n, lane, vec, wv);
 #pragma unroll
-  for (int j = 0; j < I; ++j) {
-    const int e = lane * I + j;
-    key[j] = e < n ? __float_as_uint(col_d[base + e]) : 0u;
-    if (e < n) { lo = min(lo, key[j]); hi = max(hi, key[j]); }
+    for (int j = 0; j < I; ++j) {
+      const int e = lane * I + j;
+      key[j] = e < n ? __float_as_uint(dv[j]) : 0u;
+      if (e < n) { lo = min(lo, key[j]); hi = max(hi, key[j]); }
+    }
+#pragma unroll
+    for (int q = 0; q < I / 4; ++q)
+      *reinterpret_cast<float4*>(s_w + lane * I + 4 * q) =
+          make_float4(wv[4 * q], wv[4 * q + 1], wv[4 * q + 2], wv[4 * q + 3]);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -455,10 +517,11 @@ __device__ __forceinline__ bool l1_sort_pixel_packed(float* col_d, float* col_w,
   }
   float w[I];
   float lw = 0.f, lwd = 0.f;
+  __syncwarp();  // s_w holds every lane's weights
 #pragma unroll
   for (int j = 0; j < I; ++j) {
     const bool live = key[j] != 0xffffffffu;
-    w[j] = live ? col_w[base + (key[j] & (NN - 1))] : 0.f;
+    w[j] = live ? s_w[key[j] & (NN - 1)] : 0.f;
     lw += w[j];
     lwd += w[j] * (live ? __uint_as_float((key[j] >> LOGN) + lo) : 0.f);
   }
@@ -471,19 +534,23 @@ __device__ __forceinline__ bool l1_sort_pixel_packed(float* col_d, float* col_w,
   const float Wt = __shfl_sync(FULL, iw, 31), Dt = __shfl_sync(FULL, iwd, 31);
   float pw = iw - lw, pwd = iwd - lwd;
   float raw = 0.f;
-  __syncwarp();  // every lane has read its originals
+  __syncwarp();  // every lane has read its weights from s_w
 #pragma unroll
   for (int j = 0; j < I; ++j) {
     if (key[j] != 0xffffffffu) {
       const uint32_t k = key[j] & (NN - 1);
       const float d = __uint_as_float((key[j] >> LOGN) + lo);
       raw += 2.f * w[j] * (d * pw - pwd);
-      col_d[base + k] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
-      col_w[base + k] = 2.f * w[j] * (2.f * pw + w[j] - Wt);
+      s_o[k] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
+      s_w[k] = 2.f * w[j] * (2.f * pw + w[j] - Wt);
       pw += w[j];
       pwd += w[j] * d;
     }
   }
+  __syncwarp();  // both factors assembled by compositing index
+  l1_store_run<I>(col_d, base, n, lane, vec, s_o);
+  l1_store_run<I>(col_w, base, n, lane, vec, s_w);
+  __syncwarp();  // s_w / s_o free for the warp's next pixel
   raw_out = raw;
   return true;
 }
@@ -509,10 +576,21 @@ __global__ void __launch_bounds__(128) l1_resolve_kernel(
   const int tiles_x = (cam.width + TILE - 1) / TILE;
   float* col_d = l1s;
   float* col_w = l1s + slots;
-  for (int64_t pix = (int64_t)blockIdx.x * warps + wid; pix < npix;
-       pix += (int64_t)gridDim.x * warps) {
+  // per warp: weights parked by compositing index, and the second output column
+  constexpr int NMAX = CLASS == 0 ? 256 : 512;
+  __shared__ __align__(16) float s_stage[CLASS == 2 ? 1 : 4][CLASS == 2 ? 1 : 2 * NMAX];
+  float* s_w = s_stage[CLASS == 2 ? 0 : wid];
+  float* s_o = s_w + (CLASS == 2 ? 0 : NMAX);
+  // 16-byte loads and stores need aligned columns (runs start on 8-sample boundaries)
+  const bool vec = ((reinterpret_cast<uintptr_t>(l1s) | (uintptr_t)(slots * sizeof(float))) & 15) == 0;
+  const int64_t stride = (int64_t)gridDim.x * warps;
+  int64_t pix = (int64_t)blockIdx.x * warps + wid;
+  // the sample count of the warp's next pixel is loaded one pixel ahead
+  int n_next = pix < npix ? f2i(state[pix * SF_PIXEL_STATE_FLOATS + PS_COUNT]) : 0;
+  for (; pix < npix; pix += stride) {
     float* st = state + pix * SF_PIXEL_STATE_FLOATS;
-    int n = f2i(st[PS_COUNT]);
+    int n = n_next;
+    if (pix + stride < npix) n_next = f2i(state[(pix + stride) * SF_PIXEL_STATE_FLOATS + PS_COUNT]);
     const int u = (int)(pix % cam.width), v = (int)(pix / cam.width);
     const int tile = (v / TILE) * tiles_x + (u / TILE);
     const int tid = (v % TILE) * TILE + (u % TILE);
@@ -527,14 +605,14 @@ __global__ void __launch_bounds__(128) l1_resolve_kernel(
       if (n <= 1) {
         if (n == 1 && lane == 0) { col_d[base] = 0.f; col_w[base] = 0.f; }
       } else if (n <= 128) {
-        if (!l1_sort_pixel_packed<4>(col_d, col_w, base, n, lane, raw))
+        if (!l1_sort_pixel_packed<4>(col_d, col_w, base, n, lane, vec, s_w, s_o, raw))
           raw = l1_sort_pixel<4>(col_d, col_w, base, n, lane);
       } else {
-        if (!l1_sort_pixel_packed<8>(col_d, col_w, base, n, lane, raw))
+        if (!l1_sort_pixel_packed<8>(col_d, col_w, base, n, lane, vec, s_w, s_o, raw))
           raw = l1_sort_pixel<8>(col_d, col_w, base, n, lane);
       }
     } else if (CLASS == 1) {
-      if (!l1_sort_pixel_packed<16>(col_d, col_w, base, n, lane, raw))
+      if (!l1_sort_pixel_packed<16>(col_d, col_w, base, n, lane, vec, s_w, s_o, raw))
         raw = l1_sort_pixel<16>(col_d, col_w, base, n, lane);
     } else {
       // long runs: stable warp radix sort staged in shared memory

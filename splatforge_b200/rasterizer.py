@@ -78,6 +78,11 @@ class RasterSettings:
     background: tuple = (1.0, 1.0, 1.0)
     antialiased: bool = False
     tile_size: int = 16
+    # a pixel stops compositing once its transmittance falls below this floor; the skipped
+    # tail changes any weight sum by less than the floor.  AmbiSuR renders that include a
+    # distortion do not stop early: their plane depths plane / (n . ray) are unbounded at
+    # grazing angles, so a skipped sample's share of L1 / L2 (linear / quadratic in depth)
+    # has no bound
     transmittance_floor: float = 1e-6
     # per-pixel L1 sample capacity of the first forward attempt; None adapts to the
     # largest count seen for this image size (a pixel over capacity triggers an exact
@@ -108,7 +113,7 @@ class RasterSettings:
         s.near_plane = float(self.near)
         s.far_plane = float(self.far)
         s.background[:] = [float(v) for v in self.background]
-        s.t_stop = float(self.transmittance_floor)
+        s.t_stop = 0.0 if (self.mode == "ambisur" and self.distortions != "none") else float(self.transmittance_floor)
         return s
 
 
