@@ -180,6 +180,9 @@ class RenderJob:
         self.n = self.p.means.shape[0]
         self.dev = dev
         self.reducer = distributed.GradientAllReduce(self.p.tensors(), timed=True)
+        if world > 1:
+            # the gradients accumulate in the all-reduce buffer itself (no copy in or out)
+            self.reducer.bind()
         self.last = None
 
     def cams(self, s, distinct=False):
@@ -191,8 +194,7 @@ class RenderJob:
     def step(self, s, distinct=False):
         from splatforge_b200 import rasterizer, scenes
 
-        for t in self.p.tensors():
-            t.grad = None
+        self.reducer.zero_grad()
         for c in self.cams(s, distinct):
             view = scenes.activated(self.p)
             out = rasterizer.rasterize(view.means, view.quats, view.scales, view.opacities, view.sh, 3, c,
@@ -375,6 +377,9 @@ def e2e_render(job, args, dev, rank, world, B200Renderer, distributed, scenes):
     h2d = sum(t.numel() * t.element_size() for t in host)
     loss_host = torch.empty((), pin_memory=True)
     reducers = [distributed.GradientAllReduce(b) for b in bufs]
+    if world > 1:
+        for r in reducers:
+            r.bind()
     copy_stream = torch.cuda.Stream(device=dev)
     ready = [torch.cuda.Event() for _ in range(2)]
     freed = [torch.cuda.Event() for _ in range(2)]
@@ -397,7 +402,7 @@ def e2e_render(job, args, dev, rank, world, B200Renderer, distributed, scenes):
             dev_params = bufs[slot]
             for d in dev_params:
                 d.requires_grad_(True)
-                d.grad = None
+            reducers[slot].zero_grad()
             sp = scenes.SceneParams(*dev_params, sh_degree=3)
             total = 0.0
             for c in job.cams(k):
@@ -432,7 +437,10 @@ def secondary(args, dev, rank, world):
     (values over all ranks; time = max over ranks)."""
     out = {}
     job = RenderJob("surfaces3m_views64", dev, rank, world, "gof", "l1")
-    ms_rank, per_step = time_steps(job, max(3, min(args.steps, 10)), 3)
+    # warm-up over every pose a rank renders (64 / (8 N) steps), so that the per-size L1
+    # sample capacity has settled before the timed steps
+    warm = max(3, len(job.poses) // (job.per * world))
+    ms_rank, per_step = time_steps(job, max(3, min(args.steps, 10)), warm)
     ms = _max_over_ranks(ms_rank, dev, world)
     coll = job.reducer.timings_ms() or (0.0, 0.0, 0.0)
     ranks = _gather([_median(per_step), *coll], dev, world)
@@ -443,6 +451,7 @@ def secondary(args, dev, rank, world):
         "workload": f"surfaces3m_views64: {job.n} Gaussians, {job.W}x{job.H}, mode gof, distortions l1 "
                     f"(the training profile), fwd+bwd, {job.per} views per GPU per step, {views} per step",
         "poses": f"rank r renders poses 8(r + sN) .. +7 of the {len(job.poses)} (mod {len(job.poses)}) at step s",
+        "warmup_steps": warm, "step_ms_this_rank": [round(x, 2) for x in per_step],
         "step_ms_median": [round(r[0], 3) for r in ranks], "allreduce_ms": [round(r[2], 3) for r in ranks],
         "pack_unpack_ms": [round(r[1] + r[3], 3) for r in ranks]}
     del job
@@ -467,13 +476,13 @@ def field_measure(dev, rank, world, *, steps, warmup, e2e=True, no_cpu_baseline=
     2M Gaussians, 32 view origins; rank r evaluates shard r mod 8 of the ~20M queries
     (weak scaling: 8 shards at 8 GPUs), with no collective on the data path.  Returns the
     rank-0 record (None elsewhere)."""
-    from splatforge_b200 import ops, rasterizer, scenes
+    from splatforge_b200 import distributed, ops, rasterizer, scenes
 
     params, cams = scenes.workload(workload, seed=0)
     view = scenes.activated(params)
     queries = scenes.field_queries(params, 2_000_000, seed=0)
     q = queries.shape[0]
-    lo, hi = (rank % FIELD_SHARDS) * q // FIELD_SHARDS, (rank % FIELD_SHARDS + 1) * q // FIELD_SHARDS
+    lo, hi = distributed.query_shard(q, rank, FIELD_SHARDS)
     host = {"pts": queries[lo:hi].contiguous().pin_memory(), "means": view.means.contiguous().pin_memory(),
             "Q": scenes.inverse_covariances(params).contiguous().pin_memory(),
             "opac": view.opacities.contiguous().pin_memory(),

@@ -33,6 +33,14 @@ def shard(items, rank, world):
     return items[lo:hi]
 
 
+def query_shard(n, rank, shards):
+    """[lo, hi) of query shard ``rank mod shards`` when ``n`` queries are cut into
+    ``shards`` contiguous shards of sizes differing by at most one (the opacity-field
+    workload: no collective, every rank evaluates its own queries)."""
+    r = rank % shards
+    return r * n // shards, (r + 1) * n // shards
+
+
 def init_from_env(backend=None, timeout_s=120):
     """``torch.distributed`` from torchrun's RANK / WORLD_SIZE / LOCAL_RANK / MASTER_*.
     NCCL on CUDA (device bound to LOCAL_RANK), gloo otherwise.  A short timeout makes
@@ -58,6 +66,12 @@ class GradientAllReduce:
 
     ``params`` is a sequence of the five parameter tensors in PARAM_ORDER (each [N, ...]).
     The packed buffer is allocated once and reused every step.
+
+    With ``bind()`` the buffer is laid out parameter by parameter (means [N,3], then
+    log-scales [N,3], quaternions [N,4], opacity logits [N], SH [N,3K]) and every
+    parameter's ``.grad`` is a view of its block: autograd accumulates into the buffer in
+    place, so the collective runs on the gradients where they already are, with no copy
+    in or out.  ``zero_grad()`` clears the buffer at the start of a step.
     """
 
     def __init__(self, params, *, group=None, average=False, timed=False):
@@ -76,19 +90,52 @@ class GradientAllReduce:
         # recorded on the current stream around every call
         self.timed = timed
         self.events = []
+        self.bound = False
+
+    def bind(self):
+        """Make every parameter's ``.grad`` a view of its block of the (flat) buffer."""
+        flat = self.buffer.view(-1)
+        col = 0
+        self.views = []
+        for p, w in zip(self.params, self.widths):
+            v = flat[col * self.n:(col + w) * self.n].view(p.shape)
+            self.views.append(v)
+            col += w
+        self.bound = True
+        self.zero_grad()
+        return self
+
+    def zero_grad(self):
+        """Zero the buffer and (re)attach the views as the parameters' gradients."""
+        if not self.bound:
+            for p in self.params:
+                p.grad = None
+            return
+        self.buffer.zero_()
+        for p, v in zip(self.params, self.views):
+            p.grad = v
+
+    def _in_place(self):
+        return self.bound and all(
+            p.grad is not None and p.grad.data_ptr() == v.data_ptr() for p, v in zip(self.params, self.views))
 
     @property
     def floats_per_gaussian(self):
         return sum(self.widths)
 
     def pack(self):
+        lo, hi = self.buffer.data_ptr(), self.buffer.data_ptr() + self.buffer.numel() * self.buffer.element_size()
+        # gradients that still alias the buffer (a bound reducer whose views were partly
+        # replaced) are copied out before the buffer is overwritten
+        grads = [None if p.grad is None else (p.grad.clone() if lo <= p.grad.data_ptr() < hi else p.grad)
+                 for p in self.params]
         col = 0
-        for p, w in zip(self.params, self.widths):
+        for g, w in zip(grads, self.widths):
             view = self.buffer[:, col : col + w]
-            if p.grad is None:
+            if g is None:
                 view.zero_()
             else:
-                view.copy_(p.grad.reshape(self.n, w))
+                view.copy_(g.reshape(self.n, w))
             col += w
         return self.buffer
 
@@ -106,9 +153,11 @@ class GradientAllReduce:
         if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(self.group) == 1:
             return
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if self.timed else None
+        in_place = self._in_place()
         if ev:
             ev[0].record()
-        self.pack()
+        if not in_place:
+            self.pack()
         if ev:
             ev[1].record()
         dist.all_reduce(self.buffer, op=dist.ReduceOp.SUM, group=self.group)
@@ -116,7 +165,8 @@ class GradientAllReduce:
             self.buffer /= dist.get_world_size(self.group)
         if ev:
             ev[2].record()
-        self.unpack()
+        if not in_place:
+            self.unpack()
         if ev:
             ev[3].record()
             self.events.append(ev)

@@ -28,8 +28,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _grads_for(views, params):
-    p = params.detach_clone().requires_grad_()
+def _grads_for(views, params, p=None):
+    p = params.detach_clone().requires_grad_() if p is None else p
     for cam in views:
         out = oracle_render.render(scenes.activated(p), cam, mode="gof", distortions="l1")
         sum(out[c].sum() for c in CH).backward()
@@ -46,8 +46,15 @@ def _worker(rank, world, port, mode, queue):
         mine = distributed.shard(cams[:4], rank, world)
         if mode == "fail" and rank == 1:
             raise RuntimeError("rank 1 failed before the all-reduce")
-        p = _grads_for(mine, params)
-        reducer = distributed.GradientAllReduce(p.tensors())
+        if mode == "bound":
+            # gradients accumulate straight into the collective's buffer
+            p = params.detach_clone().requires_grad_()
+            reducer = distributed.GradientAllReduce(p.tensors()).bind()
+            _grads_for(mine, params, p)
+            assert reducer._in_place()
+        else:
+            p = _grads_for(mine, params)
+            reducer = distributed.GradientAllReduce(p.tensors())
         assert reducer.floats_per_gaussian == 59
         reducer()
         queue.put((rank, "ok", [t.grad.clone() for t in p.tensors()]))
@@ -84,6 +91,50 @@ def test_allreduced_gradients_equal_full_batch_gradients():
     for rank in (0, 1):
         for got, want in zip(res[rank][1], full.tensors()):
             torch.testing.assert_close(got, want.grad, atol=2e-5, rtol=1e-4)
+
+
+def test_gradients_bound_to_the_buffer_reduce_in_place():
+    res = _run("bound")
+    assert all(s == "ok" for s, _ in res.values()), res
+    params, cams = scenes.workload("demo48", seed=0)
+    full = _grads_for(cams[:4], params)
+    for rank in (0, 1):
+        for got, want in zip(res[rank][1], full.tensors()):
+            torch.testing.assert_close(got, want.grad, atol=2e-5, rtol=1e-4)
+
+
+def test_bound_views_and_fallback_packing_on_one_process():
+    params, _ = scenes.workload("demo48", seed=0)
+    p = params.detach_clone().requires_grad_()
+    r = distributed.GradientAllReduce(p.tensors()).bind()
+    flat = r.buffer.view(-1)
+    offset = 0
+    for t in p.tensors():
+        assert t.grad.data_ptr() == flat[offset:].data_ptr() and t.grad.shape == t.shape
+        offset += t.numel()
+    assert offset == flat.numel() and float(flat.abs().sum()) == 0.0
+    # a replaced gradient: packing copies every gradient, aliasing ones included
+    for k, t in enumerate(p.tensors()):
+        t.grad.fill_(k + 1.0)
+    p.means.grad = torch.full_like(p.means, 7.0)
+    assert not r._in_place()
+    buf = r.pack().clone()
+    col = 0
+    for k, (t, w) in enumerate(zip(p.tensors(), r.widths)):
+        want = 7.0 if k == 0 else k + 1.0
+        assert torch.all(buf[:, col:col + w] == want)
+        col += w
+
+
+def test_query_shards_partition_the_query_set():
+    for n, shards in ((20_000_001, 8), (7, 8), (0, 8), (1000, 3)):
+        spans = [distributed.query_shard(n, r, shards) for r in range(shards)]
+        assert spans[0][0] == 0 and spans[-1][1] == n
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        sizes = [hi - lo for lo, hi in spans]
+        assert max(sizes) - min(sizes) <= 1
+    # more ranks than shards: rank r evaluates shard r mod shards
+    assert distributed.query_shard(100, 9, 8) == distributed.query_shard(100, 1, 8)
 
 
 def test_failed_rank_ends_its_peer_with_an_error_not_a_hang():
