@@ -328,12 +328,16 @@ __global__ void emit_kernel(const int32_t* order, const int64_t* offsets, const 
     const long long os = __shfl_sync(FULL, o, src);
     const int gs = __shfl_sync(FULL, g, src);
     const int xs = __shfl_sync(FULL, x0, src), ys = __shfl_sync(FULL, y0, src), ws = __shfl_sync(FULL, w, src);
+    // row/column of entry k in the rectangle without an integer division: lane starts at
+    // (lane / ws, lane % ws) and every step of 32 entries advances by (32 / ws, 32 % ws)
+    int row = lane / ws, col = lane - (lane / ws) * ws;
+    const int drow = 32 / ws, dcol = 32 - drow * ws;
     for (long long k = lane; k < cs; k += 32) {
-      const int kk = (int)k;
-      const int row = kk / ws;
-      const int col = kk - row * ws;
       tiles[os + k] = (uint32_t)((ys + row) * tiles_x + xs + col);
       ids[os + k] = gs;
+      row += drow;
+      col += dcol;
+      if (col >= ws) { col -= ws; ++row; }
     }
   }
 }

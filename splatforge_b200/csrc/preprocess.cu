@@ -63,6 +63,7 @@ __device__ __forceinline__ void write_bounds(int64_t i, float x, float y, float 
   depth_key[i] = c > 0 ? __float_as_uint(z) : 0xffffffffu;
 }
 
+template <int MODE>
 __global__ void __launch_bounds__(PB) project_forward_kernel(
     const float* __restrict__ means, const float* __restrict__ quats,
     const float* __restrict__ scales, const float* __restrict__ opacities,
@@ -101,13 +102,13 @@ __global__ void __launch_bounds__(PB) project_forward_kernel(
   sh_color(s_sh + threadIdx.x * stride, st.sh_degree, dir, rec + R_RGB);
   rec[R_SEL] = selected && selected[i] ? 1.f : 0.f;
   rec[R_Z] = p.mc[2];
-  if (st.mode == SF_MODE_RADEGS) {
+  if (MODE == SF_MODE_RADEGS) {
     RadeExtras e;
     rade_extras(p, e);
     rec[R_RADIAL] = e.radial;
     rec[R_GAIN] = e.gain[0]; rec[R_GAIN + 1] = e.gain[1];
     rec[R_NRM] = e.normal[0]; rec[R_NRM + 1] = e.normal[1]; rec[R_NRM + 2] = e.normal[2];
-  } else if (st.mode == SF_MODE_GOF) {
+  } else if (MODE == SF_MODE_GOF) {
     const float fx = cam.K[0], fy = cam.K[4], cx = cam.K[2], cy = cam.K[5];
     rec[R_PROXY] = (p.X - cx) * p.mc[2] / fx;
     rec[R_PROXY + 1] = (p.Y - cy) * p.mc[2] / fy;
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(PB) project_forward_kernel(
                st.far_plane, rect, count, depth_key, nonfinite);
 }
 
+template <int MODE>
 __global__ void __launch_bounds__(PB) project_backward_kernel(
     const float* __restrict__ means, const float* __restrict__ quats,
     const float* __restrict__ scales, const float* __restrict__ opacities,
@@ -158,8 +160,8 @@ __global__ void __launch_bounds__(PB) project_backward_kernel(
     float gm[3], gq[4], gs[3], go;
     float* coeffs = s_sh + threadIdx.x * stride;
     // the SH adjoint replaces the staged coefficients in place (read before written)
-    project_backward(m, q, sc, opacities[i], coeffs, st.sh_degree, cam, st, gx, g, gm, gq, gs,
-                     &go, coeffs);
+    project_backward_mode<MODE>(m, q, sc, opacities[i], coeffs, st.sh_degree, cam, st, gx, g, gm, gq, gs,
+                                &go, coeffs);
     if (g_means) { g_means[i * 3] = gm[0]; g_means[i * 3 + 1] = gm[1]; g_means[i * 3 + 2] = gm[2]; }
     if (g_quats)
       reinterpret_cast<float4*>(g_quats)[i] = make_float4(gq[0], gq[1], gq[2], gq[3]);
@@ -243,9 +245,14 @@ cudaError_t launch_project_forward(const float* means, const float* quats, const
   if (n == 0) return cudaSuccess;
   const size_t smem = (size_t)PB * (st.sh_coeffs * 3 + 1) * sizeof(float);
   count_launches(1);
-  project_forward_kernel<<<blocks_for(n, PB), PB, smem, s>>>(
-      means, quats, scales, opacities, sh, selected, n, cam, st, means2d, radii, records, rect,
-      count, depth_key, nonfinite);
+#define SF_PROJECT_FORWARD(M)                                                                              \
+  project_forward_kernel<M><<<blocks_for(n, PB), PB, smem, s>>>(means, quats, scales, opacities, sh, selected, n, \
+                                                                 cam, st, means2d, radii, records, rect, count,   \
+                                                                 depth_key, nonfinite)
+  if (st.mode == SF_MODE_RADEGS) SF_PROJECT_FORWARD(SF_MODE_RADEGS);
+  else if (st.mode == SF_MODE_GOF) SF_PROJECT_FORWARD(SF_MODE_GOF);
+  else SF_PROJECT_FORWARD(SF_MODE_AMBISUR);
+#undef SF_PROJECT_FORWARD
   return cudaGetLastError();
 }
 
@@ -258,9 +265,14 @@ cudaError_t launch_project_backward(const float* means, const float* quats, cons
   if (n == 0) return cudaSuccess;
   const size_t smem = (size_t)PB * (st.sh_coeffs * 3 + 1) * sizeof(float);
   count_launches(1);
-  project_backward_kernel<<<blocks_for(n, PB), PB, smem, s>>>(
-      means, quats, scales, opacities, sh, n, cam, st, gxy, grec, g_means, g_quats, g_scales,
-      g_opacities, g_sh);
+#define SF_PROJECT_BACKWARD(M)                                                                            \
+  project_backward_kernel<M><<<blocks_for(n, PB), PB, smem, s>>>(means, quats, scales, opacities, sh, n, cam, st, \
+                                                                  gxy, grec, g_means, g_quats, g_scales,          \
+                                                                  g_opacities, g_sh)
+  if (st.mode == SF_MODE_RADEGS) SF_PROJECT_BACKWARD(SF_MODE_RADEGS);
+  else if (st.mode == SF_MODE_GOF) SF_PROJECT_BACKWARD(SF_MODE_GOF);
+  else SF_PROJECT_BACKWARD(SF_MODE_AMBISUR);
+#undef SF_PROJECT_BACKWARD
   return cudaGetLastError();
 }
 

@@ -190,7 +190,10 @@ SF_HD float sample_adj(const float* rec, const Sample& s, const PixelGrads& pg, 
 
 // ---------------------------------------------------------------- projection adjoint
 // Reverse of project() + mode extras + SH colour, for one Gaussian.
-SF_HD void project_backward(const float* mean, const float* quat, const float* scale,
+// MODE fixed at compile time (the kernels instantiate one per rendering mode); the
+// untemplated overload below dispatches on st.mode
+template <int MODE>
+SF_HD void project_backward_mode(const float* mean, const float* quat, const float* scale,
                             float opacity, const float* sh, int degree, const sf_camera& cam,
                             const sf_settings& st, const float* gxy, const float* grec,
                             float* g_mean, float* g_quat, float* g_scale, float* g_opacity,
@@ -248,7 +251,7 @@ SF_HD void project_backward(const float* mean, const float* quat, const float* s
       gCc[i * 3 + j] += acc;
     }
   // mode extras
-  if (st.mode == SF_MODE_RADEGS) {
+  if (MODE == SF_MODE_RADEGS) {
     RadeExtras e;
     rade_extras(p, e);
     float g_rad = grec[R_RADIAL];
@@ -290,7 +293,7 @@ SF_HD void project_backward(const float* mean, const float* quat, const float* s
     float gmh[3] = {gF[6], gF[7], gF[8]}, gm[3];
     unit3_backward(p.mc, gmh, gm);
     for (int k = 0; k < 3; ++k) g_mc[k] += gm[k];
-  } else if (st.mode == SF_MODE_GOF) {
+  } else if (MODE == SF_MODE_GOF) {
     float Q[6];
     inv3_sym(p.Cc, Q);
     float Qf[9] = {Q[0], Q[1], Q[2], Q[1], Q[3], Q[4], Q[2], Q[4], Q[5]};
@@ -313,10 +316,13 @@ SF_HD void project_backward(const float* mean, const float* quat, const float* s
       gn[k] = grec[R_ANRM + k] + gpl * p.mc[k];
       g_mc[k] += gpl * e.normal[k];
     }
-    int a = e.axis;
+    const int a = e.axis;
+#pragma unroll
     for (int j = 0; j < 3; ++j) {
-      float gw = e.sign * (cam.R[0 * 3 + j] * gn[0] + cam.R[1 * 3 + j] * gn[1] + cam.R[2 * 3 + j] * gn[2]);
-      gR[j * 3 + a] += gw;
+      const float gw = e.sign * (cam.R[0 * 3 + j] * gn[0] + cam.R[1 * 3 + j] * gn[1] + cam.R[2 * 3 + j] * gn[2]);
+#pragma unroll
+      for (int c = 0; c < 3; ++c)
+        if (c == a) gR[j * 3 + c] += gw;  // constant indices (keeps gR in registers)
     }
   }
   // J and the projected mean -> guarded (x, y, z)
@@ -350,9 +356,24 @@ SF_HD void project_backward(const float* mean, const float* quat, const float* s
   // SH colour (live) and AmbiSuR ray colour (detached direction)
   float dir[3] = {mean[0] - cam.origin[0], mean[1] - cam.origin[1], mean[2] - cam.origin[2]};
   float gdir[3];
-  sh_color_backward(sh, degree, dir, grec + R_RGB, st.mode == SF_MODE_AMBISUR ? grec + G_RAYC : nullptr,
+  sh_color_backward(sh, degree, dir, grec + R_RGB, MODE == SF_MODE_AMBISUR ? grec + G_RAYC : nullptr,
                     g_sh, gdir);
   for (int k = 0; k < 3; ++k) g_mean[k] += gdir[k];
+}
+
+SF_HD void project_backward(const float* mean, const float* quat, const float* scale, float opacity,
+                            const float* sh, int degree, const sf_camera& cam, const sf_settings& st,
+                            const float* gxy, const float* grec, float* g_mean, float* g_quat, float* g_scale,
+                            float* g_opacity, float* g_sh) {
+  if (st.mode == SF_MODE_RADEGS)
+    project_backward_mode<SF_MODE_RADEGS>(mean, quat, scale, opacity, sh, degree, cam, st, gxy, grec, g_mean,
+                                          g_quat, g_scale, g_opacity, g_sh);
+  else if (st.mode == SF_MODE_GOF)
+    project_backward_mode<SF_MODE_GOF>(mean, quat, scale, opacity, sh, degree, cam, st, gxy, grec, g_mean, g_quat,
+                                       g_scale, g_opacity, g_sh);
+  else
+    project_backward_mode<SF_MODE_AMBISUR>(mean, quat, scale, opacity, sh, degree, cam, st, gxy, grec, g_mean,
+                                           g_quat, g_scale, g_opacity, g_sh);
 }
 
 }  // namespace sf

@@ -200,11 +200,16 @@ SF_HD void sh_color(const float* coeffs, int degree, const float* dir, float* rg
   float d[3];
   unit3(dir, d);
   float b[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) b[k] = 0.f;
   sh_basis(d[0], d[1], d[2], degree, b);
-  int K = sh_count(degree);
+  const int K = sh_count(degree);
+#pragma unroll
   for (int c = 0; c < 3; ++c) {
     float acc = 0.f;
-    for (int k = 0; k < K; ++k) acc += coeffs[k * 3 + c] * b[k];
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      if (k < K) acc += coeffs[k * 3 + c] * b[k];
     rgb[c] = fmaxr(0.5f + acc, 0.f);
   }
 }
@@ -216,24 +221,35 @@ SF_HD void sh_color_backward(const float* coeffs, int degree, const float* dir,
                              float* g_dir) {
   float d[3];
   unit3(dir, d);
+  // fixed-size loops with a bound check (k < K), fully unrolled, so that b and gb stay
+  // in registers for any degree
   float b[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) b[k] = 0.f;
   sh_basis(d[0], d[1], d[2], degree, b);
-  int K = sh_count(degree);
+  const int K = sh_count(degree);
   float gl[3], gdt[3];
+#pragma unroll
   for (int c = 0; c < 3; ++c) {
     float acc = 0.f;
-    for (int k = 0; k < K; ++k) acc += coeffs[k * 3 + c] * b[k];
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      if (k < K) acc += coeffs[k * 3 + c] * b[k];
     bool pass = (0.5f + acc) >= 0.f;  // clamp_min(0) passes at >= 0
     gl[c] = pass && g_live ? g_live[c] : 0.f;
     gdt[c] = pass && g_detached ? g_detached[c] : 0.f;
   }
   float gb[16];
-  for (int k = 0; k < K; ++k) {
-    gb[k] = coeffs[k * 3 + 0] * gl[0] + coeffs[k * 3 + 1] * gl[1] + coeffs[k * 3 + 2] * gl[2];
-    if (g_coeffs) {
-      g_coeffs[k * 3 + 0] = b[k] * (gl[0] + gdt[0]);
-      g_coeffs[k * 3 + 1] = b[k] * (gl[1] + gdt[1]);
-      g_coeffs[k * 3 + 2] = b[k] * (gl[2] + gdt[2]);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    gb[k] = 0.f;
+    if (k < K) {
+      gb[k] = coeffs[k * 3 + 0] * gl[0] + coeffs[k * 3 + 1] * gl[1] + coeffs[k * 3 + 2] * gl[2];
+      if (g_coeffs) {
+        g_coeffs[k * 3 + 0] = b[k] * (gl[0] + gdt[0]);
+        g_coeffs[k * 3 + 1] = b[k] * (gl[1] + gdt[1]);
+        g_coeffs[k * 3 + 2] = b[k] * (gl[2] + gdt[2]);
+      }
     }
   }
   if (g_dir) {
@@ -494,7 +510,10 @@ SF_HD void ambi_extras(const float* scale, const Projection& p, const sf_camera&
   if (scale[1] < scale[a]) a = 1;
   if (scale[2] < scale[a]) a = 2;
   e.axis = a;
-  const float w0 = p.R[0 * 3 + a], w1 = p.R[1 * 3 + a], w2 = p.R[2 * 3 + a];
+  // column a of R, selected with constant indices (keeps R in registers)
+  const float w0 = a == 0 ? p.R[0] : (a == 1 ? p.R[1] : p.R[2]);
+  const float w1 = a == 0 ? p.R[3] : (a == 1 ? p.R[4] : p.R[5]);
+  const float w2 = a == 0 ? p.R[6] : (a == 1 ? p.R[7] : p.R[8]);
   float nc[3];
   for (int i = 0; i < 3; ++i) nc[i] = dot3_rn(w0, w1, w2, cam.R[i * 3 + 0], cam.R[i * 3 + 1], cam.R[i * 3 + 2]);
   const float facing = dot3_rn(nc[0], nc[1], nc[2], p.mc[0], p.mc[1], p.mc[2]);
