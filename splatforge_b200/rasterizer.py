@@ -26,6 +26,11 @@ from . import _lib
 from ._lib import L1_SAMPLE_FLOATS, PIXEL_STATE_FLOATS, RECORD_FLOATS, Camera, Settings, call
 
 TILE = 16
+# transmittance floor of AmbiSuR renders with distortions: 1e-30 x (far = 1e4)^2 bounds the
+# skipped tail's share of L2 by 1e-22, and the floor keeps the final transmittance (kept in
+# float32 for the backward, which recovers each sample's transmittance from it by
+# division) far above float32 underflow
+AMBISUR_DISTORTION_FLOOR = 1e-30
 
 # Optional instrumentation used by bench.py: when PROFILE is a dict, CUDA events are
 # recorded on the launching stream around the raster forward / backward calls and
@@ -80,9 +85,9 @@ class RasterSettings:
     tile_size: int = 16
     # a pixel stops compositing once its transmittance falls below this floor; the skipped
     # tail changes any weight sum by less than the floor.  AmbiSuR renders that include a
-    # distortion do not stop early: their plane depths plane / (n . ray) are unbounded at
-    # grazing angles, so a skipped sample's share of L1 / L2 (linear / quadratic in depth)
-    # has no bound
+    # distortion stop only at AMBISUR_DISTORTION_FLOOR: their plane depths plane / (n . ray)
+    # reach the far plane at grazing angles, so the tail's share of L1 / L2 (linear /
+    # quadratic in depth) is bounded by floor x far^2 only
     transmittance_floor: float = 1e-6
     # per-pixel L1 sample capacity of the first forward attempt; None adapts to the
     # largest count seen for this image size (a pixel over capacity triggers an exact
@@ -113,7 +118,8 @@ class RasterSettings:
         s.near_plane = float(self.near)
         s.far_plane = float(self.far)
         s.background[:] = [float(v) for v in self.background]
-        s.t_stop = 0.0 if (self.mode == "ambisur" and self.distortions != "none") else float(self.transmittance_floor)
+        s.t_stop = (AMBISUR_DISTORTION_FLOOR if (self.mode == "ambisur" and self.distortions != "none")
+                    else float(self.transmittance_floor))
         return s
 
 
