@@ -22,6 +22,16 @@ namespace sf {
 namespace {
 
 constexpr int REC4 = SF_RECORD_FLOATS / 4;  // float4 per record
+// Records staged per shared-memory batch (forward, backward); build-time parameters.
+#ifndef SF_FWD_BATCH
+#define SF_FWD_BATCH 384
+#endif
+#ifndef SF_BWD_BATCH
+#define SF_BWD_BATCH 256
+#endif
+constexpr int FWD_BATCH = SF_FWD_BATCH;
+constexpr int BWD_BATCH = SF_BWD_BATCH;
+static_assert(FWD_BATCH % 32 == 0 && BWD_BATCH % 32 == 0, "batches are whole culling groups");
 constexpr int ACC = 24;                      // accumulator floats per batch slot (20 + absgrad 2 + pad)
 // The backward's per-batch accumulator covers record slots [BASE, 24) of each Gaussian:
 // GOF never produces adjoints for slots 0-3 (xy and the 2D conic), so its accumulator
@@ -102,7 +112,8 @@ __device__ __forceinline__ void l1_flush(float* l1s, int64_t slots, int64_t at, 
 
 template <int MODE, int DIST>
 __global__ void __launch_bounds__(TILE_PIXELS, 4) raster_forward_kernel(const RasterFwdArgs a) {
-  __shared__ float4 s_rec[TILE_PIXELS * REC4];
+  extern __shared__ float4 s_dyn[];  // the batch's records: FWD_BATCH * REC4 float4
+  float4* s_rec = s_dyn;
   __shared__ float s_ring[(DIST & SF_DIST_L1) ? 2 : 1][L1_RING][TILE_PIXELS];
   __shared__ int s_max;
   const int tile = blockIdx.x;
@@ -139,9 +150,9 @@ __global__ void __launch_bounds__(TILE_PIXELS, 4) raster_forward_kernel(const Ra
   if (tid == 0) s_max = 0;
   __syncthreads();
 
-  for (int base = rg.x; base < rg.y; base += TILE_PIXELS) {
+  for (int base = rg.x; base < rg.y; base += FWD_BATCH) {
     if (__syncthreads_count(done) == TILE_PIXELS) break;
-    const int n_in = min(TILE_PIXELS, rg.y - base);
+    const int n_in = min(FWD_BATCH, rg.y - base);
     for (int k = tid; k < n_in * REC4; k += TILE_PIXELS) {
       const int slot = k / REC4, comp = k - slot * REC4;
       const int id = __ldg(a.ids + base + slot);
@@ -670,10 +681,13 @@ __global__ void __launch_bounds__(128) l1_resolve_kernel(
 // ------------------------------------------------------------------ backward
 template <int MODE, int DIST>
 __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const RasterBwdArgs a) {
-  __shared__ float4 s_rec[TILE_PIXELS * REC4];
-  __shared__ int s_id[TILE_PIXELS];
   constexpr int AB = AccWindow<MODE>::BASE, AN = AccWindow<MODE>::N;
-  __shared__ float s_acc[TILE_PIXELS * AN];
+  // the batch's records (BWD_BATCH * REC4 float4), gradient accumulator (BWD_BATCH * AN
+  // floats) and Gaussian ids (BWD_BATCH ints), in dynamic shared memory
+  extern __shared__ float4 s_dyn[];
+  float4* s_rec = s_dyn;
+  float* s_acc = reinterpret_cast<float*>(s_dyn + BWD_BATCH * REC4);
+  int* s_id = reinterpret_cast<int*>(s_dyn + BWD_BATCH * REC4 + BWD_BATCH * AN / 4);
   __shared__ int s_max;
   constexpr int NV = SampleLayout<MODE>::NV;
   const int tile = blockIdx.x;
@@ -742,8 +756,8 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
   const int maxlast = s_max;
   float S = 0.f;
 
-  for (int hi = maxlast; hi > rg.x; hi -= TILE_PIXELS) {
-    const int lo = max(rg.x, hi - TILE_PIXELS);
+  for (int hi = maxlast; hi > rg.x; hi -= BWD_BATCH) {
+    const int lo = max(rg.x, hi - BWD_BATCH);
     const int n_in = hi - lo;
     __syncthreads();
     for (int q = tid; q < n_in * REC4; q += TILE_PIXELS) {
@@ -861,15 +875,53 @@ __global__ void pixel_counts_kernel(const float* state, int64_t npix, int32_t* c
   if (i < npix) counts[i] = (f2i(state[i * SF_PIXEL_STATE_FLOATS + PS_COUNT]) + 7) & ~7;
 }
 
+// Dynamic shared memory above the 48 KB default needs the per-kernel opt-in, set once
+// per kernel instance; the carveout preference asks for the shared memory that `ctas`
+// resident CTAs of `bytes` dynamic + `fixed` static bytes need (plus 1 KB reserved each).
+template <typename K>
+cudaError_t configure_smem(K kernel, size_t bytes, size_t fixed, int ctas, bool& done) {
+  if (done) return cudaSuccess;
+  cudaError_t e = cudaSuccess;
+  if (bytes > 48 * 1024) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  const size_t need = (size_t)ctas * (bytes + fixed + 1024);
+  if (e == cudaSuccess && need > 132 * 1024) {
+    const int pct = (int)((need * 100 + 228 * 1024 - 1) / (228 * 1024));
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, pct > 100 ? 100 : pct);
+  }
+  if (e == cudaSuccess) done = true;
+  return e;
+}
+
+template <int MODE, int DIST>
+cudaError_t fwd_launch(const RasterFwdArgs& a, int n_tiles, cudaStream_t s) {
+  constexpr size_t bytes = sizeof(float4) * FWD_BATCH * REC4;
+  constexpr size_t ring = sizeof(float) * ((DIST & SF_DIST_L1) ? 2 : 1) * L1_RING * TILE_PIXELS;
+  static bool configured = false;
+  cudaError_t e = configure_smem(raster_forward_kernel<MODE, DIST>, bytes, ring, 4, configured);
+  if (e != cudaSuccess) return e;
+  raster_forward_kernel<MODE, DIST><<<n_tiles, TILE_PIXELS, bytes, s>>>(a);
+  return cudaGetLastError();
+}
+
 template <int MODE>
 cudaError_t fwd_dispatch(const RasterFwdArgs& a, int n_tiles, cudaStream_t s) {
   count_launches(1);
   switch (a.st.distortions & 3) {
-    case 0: raster_forward_kernel<MODE, 0><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
-    case 1: raster_forward_kernel<MODE, 1><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
-    case 2: raster_forward_kernel<MODE, 2><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
-    default: raster_forward_kernel<MODE, 3><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
+    case 0: return fwd_launch<MODE, 0>(a, n_tiles, s);
+    case 1: return fwd_launch<MODE, 1>(a, n_tiles, s);
+    case 2: return fwd_launch<MODE, 2>(a, n_tiles, s);
+    default: return fwd_launch<MODE, 3>(a, n_tiles, s);
   }
+}
+
+template <int MODE, int DIST>
+cudaError_t bwd_launch(const RasterBwdArgs& a, int n_tiles, cudaStream_t s) {
+  constexpr size_t bytes =
+      sizeof(float4) * BWD_BATCH * REC4 + sizeof(float) * BWD_BATCH * AccWindow<MODE>::N + sizeof(int) * BWD_BATCH;
+  static bool configured = false;
+  cudaError_t e = configure_smem(raster_backward_kernel<MODE, DIST>, bytes, 16, 3, configured);
+  if (e != cudaSuccess) return e;
+  raster_backward_kernel<MODE, DIST><<<n_tiles, TILE_PIXELS, bytes, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -877,12 +929,11 @@ template <int MODE>
 cudaError_t bwd_dispatch(const RasterBwdArgs& a, int n_tiles, cudaStream_t s) {
   count_launches(1);
   switch (a.st.distortions & 3) {
-    case 0: raster_backward_kernel<MODE, 0><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
-    case 1: raster_backward_kernel<MODE, 1><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
-    case 2: raster_backward_kernel<MODE, 2><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
-    default: raster_backward_kernel<MODE, 3><<<n_tiles, TILE_PIXELS, 0, s>>>(a); break;
+    case 0: return bwd_launch<MODE, 0>(a, n_tiles, s);
+    case 1: return bwd_launch<MODE, 1>(a, n_tiles, s);
+    case 2: return bwd_launch<MODE, 2>(a, n_tiles, s);
+    default: return bwd_launch<MODE, 3>(a, n_tiles, s);
   }
-  return cudaGetLastError();
 }
 
 }  // namespace
