@@ -137,6 +137,13 @@ def algorithmic_flops(mode, n_pairs_fwd):
 POSES = 8  # orbit poses of the single-view workloads, cycled step by step
 
 
+def linear_loss(images, ups):
+    """sum over channels of <image, upstream>: one dot-product kernel per channel (and
+    one scaling kernel per channel in the backward), the fixed seeded stand-in for a
+    training loss whose adjoint of every image is its upstream tensor."""
+    return sum(torch.vdot(images[ch].reshape(-1), ups[ch].reshape(-1)) for ch in CHANNELS)
+
+
 def workload_label(args, n, width, height, views):
     return (f"{args.workload}: {n} Gaussians, {width}x{height}, mode {args.mode}, distortions {args.distortions}, "
             f"fwd+bwd, {views} view(s) per GPU per step")
@@ -199,7 +206,7 @@ class RenderJob:
             view = scenes.activated(self.p)
             out = rasterizer.rasterize(view.means, view.quats, view.scales, view.opacities, view.sh, 3, c,
                                        self.settings)
-            loss = sum((out[ch] * self.ups[ch]).sum() for ch in CHANNELS)
+            loss = linear_loss(out, self.ups)
             loss.backward()
         self.reducer()
         self.last = out
@@ -244,14 +251,43 @@ def time_steps(job, steps, warmup, distinct=False):
         dist.barrier()
     torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    from splatforge_b200 import rasterizer
+
+    import gc
+
+    stats0 = torch.cuda.memory_stats()
+    reruns0 = rasterizer.COUNTERS["l1_reruns"]
+    host = []
+    gc_ms = [0.0]
+    gc_t = [0.0]
+
+    def gc_cb(phase, info):
+        if phase == "start":
+            gc_t[0] = time.perf_counter()
+        else:
+            gc_ms[0] += 1e3 * (time.perf_counter() - gc_t[0])
+
+    gc.callbacks.append(gc_cb)
     ev[0].record()
     for s in range(steps):
+        h0 = time.perf_counter()
         job.step(s, distinct)
         ev[s + 1].record()
+        host.append(1e3 * (time.perf_counter() - h0))
     torch.cuda.synchronize()
+    gc.callbacks.remove(gc_cb)
     if job.world > 1:
         dist.barrier()
+    stats1 = torch.cuda.memory_stats()
     per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
+    # host-side launch time per step and the allocator's device allocations in the timed
+    # steps (a step whose device time exceeds its peers' with host time to match was held
+    # up on the host)
+    job.diag = {"host_ms": [round(x, 2) for x in host],
+                "device_allocs": stats1.get("num_device_alloc", 0) - stats0.get("num_device_alloc", 0),
+                "alloc_retries": stats1.get("num_alloc_retries", 0) - stats0.get("num_alloc_retries", 0),
+                "device_frees": stats1.get("num_device_free", 0) - stats0.get("num_device_free", 0),
+                "l1_reruns": rasterizer.COUNTERS["l1_reruns"] - reruns0, "gc_ms": round(gc_ms[0], 2)}
     return ev[0].elapsed_time(ev[-1]) / steps, per
 
 
@@ -347,6 +383,7 @@ def run_b200(args):
                       "raster_fwd_ms": [round(r[4], 3) for r in ranks], "raster_bwd_ms": [round(r[5], 3) for r in ranks],
                       "collective_share": round(_median([(r[1] + r[2] + r[3]) / r[0] for r in ranks if r[0]]) or 0.0, 4)},
             "distinct_poses": distinct,
+            "steps_this_rank": {"step_ms": [round(x, 2) for x in per_step], **job.diag},
             "gpu_launches": int(launches),
             "clocks": clk, "e2e": e2e, "roofline": roof,
         }
@@ -408,7 +445,7 @@ def e2e_render(job, args, dev, rank, world, B200Renderer, distributed, scenes):
             for c in job.cams(k):
                 v = scenes.activated(sp)
                 o = renderer.render(v, c, distortions=args.distortions)
-                loss = sum((getattr(o, ch) * job.ups[ch]).sum() for ch in CHANNELS)
+                loss = linear_loss({ch: getattr(o, ch) for ch in CHANNELS}, job.ups)
                 loss.backward()
                 total = total + loss.detach()
             reducers[slot]()
@@ -451,7 +488,8 @@ def secondary(args, dev, rank, world):
         "workload": f"surfaces3m_views64: {job.n} Gaussians, {job.W}x{job.H}, mode gof, distortions l1 "
                     f"(the training profile), fwd+bwd, {job.per} views per GPU per step, {views} per step",
         "poses": f"rank r renders poses 8(r + sN) .. +7 of the {len(job.poses)} (mod {len(job.poses)}) at step s",
-        "warmup_steps": warm, "step_ms_this_rank": [round(x, 2) for x in per_step],
+        "warmup_steps": warm, "step_ms_this_rank": [round(x, 2) for x in per_step], "diag_this_rank": job.diag,
+        "value_median_step": round(views / (_median(per_step) * 1e-3), 3),
         "step_ms_median": [round(r[0], 3) for r in ranks], "allreduce_ms": [round(r[2], 3) for r in ranks],
         "pack_unpack_ms": [round(r[1] + r[3], 3) for r in ranks]}
     del job

@@ -567,22 +567,17 @@ __device__ __forceinline__ bool l1_sort_pixel_packed(float* col_d, float* col_w,
 }
 
 // CLASS 0 resolves pixels with at most 256 samples (register sorts), CLASS 1 those
-// with 257..512 (16 per lane), CLASS 2 longer runs (shared-memory radix sort); each
-// launch skips the pixels of the other classes, so the register budget of the rare
-// long runs does not limit the occupancy of the common case.
+// with 257..512 (16 per lane); each launch skips the pixels of the other classes, so the
+// register budget of the rarer long runs does not limit the occupancy of the common case.
+// Longer runs go to l1_resolve_long_kernel.
 template <int CLASS>
 __global__ void __launch_bounds__(128) l1_resolve_kernel(
     sf_camera cam, float* state, float* l1s, int64_t slots, const int64_t* off, int cap, int smem_k,
     float* out_l1) {
-  extern __shared__ uint32_t s_l1[];
+  (void)smem_k;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int warps = blockDim.x >> 5;
-  uint32_t* k0 = s_l1 + (size_t)wid * (5 * smem_k + 256);
-  uint32_t* v0 = k0 + smem_k;
-  uint32_t* k1 = v0 + smem_k;
-  uint32_t* v1 = k1 + smem_k;
-  float* ws = reinterpret_cast<float*>(v1 + smem_k);
-  uint32_t* hist = reinterpret_cast<uint32_t*>(ws + smem_k);
+
   const int64_t npix = (int64_t)cam.width * cam.height;
   const int tiles_x = (cam.width + TILE - 1) / TILE;
   float* col_d = l1s;
@@ -625,56 +620,125 @@ __global__ void __launch_bounds__(128) l1_resolve_kernel(
     } else if (CLASS == 1) {
       if (!l1_sort_pixel_packed<16>(col_d, col_w, base, n, lane, vec, s_w, s_o, raw))
         raw = l1_sort_pixel<16>(col_d, col_w, base, n, lane);
-    } else {
-      // long runs: stable warp radix sort staged in shared memory
-      float Wt = 0.f, Dt = 0.f;
-      if (n > smem_k) n = smem_k;  // the launcher sizes smem_k >= the largest count
-      for (int k = lane; k < n; k += 32) {
-        const float d = col_d[base + k], w = col_w[base + k];
-        k0[k] = __float_as_uint(d);
-        v0[k] = (uint32_t)k;
-        ws[k] = w;
-        Wt += w; Dt += w * d;
-      }
-      Wt = warp_sum(Wt); Dt = warp_sum(Dt);
-      __syncwarp();
-      uint32_t *ks, *vs;
-      warp_radix_sort_u32(k0, v0, k1, v1, hist, n, lane, &ks, &vs);
-      float* aw = reinterpret_cast<float*>(ks == k0 ? k1 : k0);
-      float* ad = reinterpret_cast<float*>(vs == v0 ? v1 : v0);
-      float carry_w = 0.f, carry_wd = 0.f;
-      for (int c = 0; c < n; c += 32) {
-        const int r = c + lane;
-        float d = 0.f, w = 0.f;
-        uint32_t k = 0;
-        if (r < n) { k = vs[r]; d = __uint_as_float(ks[r]); w = ws[k]; }
-        float sw = w, swd = w * d;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float a1 = __shfl_up_sync(FULL, sw, o), a2 = __shfl_up_sync(FULL, swd, o);
-          if (lane >= o) { sw += a1; swd += a2; }
-        }
-        const float pw = carry_w + sw - w, pwd = carry_wd + swd - w * d;
-        carry_w += __shfl_sync(FULL, sw, 31);
-        carry_wd += __shfl_sync(FULL, swd, 31);
-        if (r < n) {
-          raw += 2.f * w * (d * pw - pwd);
-          aw[k] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
-          ad[k] = 2.f * w * (2.f * pw + w - Wt);
-        }
-      }
-      __syncwarp();
-      for (int k = lane; k < n; k += 32) {
-        col_d[base + k] = aw[k];
-        col_w[base + k] = ad[k];
-      }
-      __syncwarp();
     }
     raw = warp_sum(raw);
     if (lane == 0) {
       st[PS_L1] = raw;
       out_l1[pix] = fmaxr(raw, 0.f);
     }
+  }
+}
+
+// Runs longer than 512 samples (a camera close to a dense surface): one CTA of 256
+// threads per pixel.  The pixel's exact 64-bit (depth bits, index) keys are sorted by a
+// bitonic network in shared memory, padded to the next power of two of this pixel's
+// count (at least 1024); each thread then scans a contiguous slice of the sorted
+// samples, a block scan of the slices' totals gives every slice its prefix, and the
+// two factors are written back by compositing index.
+constexpr int LONG_THREADS = 256;
+
+__global__ void __launch_bounds__(LONG_THREADS) l1_resolve_long_kernel(
+    sf_camera cam, float* state, float* l1s, int64_t slots, const int64_t* off, int cap, int smem_k,
+    float* out_l1) {
+  extern __shared__ unsigned long long s_long[];  // smem_k keys, then smem_k weights
+  float* s_w = reinterpret_cast<float*>(s_long + smem_k);
+  __shared__ float s_tot[2][LONG_THREADS / 32];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int64_t npix = (int64_t)cam.width * cam.height;
+  const int tiles_x = (cam.width + TILE - 1) / TILE;
+  float* col_d = l1s;
+  float* col_w = l1s + slots;
+  for (int64_t pix = blockIdx.x; pix < npix; pix += gridDim.x) {
+    float* st = state + pix * SF_PIXEL_STATE_FLOATS;
+    int n = f2i(st[PS_COUNT]);  // the same for every thread: the loop stays uniform
+    const int u = (int)(pix % cam.width), v = (int)(pix / cam.width);
+    const int tile = (v / TILE) * tiles_x + (u / TILE);
+    const int ptid = (v % TILE) * TILE + (u % TILE);
+    const int64_t base = l1_base(tile, ptid, cap, off, pix);
+    const int room = off ? (int)(off[pix + 1] - off[pix]) : cap;
+    if (n > room) n = room;
+    if (n <= 512) continue;
+    if (n > smem_k) n = smem_k;  // the launcher sizes smem_k >= the largest count
+    int nn = 1024;
+    while (nn < n) nn <<= 1;
+    float Wt = 0.f, Dt = 0.f;
+    for (int k = tid; k < nn; k += LONG_THREADS) {
+      if (k < n) {
+        const float d = col_d[base + k], w = col_w[base + k];
+        s_long[k] = ((unsigned long long)__float_as_uint(d) << 32) | (unsigned)k;
+        s_w[k] = w;
+        Wt += w; Dt += w * d;
+      } else {
+        s_long[k] = ~0ull;  // padding sorts last
+      }
+    }
+    Wt = warp_sum(Wt); Dt = warp_sum(Dt);
+    if (lane == 0) { s_tot[0][wid] = Wt; s_tot[1][wid] = Dt; }
+    __syncthreads();
+    Wt = 0.f; Dt = 0.f;
+#pragma unroll
+    for (int q = 0; q < LONG_THREADS / 32; ++q) { Wt += s_tot[0][q]; Dt += s_tot[1][q]; }
+    for (int size = 2; size <= nn; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int q = tid; q < nn / 2; q += LONG_THREADS) {
+          const int i = ((q & ~(stride - 1)) << 1) | (q & (stride - 1));
+          const int j = i + stride;
+          const unsigned long long a = s_long[i], b = s_long[j];
+          if ((a > b) == ((i & size) == 0)) { s_long[i] = b; s_long[j] = a; }
+        }
+        __syncthreads();
+      }
+    }
+    // each thread's contiguous slice of E sorted samples
+    const int E = nn / LONG_THREADS;
+    const int r0 = tid * E;
+    float tw = 0.f, twd = 0.f;
+    for (int e = 0; e < E; ++e) {
+      const int r = r0 + e;
+      if (r < n) {
+        const unsigned long long key = s_long[r];
+        const float d = __uint_as_float((uint32_t)(key >> 32)), w = s_w[(uint32_t)key];
+        tw += w; twd += w * d;
+      }
+    }
+    // exclusive block scan of the slice totals
+    float iw = tw, iwd = twd;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float a1 = __shfl_up_sync(FULL, iw, o), a2 = __shfl_up_sync(FULL, iwd, o);
+      if (lane >= o) { iw += a1; iwd += a2; }
+    }
+    __syncthreads();  // every thread has read the block totals above
+    if (lane == 31) { s_tot[0][wid] = iw; s_tot[1][wid] = iwd; }
+    __syncthreads();
+    float pw = iw - tw, pwd = iwd - twd;
+    for (int q = 0; q < wid; ++q) { pw += s_tot[0][q]; pwd += s_tot[1][q]; }
+    float raw = 0.f;
+    for (int e = 0; e < E; ++e) {
+      const int r = r0 + e;
+      if (r < n) {
+        const unsigned long long key = s_long[r];
+        const uint32_t k = (uint32_t)key;
+        const float d = __uint_as_float((uint32_t)(key >> 32)), w = s_w[k];
+        raw += 2.f * w * (d * pw - pwd);
+        col_d[base + k] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
+        col_w[base + k] = 2.f * w * (2.f * pw + w - Wt);
+        pw += w;
+        pwd += w * d;
+      }
+    }
+    raw = warp_sum(raw);
+    __syncthreads();  // every thread has read the scan totals
+    if (lane == 0) s_tot[0][wid] = raw;
+    __syncthreads();
+    if (tid == 0) {
+      float total = 0.f;
+#pragma unroll
+      for (int q = 0; q < LONG_THREADS / 32; ++q) total += s_tot[0][q];
+      st[PS_L1] = total;
+      out_l1[pix] = fmaxr(total, 0.f);
+    }
+    __syncthreads();  // shared memory is free for the next pixel
   }
 }
 
@@ -956,7 +1020,7 @@ cudaError_t launch_raster_backward(const RasterBwdArgs& a, int n_tiles, cudaStre
   }
 }
 
-size_t l1_resolve_smem_per_warp(int smem_k) { return ((size_t)5 * smem_k + 256) * sizeof(uint32_t); }
+size_t l1_resolve_smem_per_warp(int smem_k) { return (size_t)smem_k * (sizeof(unsigned long long) + sizeof(float)); }
 
 cudaError_t launch_l1_resolve(const sf_camera& cam, const sf_settings& st, float* state,
                               float* l1s, int64_t slots, const int64_t* off, int cap, int max_samples,
@@ -975,18 +1039,19 @@ cudaError_t launch_l1_resolve(const sf_camera& cam, const sf_settings& st, float
                                                                                      cap, 0, out_l1);
   e = cudaGetLastError();
   if (e != cudaSuccess || max_samples <= 512) return e;
-  const int smem_k = ((max_samples + 31) / 32) * 32;
-  const size_t per_warp = l1_resolve_smem_per_warp(smem_k);
-  const size_t budget = 200 * 1024;
-  if (per_warp > budget) return cudaErrorInvalidValue;
-  const int warps = (int)min((size_t)4, budget / per_warp);
-  const size_t smem = per_warp * warps;
-  e = cudaFuncSetAttribute(l1_resolve_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int smem_k = 1024;  // a power of two >= the largest count (the largest bitonic network)
+  while (smem_k < max_samples) smem_k <<= 1;
+  const size_t smem = l1_resolve_smem_per_warp(smem_k);  // one pixel per CTA
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  e = cudaFuncSetAttribute(l1_resolve_long_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(l1_resolve_long_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e != cudaSuccess) return e;
-  int64_t b2 = (npix + warps - 1) / warps;
-  if (b2 > 148 * 8) b2 = 148 * 8;
+  const int per_sm = (int)min((size_t)8, (size_t)(220 * 1024) / (smem + 1024));
+  const int64_t b2 = min(npix, (int64_t)148 * (per_sm > 0 ? per_sm : 1));
   count_launches(1);
-  l1_resolve_kernel<2><<<(unsigned)b2, warps * 32, smem, s>>>(cam, state, l1s, slots, off, cap, smem_k, out_l1);
+  l1_resolve_long_kernel<<<(unsigned)b2, LONG_THREADS, smem, s>>>(cam, state, l1s, slots, off, cap, smem_k,
+                                                                  out_l1);
   return cudaGetLastError();
 }
 

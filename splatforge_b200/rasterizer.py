@@ -38,6 +38,8 @@ AMBISUR_DISTORTION_FLOOR = 1e-30
 PROFILE = None
 # largest per-pixel L1 sample count seen, per image size (capacity of the next render)
 _L1_SEEN = {}
+# renders whose L1 samples overflowed the fixed capacity and were rerun with exact offsets
+COUNTERS = {"l1_reruns": 0}
 
 
 def _ptr(t):
@@ -324,12 +326,17 @@ class _Raster(torch.autograd.Function):
             plan.stats["l1_max_samples"] = most
             plan.stats["l1_capacity"] = cap
             if plan.l1_capacity is None:
-                # the largest count seen for this size, with headroom (never shrinks, so
-                # a sequence of poses settles on one capacity)
-                _L1_SEEN[key] = max(_L1_SEEN.get(key, 0), int(most * 1.2 + 31) // 32 * 32)
+                # capacity of the next render of this size: at least 1.2x the largest count
+                # seen; it never shrinks and grows by at least half each time it must, so a
+                # sequence of poses settles on one capacity (one buffer size) quickly
+                want = int(most * 1.2 + 31) // 32 * 32
+                current = _L1_SEEN.get(key, 0)
+                if want > current:
+                    _L1_SEEN[key] = max(want, (current * 3 // 2 + 63) // 64 * 64)
             if most > cap:
                 # capacity exceeded somewhere: exact per-pixel (CSR) storage and a rerun
                 plan.stats["l1_rerun"] = True
+                COUNTERS["l1_reruns"] += 1
                 ws_bytes = (H * W + 2048) * 8 + H * W * 4 + 4096
                 ws = torch.empty((ws_bytes,), device=dev, dtype=torch.uint8)
                 l1_off = torch.empty((H * W + 1,), device=dev, dtype=torch.int64)
