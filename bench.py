@@ -496,6 +496,19 @@ def secondary(args, dev, rank, world):
         "pack_unpack_ms": [round(r[1] + r[3], 3) for r in ranks]}
     del job
     torch.cuda.empty_cache()
+    # the C3 frame in the other two modes (the headline is GOF), every output channel
+    for mode in ("radegs", "ambisur"):
+        job = RenderJob(DEFAULT_WORKLOAD, dev, rank, world, mode, "both")
+        ms_rank, per_step = time_steps(job, POSES, 3)
+        ms = _max_over_ranks(ms_rank, dev, world)
+        out[f"c3_{mode}"] = {
+            "metric": "fwd+bwd rendered Mpix/s", "unit": "Mpix/s",
+            "value": round(job.pixels_per_step() / (ms * 1e-3) / 1e6, 3), "ms_per_step": round(ms, 3),
+            "workload": workload_label(argparse.Namespace(workload=DEFAULT_WORKLOAD, mode=mode, distortions="both"),
+                                       job.n, job.W, job.H, 1),
+            "steps": POSES, "warmup": 3, "n_isect_last": int(job.last["n_isect"])}
+        del job
+        torch.cuda.empty_cache()
     field = field_measure(dev, rank, world, steps=2, warmup=1, e2e=False)
     out["opacity_field"] = field
     torch.cuda.empty_cache()

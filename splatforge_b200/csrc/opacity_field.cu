@@ -274,17 +274,62 @@ __device__ __forceinline__ float field_contribution(const float* g, float ox, fl
   return fminf(fmaxf(g[9] * expf(-0.5f * fmaxf(e, 0.f)), 0.f), 0.999f);
 }
 
-// Per view, every query's cube-map cell (a query at the origin has no direction and
-// gets field 0 for this view right here) as a sort key with the query's index.
+// Query order inside a cell: a query's sort key carries, below its cube-map cell, its
+// position on a QSUB x QSUB grid inside the cell and its quantised log distance, so that
+// the 32 queries of a warp look in nearly the same direction from nearly the same
+// distance: they hit the same candidate balls and stop near the same list position,
+// and fewer lanes idle beside the ones that evaluate a contribution.
+#ifndef SF_FIELD_QUERY_ORDER
+#define SF_FIELD_QUERY_ORDER 1
+#endif
+// Low key bits (sub-cell bits per axis, distance bits) that fit below `cell_bits`.
+inline void query_order_bits(int cell_bits, int& sub_bits, int& dist_bits) {
+  sub_bits = dist_bits = 0;
+  if (!SF_FIELD_QUERY_ORDER) return;
+  if (cell_bits + 4 <= 32) sub_bits = 2;
+  if (cell_bits + 12 <= 32) dist_bits = 8;
+}
+
+// The query's cube-map cell (6 F^2 for a query at the origin) in the high bits, the
+// in-cell order bits below.
+__device__ __forceinline__ uint32_t query_key(float dx, float dy, float dz, int F, int sub_bits, int dist_bits) {
+  const int low = 2 * sub_bits + dist_bits;
+  const float d2 = dx * dx + dy * dy + dz * dz;
+  if (!(d2 > 0.f)) return (uint32_t)(6 * F * F) << low;
+  const int Ff = F << sub_bits;
+  const int fine = cube_cell(dx, dy, dz, Ff);  // (face * Ff + iy) * Ff + ix at the finer grid
+  const int ix = fine % Ff, rest = fine / Ff, iy = rest % Ff, face = rest / Ff;
+  const int cell = (face * F + (iy >> sub_bits)) * F + (ix >> sub_bits);
+  const int mask = (1 << sub_bits) - 1;
+  const uint32_t sub = (uint32_t)(((iy & mask) << sub_bits) | (ix & mask));
+  uint32_t dq = 0;
+  if (dist_bits > 0) {
+    const float l = 0.5f * __log2f(d2) * 16.f + 128.f;  // 16 steps per octave of distance
+    dq = (uint32_t)fminf(fmaxf(l, 0.f), (float)((1 << dist_bits) - 1));
+  }
+  return ((uint32_t)cell << low) | (sub << dist_bits) | dq;
+}
+
+// Per view, every query's sort key (query_key) with the query's index; a query at the
+// origin has no direction and gets field 0 for this view right here.
 __global__ void cfield_qcell_kernel(const float* pts, int64_t np, float ox, float oy, float oz, int F,
-                                    uint32_t* qkey, int32_t* qidx, uint32_t* out) {
+                                    int sub_bits, int dist_bits, uint32_t* qkey, int32_t* qidx, uint32_t* out) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= np) return;
   const float dx = pts[i * 3] - ox, dy = pts[i * 3 + 1] - oy, dz = pts[i * 3 + 2] - oz;
   const bool at_origin = !(dx * dx + dy * dy + dz * dz > 0.f);
-  qkey[i] = at_origin ? (uint32_t)(6 * F * F) : (uint32_t)cube_cell(dx, dy, dz, F);
+  qkey[i] = query_key(dx, dy, dz, F, sub_bits, dist_bits);
   qidx[i] = (int32_t)i;
   if (at_origin) atomicMin(out + i, 0u);
+}
+
+// [begin, end) of every cell in keys sorted by query_key (the cell is key >> shift).
+__global__ void cfield_cell_ranges_kernel(const uint32_t* keys, int64_t n, int shift, int2* ranges) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t c = keys[i] >> shift;
+  if (i == 0 || (keys[i - 1] >> shift) != c) ranges[c].x = (int)i;
+  if (i == n - 1 || (keys[i + 1] >> shift) != c) ranges[c].y = (int)(i + 1);
 }
 
 constexpr int CF_THREADS = 256;
@@ -570,6 +615,10 @@ cudaError_t launch_opacity_field_culled(const float* pts, int64_t np, const floa
   void* cscan_ws = take(cscan_bytes);
   int qbits = 1;
   while ((1LL << qbits) < 6LL * F * F + 1) ++qbits;
+  int sub_bits, dist_bits;
+  query_order_bits(qbits, sub_bits, dist_bits);
+  const int qlow = 2 * sub_bits + dist_bits;
+  qbits += qlow;
 
   const unsigned gb = (unsigned)((ng + 255) / 256), qb = (unsigned)((np + 255) / 256);
   count_launches(1);
@@ -626,10 +675,15 @@ cudaError_t launch_opacity_field_culled(const float* pts, int64_t np, const floa
     if (e == cudaSuccess) e = key_ranges(keys, m, 6LL * F * F, ranges, s);
     if (e != cudaSuccess) break;
     count_launches(1);
-    cfield_qcell_kernel<<<qb, 256, 0, s>>>(pts, np, ox, oy, oz, F, qkey, qidx, o);
+    cfield_qcell_kernel<<<qb, 256, 0, s>>>(pts, np, ox, oy, oz, F, sub_bits, dist_bits, qkey, qidx, o);
     e = cudaGetLastError();
     if (e == cudaSuccess) e = sort_pairs(qkey, qidx, np, qbits, qsort_ws, qsort_bytes, s);
-    if (e == cudaSuccess) e = key_ranges(qkey, np, 6LL * F * F + 1, qranges, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(qranges, 0, sizeof(int2) * (size_t)(6LL * F * F + 1), s);
+    if (e == cudaSuccess && np > 0) {
+      count_launches(1);
+      cfield_cell_ranges_kernel<<<qb, 256, 0, s>>>(qkey, np, qlow, reinterpret_cast<int2*>(qranges));
+      e = cudaGetLastError();
+    }
     if (e != cudaSuccess) break;
     count_launches(1);
     cfield_chunks_kernel<<<(unsigned)((ncells + 255) / 256), 256, 0, s>>>(reinterpret_cast<const int2*>(qranges),

@@ -23,26 +23,40 @@ constexpr int PB = 128;  // Gaussians per CTA
 // is 16-byte aligned, scalar loads otherwise.
 __device__ __forceinline__ int row_stride(int width) { return width + ((width & 1) ^ 1); }
 
+// (row, column) of flat index k of a [rows, width] slab, advanced by a fixed step without
+// a division per element: one division at the start, then carries.
+struct RowCursor {
+  int r, c, dr, dc, width;
+  __device__ __forceinline__ RowCursor(int k, int step, int w)
+      : r(k / w), c(k - (k / w) * w), dr(step / w), dc(step - (step / w) * w), width(w) {}
+  __device__ __forceinline__ void advance() {
+    r += dr;
+    c += dc;
+    if (c >= width) { c -= width; ++r; }
+  }
+};
+
 __device__ __forceinline__ void stage_rows(float* dst, const float* src, int64_t first, int rows, int width,
                                            int stride) {
   const int count = rows * width;
   const float* base = src + first * width;
   if ((((uintptr_t)base) & 15) == 0 && (count & 3) == 0) {
     const float4* s4 = reinterpret_cast<const float4*>(base);
-    for (int k = threadIdx.x; k < count / 4; k += blockDim.x) {
+    RowCursor at(4 * (int)threadIdx.x, 4 * (int)blockDim.x, width);
+    for (int k = threadIdx.x; k < count / 4; k += blockDim.x, at.advance()) {
       const float4 v = __ldg(s4 + k);
       const float e[4] = {v.x, v.y, v.z, v.w};
+      // the four elements may cross into the next row
+      int r = at.r, c = at.c;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int idx = 4 * k + c, r = idx / width;
-        dst[r * stride + (idx - r * width)] = e[c];
+      for (int q = 0; q < 4; ++q) {
+        dst[r * stride + c] = e[q];
+        if (++c == width) { c = 0; ++r; }
       }
     }
   } else {
-    for (int k = threadIdx.x; k < count; k += blockDim.x) {
-      const int r = k / width;
-      dst[r * stride + (k - r * width)] = __ldg(base + k);
-    }
+    RowCursor at(threadIdx.x, blockDim.x, width);
+    for (int k = threadIdx.x; k < count; k += blockDim.x, at.advance()) dst[at.r * stride + at.c] = __ldg(base + k);
   }
 }
 
@@ -172,12 +186,10 @@ __global__ void __launch_bounds__(PB) project_backward_kernel(
   __syncthreads();
   if (g_sh) {
     // coalesced write-back of the staged coefficient adjoints
-    const int64_t count = (int64_t)rows * K * 3;
+    const int count = rows * K * 3;
     float* base = g_sh + first * K * 3;
-    for (int64_t k = threadIdx.x; k < count; k += blockDim.x) {
-      const int r = (int)(k / (K * 3));
-      base[k] = s_sh[r * stride + (int)(k - (int64_t)r * K * 3)];
-    }
+    RowCursor at(threadIdx.x, blockDim.x, K * 3);
+    for (int k = threadIdx.x; k < count; k += blockDim.x, at.advance()) base[k] = s_sh[at.r * stride + at.c];
   }
 }
 

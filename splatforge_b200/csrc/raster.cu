@@ -29,6 +29,7 @@ constexpr int REC4 = SF_RECORD_FLOATS / 4;  // float4 per record
 #ifndef SF_BWD_BATCH
 #define SF_BWD_BATCH 256
 #endif
+
 constexpr int FWD_BATCH = SF_FWD_BATCH;
 constexpr int BWD_BATCH = SF_BWD_BATCH;
 static_assert(FWD_BATCH % 32 == 0 && BWD_BATCH % 32 == 0, "batches are whole culling groups");
