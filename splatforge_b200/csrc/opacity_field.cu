@@ -287,27 +287,35 @@ inline void query_order_bits(int cell_bits, int& sub_bits, int& dist_bits) {
   sub_bits = dist_bits = 0;
   if (!SF_FIELD_QUERY_ORDER) return;
   if (cell_bits + 4 <= 32) sub_bits = 2;
-  if (cell_bits + 12 <= 32) dist_bits = 8;
+  const int room = 32 - cell_bits - 2 * sub_bits;
+  dist_bits = room < 0 ? 0 : (room > 8 ? 8 : room);
 }
 
-// The query's cube-map cell (6 F^2 for a query at the origin) in the high bits, the
-// in-cell order bits below.
-__device__ __forceinline__ uint32_t query_key(float dx, float dy, float dz, int F, int sub_bits, int dist_bits) {
-  const int low = 2 * sub_bits + dist_bits;
+// A query's cube-map cell (6 F^2 for a query at the origin) and its in-cell order bits.
+__device__ __forceinline__ void query_key_parts(float dx, float dy, float dz, int F, int sub_bits, int dist_bits,
+                                                uint32_t& cell_out, uint32_t& low_out) {
   const float d2 = dx * dx + dy * dy + dz * dz;
-  if (!(d2 > 0.f)) return (uint32_t)(6 * F * F) << low;
+  if (!(d2 > 0.f)) { cell_out = (uint32_t)(6 * F * F); low_out = 0; return; }
   const int Ff = F << sub_bits;
   const int fine = cube_cell(dx, dy, dz, Ff);  // (face * Ff + iy) * Ff + ix at the finer grid
   const int ix = fine % Ff, rest = fine / Ff, iy = rest % Ff, face = rest / Ff;
-  const int cell = (face * F + (iy >> sub_bits)) * F + (ix >> sub_bits);
+  cell_out = (uint32_t)((face * F + (iy >> sub_bits)) * F + (ix >> sub_bits));
   const int mask = (1 << sub_bits) - 1;
   const uint32_t sub = (uint32_t)(((iy & mask) << sub_bits) | (ix & mask));
   uint32_t dq = 0;
   if (dist_bits > 0) {
-    const float l = 0.5f * __log2f(d2) * 16.f + 128.f;  // 16 steps per octave of distance
+    // 16 steps per octave of distance, centred so that distances 1/256 .. 256 stay apart
+    const float l = 0.5f * __log2f(d2) * 16.f + (float)(1 << (dist_bits - 1));
     dq = (uint32_t)fminf(fmaxf(l, 0.f), (float)((1 << dist_bits) - 1));
   }
-  return ((uint32_t)cell << low) | (sub << dist_bits) | dq;
+  low_out = (sub << dist_bits) | dq;
+}
+
+// The query's cell in the high bits, the in-cell order bits below.
+__device__ __forceinline__ uint32_t query_key(float dx, float dy, float dz, int F, int sub_bits, int dist_bits) {
+  uint32_t cell, low;
+  query_key_parts(dx, dy, dz, F, sub_bits, dist_bits, cell, low);
+  return (cell << (2 * sub_bits + dist_bits)) | low;
 }
 
 // Per view, every query's sort key (query_key) with the query's index; a query at the
@@ -456,7 +464,7 @@ __global__ void __launch_bounds__(CF_THREADS) cfield_cell_kernel(
 // query i of view v: key v * (ncells + 1) + cell, ncells for a query at the origin
 // (whose field is 0 for that view, set here)
 __global__ void cfield_plan_qcell_kernel(const float* pts, int64_t np, const float* origins, int nc, int F,
-                                         uint32_t* qkey, int32_t* qidx, uint32_t* out) {
+                                         int sub_bits, int dist_bits, uint32_t* qkey, int32_t* qidx, uint32_t* out) {
   const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= np * nc) return;
   const int v = (int)(j / np);
@@ -465,7 +473,9 @@ __global__ void cfield_plan_qcell_kernel(const float* pts, int64_t np, const flo
               dz = pts[i * 3 + 2] - origins[v * 3 + 2];
   const bool at_origin = !(dx * dx + dy * dy + dz * dz > 0.f);
   const uint32_t cells = (uint32_t)(6 * F * F);
-  qkey[j] = (uint32_t)v * (cells + 1) + (at_origin ? cells : (uint32_t)cube_cell(dx, dy, dz, F));
+  uint32_t cell, low;
+  query_key_parts(dx, dy, dz, F, sub_bits, dist_bits, cell, low);
+  qkey[j] = (((uint32_t)v * (cells + 1) + cell) << (2 * sub_bits + dist_bits)) | low;
   qidx[j] = (int32_t)i;
   if (at_origin) atomicMin(out + i, 0u);
 }
@@ -879,11 +889,22 @@ cudaError_t field_plan_eval(const void* plan, int64_t ng, int nc, int F, int64_t
   const int64_t nkeys = (int64_t)nc * per_view;
   int qbits = 1;
   while ((1LL << qbits) < nkeys) ++qbits;
+  int sub_bits, dist_bits;
+  query_order_bits(qbits, sub_bits, dist_bits);
+  const int qlow = 2 * sub_bits + dist_bits;
+  qbits += qlow;
   count_launches(1);
-  cfield_plan_qcell_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(pts, np, origins, nc, F, Q.qkey, Q.qidx, o);
+  cfield_plan_qcell_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(pts, np, origins, nc, F, sub_bits, dist_bits,
+                                                                      Q.qkey, Q.qidx, o);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) e = sort_pairs(Q.qkey, Q.qidx, n, qbits, Q.sort_ws, Q.sort_bytes, s);
-  if (e == cudaSuccess) e = key_ranges(Q.qkey, n, nkeys, Q.qranges, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(Q.qranges, 0, sizeof(int2) * (size_t)nkeys, s);
+  if (e == cudaSuccess) {
+    count_launches(1);
+    cfield_cell_ranges_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(Q.qkey, n, qlow,
+                                                                         reinterpret_cast<int2*>(Q.qranges));
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) return e;
   const unsigned kb = (unsigned)((nkeys + 255) / 256);
   count_launches(1);
