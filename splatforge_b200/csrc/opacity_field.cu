@@ -275,18 +275,21 @@ __device__ __forceinline__ float field_contribution(const float* g, float ox, fl
 }
 
 // Query order inside a cell: a query's sort key carries, below its cube-map cell, its
-// position on a QSUB x QSUB grid inside the cell and its quantised log distance, so that
+// position on a 2^SUB x 2^SUB grid inside the cell and its quantised log distance, so that
 // the 32 queries of a warp look in nearly the same direction from nearly the same
 // distance: they hit the same candidate balls and stop near the same list position,
 // and fewer lanes idle beside the ones that evaluate a contribution.
 #ifndef SF_FIELD_QUERY_ORDER
 #define SF_FIELD_QUERY_ORDER 1
 #endif
+#ifndef SF_FIELD_SUB_BITS
+#define SF_FIELD_SUB_BITS 2  // SUB: sub-cell bits per axis
+#endif
 // Low key bits (sub-cell bits per axis, distance bits) that fit below `cell_bits`.
 inline void query_order_bits(int cell_bits, int& sub_bits, int& dist_bits) {
   sub_bits = dist_bits = 0;
   if (!SF_FIELD_QUERY_ORDER) return;
-  if (cell_bits + 4 <= 32) sub_bits = 2;
+  if (cell_bits + 2 * SF_FIELD_SUB_BITS <= 32) sub_bits = SF_FIELD_SUB_BITS;
   const int room = 32 - cell_bits - 2 * sub_bits;
   dist_bits = room < 0 ? 0 : (room > 8 ? 8 : room);
 }
@@ -340,7 +343,10 @@ __global__ void cfield_cell_ranges_kernel(const uint32_t* keys, int64_t n, int s
   if (i == n - 1 || (keys[i + 1] >> shift) != c) ranges[c].y = (int)(i + 1);
 }
 
-constexpr int CF_THREADS = 256;
+#ifndef SF_FIELD_CHUNK
+#define SF_FIELD_CHUNK 256
+#endif
+constexpr int CF_THREADS = SF_FIELD_CHUNK;  // queries per work item (one thread each)
 
 // One CTA per cube-map cell: the cell's queries (in chunks of CF_THREADS, one per
 // thread) walk the cell's front-to-back candidate list, staged CF_THREADS records at a
