@@ -127,7 +127,10 @@ cudaError_t exclusive_scan(const TI* in, int64_t n, TO* out, TO* partial, TO* gr
 // ------------------------------------------------------------------ radix sort
 constexpr int RS_THREADS = 256;
 constexpr int RS_WARPS = RS_THREADS / 32;
-constexpr int RS_ROUNDS = 8;                          // 32-key rounds per warp
+#ifndef SF_RS_ROUNDS
+#define SF_RS_ROUNDS 8
+#endif
+constexpr int RS_ROUNDS = SF_RS_ROUNDS;               // 32-key rounds per warp
 constexpr int RS_CHUNK = RS_THREADS * RS_ROUNDS;      // keys per CTA
 constexpr int RADIX = 256;
 
@@ -167,7 +170,7 @@ __global__ void __launch_bounds__(RS_THREADS) radix_upsweep_kernel(const uint32_
 // keep their input order), then the block's keys are regrouped by digit in shared
 // memory and written out from there, so consecutive threads store consecutive
 // addresses of one digit's run instead of 32 scattered runs per instruction.
-__global__ void __launch_bounds__(RS_THREADS, 4) radix_downsweep_kernel(
+__global__ void __launch_bounds__(RS_THREADS, RS_ROUNDS <= 8 ? 4 : 2) radix_downsweep_kernel(
     const uint32_t* keys_in, const int32_t* vals_in, int64_t n, int shift, int nb,
     const uint32_t* offsets, uint32_t* keys_out, int32_t* vals_out) {
   __shared__ uint32_t s_cnt[RS_WARPS][RADIX];

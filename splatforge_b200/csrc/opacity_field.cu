@@ -283,7 +283,7 @@ __device__ __forceinline__ float field_contribution(const float* g, float ox, fl
 #define SF_FIELD_QUERY_ORDER 1
 #endif
 #ifndef SF_FIELD_SUB_BITS
-#define SF_FIELD_SUB_BITS 2  // SUB: sub-cell bits per axis
+#define SF_FIELD_SUB_BITS 1  // SUB: sub-cell bits per axis
 #endif
 // Low key bits (sub-cell bits per axis, distance bits) that fit below `cell_bits`.
 inline void query_order_bits(int cell_bits, int& sub_bits, int& dist_bits) {
@@ -344,7 +344,7 @@ __global__ void cfield_cell_ranges_kernel(const uint32_t* keys, int64_t n, int s
 }
 
 #ifndef SF_FIELD_CHUNK
-#define SF_FIELD_CHUNK 256
+#define SF_FIELD_CHUNK 128
 #endif
 constexpr int CF_THREADS = SF_FIELD_CHUNK;  // queries per work item (one thread each)
 

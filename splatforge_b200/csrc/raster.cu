@@ -30,6 +30,11 @@ constexpr int REC4 = SF_RECORD_FLOATS / 4;  // float4 per record
 #define SF_BWD_BATCH 256
 #endif
 
+// resident CTAs per SM the forward is compiled for (register budget 65536 / (256 x this))
+#ifndef SF_FWD_MIN_CTAS
+#define SF_FWD_MIN_CTAS 4
+#endif
+
 constexpr int FWD_BATCH = SF_FWD_BATCH;
 constexpr int BWD_BATCH = SF_BWD_BATCH;
 static_assert(FWD_BATCH % 32 == 0 && BWD_BATCH % 32 == 0, "batches are whole culling groups");
@@ -112,7 +117,7 @@ __device__ __forceinline__ void l1_flush(float* l1s, int64_t slots, int64_t at, 
 }
 
 template <int MODE, int DIST>
-__global__ void __launch_bounds__(TILE_PIXELS, 4) raster_forward_kernel(const RasterFwdArgs a) {
+__global__ void __launch_bounds__(TILE_PIXELS, SF_FWD_MIN_CTAS) raster_forward_kernel(const RasterFwdArgs a) {
   extern __shared__ float4 s_dyn[];  // the batch's records: FWD_BATCH * REC4 float4
   float4* s_rec = s_dyn;
   __shared__ float s_ring[(DIST & SF_DIST_L1) ? 2 : 1][L1_RING][TILE_PIXELS];
@@ -590,42 +595,61 @@ __global__ void __launch_bounds__(128) l1_resolve_kernel(
   float* s_o = s_w + (CLASS == 2 ? 0 : NMAX);
   // 16-byte loads and stores need aligned columns (runs start on 8-sample boundaries)
   const bool vec = ((reinterpret_cast<uintptr_t>(l1s) | (uintptr_t)(slots * sizeof(float))) & 15) == 0;
-  const int64_t stride = (int64_t)gridDim.x * warps;
-  int64_t pix = (int64_t)blockIdx.x * warps + wid;
-  // the sample count of the warp's next pixel is loaded one pixel ahead
-  int n_next = pix < npix ? f2i(state[pix * SF_PIXEL_STATE_FLOATS + PS_COUNT]) : 0;
-  for (; pix < npix; pix += stride) {
-    float* st = state + pix * SF_PIXEL_STATE_FLOATS;
-    int n = n_next;
-    if (pix + stride < npix) n_next = f2i(state[(pix + stride) * SF_PIXEL_STATE_FLOATS + PS_COUNT]);
-    const int u = (int)(pix % cam.width), v = (int)(pix / cam.width);
-    const int tile = (v / TILE) * tiles_x + (u / TILE);
-    const int tid = (v % TILE) * TILE + (u % TILE);
-    const int64_t base = l1_base(tile, tid, cap, off, pix);
-    // never read past the pixel's run (a capacity overflow is rerun by the caller)
-    const int room = off ? (int)(off[pix + 1] - off[pix]) : cap;
-    if (n > room) n = room;
-    const int cls = n <= 256 ? 0 : (n <= 512 ? 1 : 2);
-    if (cls != CLASS) continue;
-    float raw = 0.f;
-    if (CLASS == 0) {
-      if (n <= 1) {
-        if (n == 1 && lane == 0) { col_d[base] = 0.f; col_w[base] = 0.f; }
-      } else if (n <= 128) {
-        if (!l1_sort_pixel_packed<4>(col_d, col_w, base, n, lane, vec, s_w, s_o, raw))
-          raw = l1_sort_pixel<4>(col_d, col_w, base, n, lane);
-      } else {
-        if (!l1_sort_pixel_packed<8>(col_d, col_w, base, n, lane, vec, s_w, s_o, raw))
-          raw = l1_sort_pixel<8>(col_d, col_w, base, n, lane);
+  // Pixels go to warps in groups of 32: lane l of group g reads the sample count and
+  // run start of pixel g + l G (G groups, so a group's pixels lie spread over the frame
+  // and a cluster of long runs spreads over many warps), a ballot picks the group's
+  // pixels of this class, and the warp resolves them one after another with their
+  // counts already in registers: one load latency per 32 pixels, where a launch that
+  // skips most pixels (the longer classes) would otherwise wait once per pixel.
+  const int64_t groups = (npix + 31) >> 5;
+  for (int64_t g = (int64_t)blockIdx.x * warps + wid; g < groups; g += (int64_t)gridDim.x * warps) {
+    const int64_t mine = g + lane * groups;
+    int my_n = 0;
+    int64_t my_base = 0;
+    bool here = false;
+    if (mine < npix) {
+      my_n = f2i(state[mine * SF_PIXEL_STATE_FLOATS + PS_COUNT]);
+      const int u = (int)(mine % cam.width), v = (int)(mine / cam.width);
+      const int tile = (v / TILE) * tiles_x + (u / TILE);
+      const int tid = (v % TILE) * TILE + (u % TILE);
+      my_base = l1_base(tile, tid, cap, off, mine);
+      // never read past the pixel's run (a capacity overflow is rerun by the caller)
+      const int room = off ? (int)(off[mine + 1] - off[mine]) : cap;
+      if (my_n > room) my_n = room;
+      here = (my_n <= 256 ? 0 : (my_n <= 512 ? 1 : 2)) == CLASS;
+      if (CLASS == 0 && here && my_n <= 1) {
+        // nothing to sort: the lane writes its own pixel's outputs
+        if (my_n == 1) { col_d[my_base] = 0.f; col_w[my_base] = 0.f; }
+        state[mine * SF_PIXEL_STATE_FLOATS + PS_L1] = 0.f;
+        out_l1[mine] = 0.f;
+        here = false;
       }
-    } else if (CLASS == 1) {
-      if (!l1_sort_pixel_packed<16>(col_d, col_w, base, n, lane, vec, s_w, s_o, raw))
-        raw = l1_sort_pixel<16>(col_d, col_w, base, n, lane);
     }
-    raw = warp_sum(raw);
-    if (lane == 0) {
-      st[PS_L1] = raw;
-      out_l1[pix] = fmaxr(raw, 0.f);
+    unsigned todo = __ballot_sync(FULL, here);
+    while (todo) {
+      const int l = __ffs(todo) - 1;
+      todo &= todo - 1;
+      const int64_t pix = g + l * groups;
+      const int n = __shfl_sync(FULL, my_n, l);
+      const int64_t base = __shfl_sync(FULL, my_base, l);
+      float raw = 0.f;
+      if (CLASS == 0) {
+        if (n <= 128) {
+          if (!l1_sort_pixel_packed<4>(col_d, col_w, base, n, lane, vec, s_w, s_o, raw))
+            raw = l1_sort_pixel<4>(col_d, col_w, base, n, lane);
+        } else {
+          if (!l1_sort_pixel_packed<8>(col_d, col_w, base, n, lane, vec, s_w, s_o, raw))
+            raw = l1_sort_pixel<8>(col_d, col_w, base, n, lane);
+        }
+      } else if (CLASS == 1) {
+        if (!l1_sort_pixel_packed<16>(col_d, col_w, base, n, lane, vec, s_w, s_o, raw))
+          raw = l1_sort_pixel<16>(col_d, col_w, base, n, lane);
+      }
+      raw = warp_sum(raw);
+      if (lane == 0) {
+        state[pix * SF_PIXEL_STATE_FLOATS + PS_L1] = raw;
+        out_l1[pix] = fmaxr(raw, 0.f);
+      }
     }
   }
 }
@@ -649,7 +673,27 @@ __global__ void __launch_bounds__(LONG_THREADS) l1_resolve_long_kernel(
   const int tiles_x = (cam.width + TILE - 1) / TILE;
   float* col_d = l1s;
   float* col_w = l1s + slots;
-  for (int64_t pix = blockIdx.x; pix < npix; pix += gridDim.x) {
+  __shared__ int s_list[LONG_THREADS];
+  __shared__ int s_nlist;
+  // Pixels go to CTAs in groups of LONG_THREADS: thread t of group j reads the count of
+  // pixel j + t J (J groups: a cluster of long runs spreads over many CTAs), the group's
+  // long runs are listed in shared memory, and the CTA resolves the listed pixels one
+  // after another (one load latency per group, not per pixel).
+  const int64_t ngroups = (npix + LONG_THREADS - 1) / LONG_THREADS;
+  for (int64_t j = blockIdx.x; j < ngroups; j += gridDim.x) {
+    if (tid == 0) s_nlist = 0;
+    __syncthreads();
+    if (j + tid * ngroups < npix) {
+      const int64_t q = j + tid * ngroups;
+      int c = f2i(state[q * SF_PIXEL_STATE_FLOATS + PS_COUNT]);
+      const int room = off ? (int)(off[q + 1] - off[q]) : cap;
+      if (c > room) c = room;
+      if (c > 512) s_list[atomicAdd(&s_nlist, 1)] = tid;
+    }
+    __syncthreads();
+    const int nlist = s_nlist;
+   for (int li = 0; li < nlist; ++li) {
+    const int64_t pix = j + s_list[li] * ngroups;
     float* st = state + pix * SF_PIXEL_STATE_FLOATS;
     int n = f2i(st[PS_COUNT]);  // the same for every thread: the loop stays uniform
     const int u = (int)(pix % cam.width), v = (int)(pix / cam.width);
@@ -658,7 +702,6 @@ __global__ void __launch_bounds__(LONG_THREADS) l1_resolve_long_kernel(
     const int64_t base = l1_base(tile, ptid, cap, off, pix);
     const int room = off ? (int)(off[pix + 1] - off[pix]) : cap;
     if (n > room) n = room;
-    if (n <= 512) continue;
     if (n > smem_k) n = smem_k;  // the launcher sizes smem_k >= the largest count
     int nn = 1024;
     while (nn < n) nn <<= 1;
@@ -740,6 +783,7 @@ __global__ void __launch_bounds__(LONG_THREADS) l1_resolve_long_kernel(
       out_l1[pix] = fmaxr(total, 0.f);
     }
     __syncthreads();  // shared memory is free for the next pixel
+   }
   }
 }
 
@@ -962,7 +1006,7 @@ cudaError_t fwd_launch(const RasterFwdArgs& a, int n_tiles, cudaStream_t s) {
   constexpr size_t bytes = sizeof(float4) * FWD_BATCH * REC4;
   constexpr size_t ring = sizeof(float) * ((DIST & SF_DIST_L1) ? 2 : 1) * L1_RING * TILE_PIXELS;
   static bool configured = false;
-  cudaError_t e = configure_smem(raster_forward_kernel<MODE, DIST>, bytes, ring, 4, configured);
+  cudaError_t e = configure_smem(raster_forward_kernel<MODE, DIST>, bytes, ring, SF_FWD_MIN_CTAS, configured);
   if (e != cudaSuccess) return e;
   raster_forward_kernel<MODE, DIST><<<n_tiles, TILE_PIXELS, bytes, s>>>(a);
   return cudaGetLastError();
@@ -1029,8 +1073,9 @@ cudaError_t launch_l1_resolve(const sf_camera& cam, const sf_settings& st, float
   (void)st;
   const int64_t npix = (int64_t)cam.width * cam.height;
   if (npix == 0) return cudaSuccess;
-  int64_t blocks = (npix + 3) / 4;
-  if (blocks > 148 * 64) blocks = 148 * 64;
+  // one 32-pixel group per warp (4 warps per CTA) for the common class; the longer
+  // classes stride over the groups with a grid of 8 CTAs per SM
+  const int64_t blocks = (npix + 127) / 128;
   count_launches(1);
   l1_resolve_kernel<0><<<(unsigned)blocks, 128, 0, s>>>(cam, state, l1s, slots, off, cap, 0, out_l1);
   cudaError_t e = cudaGetLastError();

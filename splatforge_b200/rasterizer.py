@@ -219,6 +219,23 @@ class _Project(torch.autograd.Function):
         return (*outs, None)
 
 
+def _size_class(n):
+    """Round a buffer length up to one of eight classes per octave (<= 12.5% larger).
+
+    The per-render buffers whose size follows the pose (intersection ids, the binning
+    workspace) then come from a small set of sizes, so the caching allocator finds an
+    exact-size cached block for a pose it has seen before instead of splitting blocks
+    until a request needs a fresh device allocation."""
+    if n <= 1 << 20:
+        return n
+    step = 1 << (n.bit_length() - 4)
+    return (n + step - 1) // step * step
+
+
+def _class_empty(n, dtype, dev):
+    return torch.empty((_size_class(n),), device=dev, dtype=dtype)[:n]
+
+
 _PINNED = {}
 
 
@@ -257,8 +274,8 @@ def bin_gaussians(plan):
     plan.n_isect = int(total)
     call("sf_b200_bin_workspace_bytes", n, plan.n_isect, plan.n_tiles, ctypes.byref(size))
     if size.value > ws.numel():
-        ws = torch.empty((size.value,), device=dev, dtype=torch.uint8)
-    plan.ids = torch.empty((max(plan.n_isect, 1),), device=dev, dtype=torch.int32)
+        ws = _class_empty(size.value, torch.uint8, dev)
+    plan.ids = _class_empty(max(plan.n_isect, 1), torch.int32, dev)
     plan.ranges = torch.empty((plan.n_tiles, 2), device=dev, dtype=torch.int32)
     call(
         "sf_b200_bin_emit", _ptr(order), _ptr(offsets), _ptr(plan.rect), n, plan.n_isect,
@@ -349,15 +366,17 @@ class _Raster(torch.autograd.Function):
                 "sf_b200_l1_resolve", ctypes.byref(plan.cam), ctypes.byref(plan.settings), _ptr(state),
                 _ptr(l1s), slots, _ptr(l1_off), cap, most, _ptr(l1), _stream(dev),
             )
-        ctx.save_for_backward(records)
+        # the pixel state and the L1 sample store are saved tensors, so autograd frees
+        # them once the backward has run (a caller that keeps the outputs of one view
+        # while rendering the next then holds one L1 store, not two)
+        ctx.save_for_backward(records, state, l1s, l1_off)
         ctx.plan = plan
-        ctx.state = state
-        ctx.l1 = (l1s, slots, l1_off, cap)
+        ctx.l1 = (slots, cap)
         return rgb, alpha, depth, normals, l1, l2, median, ray_color, amb
 
     @staticmethod
     def backward(ctx, g_rgb, g_alpha, g_depth, g_normals, g_l1, g_l2, g_median, g_var, g_amb):
-        (records,) = ctx.saved_tensors
+        records, state, l1s, l1_off = ctx.saved_tensors
         plan = ctx.plan
         dev, n = plan.device, plan.n
         grads = [
@@ -367,7 +386,7 @@ class _Raster(torch.autograd.Function):
         grad_records = torch.zeros((n, RECORD_FLOATS), device=dev, dtype=torch.float32)
         grad_means2d = torch.empty((n, 2), device=dev, dtype=torch.float32)
         absgrad = plan.absgrad if plan.absgrad is not None else torch.zeros((n, 2), device=dev)
-        l1s, slots, l1_off, cap = ctx.l1
+        slots, cap = ctx.l1
         ev = None
         if PROFILE is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -375,7 +394,7 @@ class _Raster(torch.autograd.Function):
         plan.error_word = torch.zeros((1,), device=dev, dtype=torch.int32)
         call(
             "sf_b200_raster_backward", _ptr(records), n, _ptr(plan.ids), _ptr(plan.ranges),
-            ctypes.byref(plan.cam), ctypes.byref(plan.settings), _ptr(ctx.state), _ptr(l1s), slots,
+            ctypes.byref(plan.cam), ctypes.byref(plan.settings), _ptr(state), _ptr(l1s), slots,
             _ptr(l1_off), cap, *(_ptr(g) for g in grads), _ptr(grad_records), _ptr(grad_means2d),
             _ptr(absgrad), _ptr(plan.error_word), _stream(dev),
         )
