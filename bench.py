@@ -161,9 +161,12 @@ class RenderJob:
     * single-view workloads: at step s every rank renders orbit pose s mod 8 (with
       ``distinct=True``, rank r renders pose (s + r) mod 8 instead, the load imbalance of
       a batch of different poses);
-    * view-batched workloads: rank r renders the 8 poses 8(r + sN) .. 8(r + sN) + 7 of the
+    * view-batched workloads: step s renders the 8N poses 8sN .. 8sN + 8N - 1 of the
       workload's 64 (mod 64), so one rank cycles through all 64 and eight ranks render
-      all 64 every step.
+      all 64 every step.  During the warm-up rank r renders poses 8(r + sN) .. +7 and
+      times each view; after it the ranks share the per-pose times (one all-reduce) and
+      every timed step splits its 8N poses across the ranks by measured cost, longest
+      first (distributed.balanced_views), so the close-up poses do not pile onto one rank.
     """
 
     def __init__(self, workload, dev, rank, world, mode, distortions):
@@ -193,26 +196,60 @@ class RenderJob:
             # the gradients accumulate in the all-reduce buffer itself (no copy in or out)
             self.reducer.bind()
         self.last = None
+        self.costs = None      # per-pose render ms shared by all ranks (view-batched)
+        self.view_events = []  # (pose, start, end) timed during the warm-up
+        self.views_per_rank = None
+
+    def pose_ids(self, s, distinct=False):
+        if self.per == 1:
+            return [((s + self.rank) if distinct else s) % len(self.poses)]
+        if self.costs is None:
+            base = self.per * (self.rank + s * self.world)
+            return [(base + v) % len(self.poses) for v in range(self.per)]
+        from splatforge_b200 import distributed
+
+        step_poses = [(self.per * self.world * s + k) % len(self.poses) for k in range(self.per * self.world)]
+        split = distributed.balanced_views(step_poses, self.costs, self.world)
+        self.views_per_rank = [len(x) for x in split]
+        return split[self.rank]
 
     def cams(self, s, distinct=False):
-        if self.per == 1:
-            return [self.poses[((s + self.rank) if distinct else s) % len(self.poses)]]
-        base = self.per * (self.rank + s * self.world)
-        return [self.poses[(base + v) % len(self.poses)] for v in range(self.per)]
+        return [self.poses[i] for i in self.pose_ids(s, distinct)]
 
     def step(self, s, distinct=False):
         from splatforge_b200 import rasterizer, scenes
 
         self.reducer.zero_grad()
-        for c in self.cams(s, distinct):
+        timing = self.per > 1 and self.costs is None
+        out = None
+        for i in self.pose_ids(s, distinct):
+            if timing:
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record()
             view = scenes.activated(self.p)
-            out = rasterizer.rasterize(view.means, view.quats, view.scales, view.opacities, view.sh, 3, c,
-                                       self.settings)
+            out = rasterizer.rasterize(view.means, view.quats, view.scales, view.opacities, view.sh, 3,
+                                       self.poses[i], self.settings)
             loss = linear_loss(out, self.ups)
             loss.backward()
+            if timing:
+                ev[1].record()
+                self.view_events.append((i, ev[0], ev[1]))
         self.reducer()
         self.last = out
         return out
+
+    def share_costs(self):
+        """After the warm-up (every rank): the per-pose render times become one table."""
+        from splatforge_b200 import distributed
+
+        if self.per == 1 or self.costs is not None or not self.view_events:
+            return  # (the same on every rank: all ran the same warm-up steps)
+        torch.cuda.synchronize()
+        local = {}
+        for i, a, b in self.view_events:
+            local[i] = max(local.get(i, 0.0), a.elapsed_time(b))
+        self.view_events = []
+        self.costs = distributed.shared_view_costs(local, len(self.poses), device=self.dev)
 
     def pixels_per_step(self):
         return self.H * self.W * self.per * self.world
@@ -247,6 +284,7 @@ def time_steps(job, steps, warmup, distinct=False):
 
     for s in range(warmup):
         job.step(s, distinct)
+    job.share_costs()
     torch.cuda.synchronize()
     job.reducer.events.clear()
     if job.world > 1:
@@ -366,7 +404,8 @@ def run_b200(args):
                     "peak_source": f"FP32 SIMT 148 SM x 128 lanes x 2 at the sampled {sm_mhz:.0f} MHz",
                     "hbm_peak_gbs": peaks.get("hbm_gbs")}
         poses = ("every rank renders orbit pose s mod 8 at step s" if job.per == 1 else
-                 f"rank r renders poses 8(r + sN) .. +7 of the {len(job.poses)} (mod {len(job.poses)}) at step s")
+                 f"step s renders poses 8sN .. 8sN + 8N - 1 of the {len(job.poses)} (mod {len(job.poses)}), split "
+                 "across the ranks by the per-pose render times measured in the warm-up (longest first)")
         result = {
             "metric": METRIC, "value": round(value, 3), "unit": "Mpix/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
@@ -489,7 +528,9 @@ def secondary(args, dev, rank, world):
         "mpix_per_s": round(job.pixels_per_step() / (ms * 1e-3) / 1e6, 3), "ms_per_step": round(ms, 3),
         "workload": f"surfaces3m_views64: {job.n} Gaussians, {job.W}x{job.H}, mode gof, distortions l1 "
                     f"(the training profile), fwd+bwd, {job.per} views per GPU per step, {views} per step",
-        "poses": f"rank r renders poses 8(r + sN) .. +7 of the {len(job.poses)} (mod {len(job.poses)}) at step s",
+        "poses": f"step s renders poses 8sN .. 8sN + 8N - 1 of the {len(job.poses)} (mod {len(job.poses)}), "
+                 "split across the ranks by the per-pose render times measured in the warm-up (longest first)",
+        "views_per_rank_last_step": job.views_per_rank,
         "warmup_steps": warm, "step_ms_this_rank": [round(x, 2) for x in per_step], "diag_this_rank": job.diag,
         "value_median_step": round(views / (_median(per_step) * 1e-3), 3),
         "step_ms_median": [round(r[0], 3) for r in ranks], "allreduce_ms": [round(r[2], 3) for r in ranks],

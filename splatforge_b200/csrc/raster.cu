@@ -655,14 +655,185 @@ __global__ void __launch_bounds__(128) l1_resolve_kernel(
 }
 
 // Runs longer than 512 samples (a camera close to a dense surface): one CTA of 256
-// threads per pixel.  The pixel's exact 64-bit (depth bits, index) keys are sorted by a
-// bitonic network in shared memory, padded to the next power of two of this pixel's
-// count (at least 1024); each thread then scans a contiguous slice of the sorted
-// samples, a block scan of the slices' totals gives every slice its prefix, and the
-// two factors are written back by compositing index.
+// threads per pixel.
 constexpr int LONG_THREADS = 256;
 
-__global__ void __launch_bounds__(LONG_THREADS) l1_resolve_long_kernel(
+__device__ __forceinline__ unsigned long long kmin(unsigned long long a, unsigned long long b) { return a < b ? a : b; }
+__device__ __forceinline__ unsigned long long kmax(unsigned long long a, unsigned long long b) { return a < b ? b : a; }
+
+// Runs of 513 .. 256 I samples, I = 4, 8, 16: the CTA sorts the pixel's exact 64-bit
+// (depth bits, compositing index) keys as one bitonic network of NN = 256 I positions
+// held in registers, thread t owning positions t I .. t I + I - 1.  The network is the
+// all-ascending form of l1_sort_pixel_packed (a merge of size s first compares p with
+// its mirror p ^ (s - 1), then half-cleaners p vs p ^ h, the lower position taking the
+// minimum).  A compare-exchange whose partner is in the same thread is a register
+// min/max, one in the same warp a shuffle, and only the stages whose partner is in
+// another warp (6 of the 78 stages at NN = 4096) exchange through shared memory, where
+// the keys sit striped (position t I + j at j * 256 + t: conflict-free for every
+// partner distance).  The weights are parked by compositing index in s_w; after the
+// sort each thread scans its I sorted samples, a block scan of the per-thread totals
+// gives each its prefix, and both factors are assembled in shared memory by compositing
+// index and leave in blocked layout.  Returns this thread's share of the L1 value.
+template <int I>
+__device__ float l1_sort_pixel_cta(float* col_d, float* col_w, int64_t base, int n, bool vec,
+                                   unsigned long long* s_key, float* s_w, float (*s_tot)[LONG_THREADS / 32]) {
+  constexpr int NN = LONG_THREADS * I;
+  constexpr int WI = 32 * I;  // positions per warp
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  unsigned long long key[I];
+  {
+    float dv[I], wv[I];
+    l1_load_run<I>(col_d, base, n, tid, vec, dv);
+    l1_load_run<I>(col_w, base, n, tid, vec, wv);
+#pragma unroll
+    for (int j = 0; j < I; ++j) {
+      const int e = tid * I + j;
+      key[j] = e < n ? ((unsigned long long)__float_as_uint(dv[j]) << 32) | (unsigned)e : ~0ull;
+    }
+#pragma unroll
+    for (int q = 0; q < I / 4; ++q)
+      *reinterpret_cast<float4*>(s_w + tid * I + 4 * q) =
+          make_float4(wv[4 * q], wv[4 * q + 1], wv[4 * q + 2], wv[4 * q + 3]);
+  }
+  // in-thread merges of sizes 2 .. I
+#pragma unroll
+  for (int size = 2; size <= I; size <<= 1) {
+#pragma unroll
+    for (int j = 0; j < I; ++j) {
+      const int m = j ^ (size - 1);
+      if (j < m) {
+        const unsigned long long a = kmin(key[j], key[m]), b = kmax(key[j], key[m]);
+        key[j] = a;
+        key[m] = b;
+      }
+    }
+#pragma unroll
+    for (int stride = size >> 2; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int j = 0; j < I; ++j) {
+        if ((j & stride) == 0) {
+          const unsigned long long a = kmin(key[j], key[j + stride]), b = kmax(key[j], key[j + stride]);
+          key[j] = a;
+          key[j + stride] = b;
+        }
+      }
+    }
+  }
+#pragma unroll 1
+  for (int size = 2 * I; size <= NN; size <<= 1) {
+    if (size <= WI) {
+      // mirror partner in this warp: lane ^ (size / I - 1), element I - 1 - j
+      const int lm = size / I - 1;
+      const bool take_min = (lane & (size / (2 * I))) == 0;
+#pragma unroll
+      for (int j = 0; j < I / 2; ++j) {
+        const unsigned long long o1 = __shfl_xor_sync(FULL, key[I - 1 - j], lm);
+        const unsigned long long o2 = __shfl_xor_sync(FULL, key[j], lm);
+        key[j] = take_min ? kmin(key[j], o1) : kmax(key[j], o1);
+        key[I - 1 - j] = take_min ? kmin(key[I - 1 - j], o2) : kmax(key[I - 1 - j], o2);
+      }
+    } else {
+      // mirror partner in another warp: thread tid ^ (size / I - 1), element I - 1 - j
+      const int tm = size / I - 1;
+      const bool take_min = (tid & (size / (2 * I))) == 0;
+      __syncthreads();  // the previous exchange has been read
+#pragma unroll
+      for (int j = 0; j < I; ++j) s_key[j * LONG_THREADS + tid] = key[j];
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < I; ++j) {
+        const unsigned long long o = s_key[(I - 1 - j) * LONG_THREADS + (tid ^ tm)];
+        key[j] = take_min ? kmin(key[j], o) : kmax(key[j], o);
+      }
+    }
+#pragma unroll 1
+    for (int h = size >> 2; h >= I; h >>= 1) {
+      const int ts = h / I;  // partner thread distance
+      const bool take_min = (tid & ts) == 0;
+      if (h >= WI) {
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < I; ++j) s_key[j * LONG_THREADS + tid] = key[j];
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < I; ++j) {
+          const unsigned long long o = s_key[j * LONG_THREADS + (tid ^ ts)];
+          key[j] = take_min ? kmin(key[j], o) : kmax(key[j], o);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < I; ++j) {
+          const unsigned long long o = __shfl_xor_sync(FULL, key[j], ts);
+          key[j] = take_min ? kmin(key[j], o) : kmax(key[j], o);
+        }
+      }
+    }
+#pragma unroll
+    for (int stride = I >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int j = 0; j < I; ++j) {
+        if ((j & stride) == 0) {
+          const unsigned long long a = kmin(key[j], key[j + stride]), b = kmax(key[j], key[j + stride]);
+          key[j] = a;
+          key[j + stride] = b;
+        }
+      }
+    }
+  }
+  __syncthreads();  // every thread's weights are in s_w; the last exchange has been read
+  float w[I];
+  float lw = 0.f, lwd = 0.f;
+#pragma unroll
+  for (int j = 0; j < I; ++j) {
+    const bool live = key[j] != ~0ull;
+    w[j] = live ? s_w[(uint32_t)key[j]] : 0.f;
+    lw += w[j];
+    lwd += w[j] * (live ? __uint_as_float((uint32_t)(key[j] >> 32)) : 0.f);
+  }
+  // block scan of the per-thread totals (threads hold consecutive sorted positions)
+  float iw = lw, iwd = lwd;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float a1 = __shfl_up_sync(FULL, iw, o), a2 = __shfl_up_sync(FULL, iwd, o);
+    if (lane >= o) { iw += a1; iwd += a2; }
+  }
+  if (lane == 31) { s_tot[0][wid] = iw; s_tot[1][wid] = iwd; }
+  __syncthreads();  // also: every thread has read its weights from s_w
+  float pw = iw - lw, pwd = iwd - lwd, Wt = 0.f, Dt = 0.f;
+#pragma unroll
+  for (int q = 0; q < LONG_THREADS / 32; ++q) {
+    if (q < wid) { pw += s_tot[0][q]; pwd += s_tot[1][q]; }
+    Wt += s_tot[0][q];
+    Dt += s_tot[1][q];
+  }
+  float* s_o = reinterpret_cast<float*>(s_key);  // the keys' space is free
+  float raw = 0.f;
+#pragma unroll
+  for (int j = 0; j < I; ++j) {
+    if (key[j] != ~0ull) {
+      const uint32_t k = (uint32_t)key[j];
+      const float d = __uint_as_float((uint32_t)(key[j] >> 32));
+      raw += 2.f * w[j] * (d * pw - pwd);
+      s_o[k] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
+      s_w[k] = 2.f * w[j] * (2.f * pw + w[j] - Wt);
+      pw += w[j];
+      pwd += w[j] * d;
+    }
+  }
+  __syncthreads();  // both factors assembled by compositing index
+  l1_store_run<I>(col_d, base, n, tid, vec, s_o);
+  l1_store_run<I>(col_w, base, n, tid, vec, s_w);
+  return raw;
+}
+
+// The long-run kernel: runs of up to 4096 samples take l1_sort_pixel_cta; longer ones
+// (up to the launcher's smem_k) sort their exact 64-bit keys by a bitonic network in
+// shared memory padded to the next power of two of the pixel's count, each thread then
+// scans a contiguous slice of the sorted samples, a block scan of the slices' totals
+// gives every slice its prefix, and the two factors are written back by compositing
+// index.
+
+__global__ void __launch_bounds__(LONG_THREADS, 2) l1_resolve_long_kernel(
     sf_camera cam, float* state, float* l1s, int64_t slots, const int64_t* off, int cap, int smem_k,
     float* out_l1) {
   extern __shared__ unsigned long long s_long[];  // smem_k keys, then smem_k weights
@@ -673,6 +844,8 @@ __global__ void __launch_bounds__(LONG_THREADS) l1_resolve_long_kernel(
   const int tiles_x = (cam.width + TILE - 1) / TILE;
   float* col_d = l1s;
   float* col_w = l1s + slots;
+  // 16-byte loads and stores need aligned columns (runs start on 8-sample boundaries)
+  const bool vec = ((reinterpret_cast<uintptr_t>(l1s) | (uintptr_t)(slots * sizeof(float))) & 15) == 0;
   __shared__ int s_list[LONG_THREADS];
   __shared__ int s_nlist;
   // Pixels go to CTAs in groups of LONG_THREADS: thread t of group j reads the count of
@@ -705,70 +878,77 @@ __global__ void __launch_bounds__(LONG_THREADS) l1_resolve_long_kernel(
     if (n > smem_k) n = smem_k;  // the launcher sizes smem_k >= the largest count
     int nn = 1024;
     while (nn < n) nn <<= 1;
-    float Wt = 0.f, Dt = 0.f;
-    for (int k = tid; k < nn; k += LONG_THREADS) {
-      if (k < n) {
-        const float d = col_d[base + k], w = col_w[base + k];
-        s_long[k] = ((unsigned long long)__float_as_uint(d) << 32) | (unsigned)k;
-        s_w[k] = w;
-        Wt += w; Dt += w * d;
-      } else {
-        s_long[k] = ~0ull;  // padding sorts last
-      }
-    }
-    Wt = warp_sum(Wt); Dt = warp_sum(Dt);
-    if (lane == 0) { s_tot[0][wid] = Wt; s_tot[1][wid] = Dt; }
-    __syncthreads();
-    Wt = 0.f; Dt = 0.f;
-#pragma unroll
-    for (int q = 0; q < LONG_THREADS / 32; ++q) { Wt += s_tot[0][q]; Dt += s_tot[1][q]; }
-    for (int size = 2; size <= nn; size <<= 1) {
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        for (int q = tid; q < nn / 2; q += LONG_THREADS) {
-          const int i = ((q & ~(stride - 1)) << 1) | (q & (stride - 1));
-          const int j = i + stride;
-          const unsigned long long a = s_long[i], b = s_long[j];
-          if ((a > b) == ((i & size) == 0)) { s_long[i] = b; s_long[j] = a; }
+    float raw;
+    if (nn <= 4096) {
+      raw = nn == 1024 ? l1_sort_pixel_cta<4>(col_d, col_w, base, n, vec, s_long, s_w, s_tot)
+          : nn == 2048 ? l1_sort_pixel_cta<8>(col_d, col_w, base, n, vec, s_long, s_w, s_tot)
+                       : l1_sort_pixel_cta<16>(col_d, col_w, base, n, vec, s_long, s_w, s_tot);
+    } else {
+      float Wt = 0.f, Dt = 0.f;
+      for (int k = tid; k < nn; k += LONG_THREADS) {
+        if (k < n) {
+          const float d = col_d[base + k], w = col_w[base + k];
+          s_long[k] = ((unsigned long long)__float_as_uint(d) << 32) | (unsigned)k;
+          s_w[k] = w;
+          Wt += w; Dt += w * d;
+        } else {
+          s_long[k] = ~0ull;  // padding sorts last
         }
-        __syncthreads();
       }
-    }
-    // each thread's contiguous slice of E sorted samples
-    const int E = nn / LONG_THREADS;
-    const int r0 = tid * E;
-    float tw = 0.f, twd = 0.f;
-    for (int e = 0; e < E; ++e) {
-      const int r = r0 + e;
-      if (r < n) {
-        const unsigned long long key = s_long[r];
-        const float d = __uint_as_float((uint32_t)(key >> 32)), w = s_w[(uint32_t)key];
-        tw += w; twd += w * d;
+      Wt = warp_sum(Wt); Dt = warp_sum(Dt);
+      if (lane == 0) { s_tot[0][wid] = Wt; s_tot[1][wid] = Dt; }
+      __syncthreads();
+      Wt = 0.f; Dt = 0.f;
+  #pragma unroll
+      for (int q = 0; q < LONG_THREADS / 32; ++q) { Wt += s_tot[0][q]; Dt += s_tot[1][q]; }
+      for (int size = 2; size <= nn; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+          for (int q = tid; q < nn / 2; q += LONG_THREADS) {
+            const int i = ((q & ~(stride - 1)) << 1) | (q & (stride - 1));
+            const int j = i + stride;
+            const unsigned long long a = s_long[i], b = s_long[j];
+            if ((a > b) == ((i & size) == 0)) { s_long[i] = b; s_long[j] = a; }
+          }
+          __syncthreads();
+        }
       }
-    }
-    // exclusive block scan of the slice totals
-    float iw = tw, iwd = twd;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float a1 = __shfl_up_sync(FULL, iw, o), a2 = __shfl_up_sync(FULL, iwd, o);
-      if (lane >= o) { iw += a1; iwd += a2; }
-    }
-    __syncthreads();  // every thread has read the block totals above
-    if (lane == 31) { s_tot[0][wid] = iw; s_tot[1][wid] = iwd; }
-    __syncthreads();
-    float pw = iw - tw, pwd = iwd - twd;
-    for (int q = 0; q < wid; ++q) { pw += s_tot[0][q]; pwd += s_tot[1][q]; }
-    float raw = 0.f;
-    for (int e = 0; e < E; ++e) {
-      const int r = r0 + e;
-      if (r < n) {
-        const unsigned long long key = s_long[r];
-        const uint32_t k = (uint32_t)key;
-        const float d = __uint_as_float((uint32_t)(key >> 32)), w = s_w[k];
-        raw += 2.f * w * (d * pw - pwd);
-        col_d[base + k] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
-        col_w[base + k] = 2.f * w * (2.f * pw + w - Wt);
-        pw += w;
-        pwd += w * d;
+      // each thread's contiguous slice of E sorted samples
+      const int E = nn / LONG_THREADS;
+      const int r0 = tid * E;
+      float tw = 0.f, twd = 0.f;
+      for (int e = 0; e < E; ++e) {
+        const int r = r0 + e;
+        if (r < n) {
+          const unsigned long long key = s_long[r];
+          const float d = __uint_as_float((uint32_t)(key >> 32)), w = s_w[(uint32_t)key];
+          tw += w; twd += w * d;
+        }
+      }
+      // exclusive block scan of the slice totals
+      float iw = tw, iwd = twd;
+  #pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float a1 = __shfl_up_sync(FULL, iw, o), a2 = __shfl_up_sync(FULL, iwd, o);
+        if (lane >= o) { iw += a1; iwd += a2; }
+      }
+      __syncthreads();  // every thread has read the block totals above
+      if (lane == 31) { s_tot[0][wid] = iw; s_tot[1][wid] = iwd; }
+      __syncthreads();
+      float pw = iw - tw, pwd = iwd - twd;
+      for (int q = 0; q < wid; ++q) { pw += s_tot[0][q]; pwd += s_tot[1][q]; }
+      raw = 0.f;
+      for (int e = 0; e < E; ++e) {
+        const int r = r0 + e;
+        if (r < n) {
+          const unsigned long long key = s_long[r];
+          const uint32_t k = (uint32_t)key;
+          const float d = __uint_as_float((uint32_t)(key >> 32)), w = s_w[k];
+          raw += 2.f * w * (d * pw - pwd);
+          col_d[base + k] = 2.f * (2.f * d * pw - d * Wt + Dt - 2.f * pwd);
+          col_w[base + k] = 2.f * w * (2.f * pw + w - Wt);
+          pw += w;
+          pwd += w * d;
+        }
       }
     }
     raw = warp_sum(raw);
@@ -1093,7 +1273,8 @@ cudaError_t launch_l1_resolve(const sf_camera& cam, const sf_settings& st, float
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(l1_resolve_long_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e != cudaSuccess) return e;
-  const int per_sm = (int)min((size_t)8, (size_t)(220 * 1024) / (smem + 1024));
+  // resident CTAs per SM: the register budget (launch bounds) allows 2
+  const int per_sm = (int)min((size_t)2, (size_t)(220 * 1024) / (smem + 1024));
   const int64_t b2 = min(npix, (int64_t)148 * (per_sm > 0 ? per_sm : 1));
   count_launches(1);
   l1_resolve_long_kernel<<<(unsigned)b2, LONG_THREADS, smem, s>>>(cam, state, l1s, slots, off, cap, smem_k,

@@ -33,6 +33,41 @@ def shard(items, rank, world):
     return items[lo:hi]
 
 
+def balanced_views(views, costs, world):
+    """Cost-balanced assignment of one step's views to ``world`` ranks.
+
+    ``views`` are view indices, ``costs[v]`` the measured render time of view v (the
+    same table on every rank, see :func:`shared_view_costs`).  Longest processing time
+    first: views in decreasing cost (ties by index) each go to the rank with the least
+    load so far (ties to the lowest rank).  Ranks may get different numbers of views;
+    the gradients are summed over all of them by the all-reduce either way, so the step
+    computes the same sum while its slowest rank — the step's length in a synchronous
+    step — carries as little as the costs allow.  Deterministic: every rank derives the
+    same assignment.  Returns a list of ``world`` lists, each in increasing view order.
+    """
+    order = sorted(views, key=lambda v: (-float(costs[v]), v))
+    load = [0.0] * world
+    out = [[] for _ in range(world)]
+    for v in order:
+        r = min(range(world), key=lambda k: (load[k], k))
+        out[r].append(v)
+        load[r] += float(costs[v])
+    return [sorted(o) for o in out]
+
+
+def shared_view_costs(local_costs, n_views, device=None):
+    """One cost table for every rank: ``local_costs`` maps the views this rank timed to
+    their render times; the table holds, per view, the largest time any rank reported
+    (0 for views no rank timed).  One all-reduce (MAX) of n_views floats when a process
+    group is up."""
+    t = torch.zeros(n_views, dtype=torch.float32, device=device)
+    for v, c in local_costs.items():
+        t[v] = max(float(t[v]), float(c))
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
+
+
 def query_shard(n, rank, shards):
     """[lo, hi) of query shard ``rank mod shards`` when ``n`` queries are cut into
     ``shards`` contiguous shards of sizes differing by at most one (the opacity-field

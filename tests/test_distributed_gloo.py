@@ -44,6 +44,14 @@ def _worker(rank, world, port, mode, queue):
         distributed.init_from_env(backend="gloo", timeout_s=10)
         params, cams = scenes.workload("demo48", seed=0)
         mine = distributed.shard(cams[:4], rank, world)
+        if mode == "balanced":
+            # each rank timed two of the four views; the shared table decides the split
+            timed = {0: {0: 5.0, 1: 1.0}, 1: {2: 9.0, 3: 1.0}}[rank]
+            costs = distributed.shared_view_costs(timed, 4)
+            assert costs == [5.0, 1.0, 9.0, 1.0], costs
+            split = distributed.balanced_views([0, 1, 2, 3], costs, world)
+            assert split == [[2], [0, 1, 3]], split
+            mine = [cams[i] for i in split[rank]]
         if mode == "fail" and rank == 1:
             raise RuntimeError("rank 1 failed before the all-reduce")
         if mode == "bound":
@@ -101,6 +109,39 @@ def test_gradients_bound_to_the_buffer_reduce_in_place():
     for rank in (0, 1):
         for got, want in zip(res[rank][1], full.tensors()):
             torch.testing.assert_close(got, want.grad, atol=2e-5, rtol=1e-4)
+
+
+def test_cost_balanced_views_sum_to_the_full_batch_gradients():
+    """Ranks share their measured view costs, split the step's views longest first
+    (one rank gets one view, the other three) and the all-reduce still yields the
+    full batch's gradients on both."""
+    res = _run("balanced")
+    assert all(s == "ok" for s, _ in res.values()), res
+    params, cams = scenes.workload("demo48", seed=0)
+    full = _grads_for(cams[:4], params)
+    for rank in (0, 1):
+        for got, want in zip(res[rank][1], full.tensors()):
+            torch.testing.assert_close(got, want.grad, atol=2e-5, rtol=1e-4)
+
+
+def test_balanced_views_partition_and_bound():
+    import random
+
+    rnd = random.Random(3)
+    for world in (1, 2, 3, 8):
+        costs = [rnd.choice([1.0, 1.2, 0.9, 11.0]) for _ in range(64)]
+        views = list(range(5, 5 + 8 * world))
+        views = [v % 64 for v in views]
+        split = distributed.balanced_views(views, costs, world)
+        assert sorted(v for part in split for v in part) == sorted(views)
+        assert split == distributed.balanced_views(views, costs, world)  # deterministic
+        loads = [sum(costs[v] for v in part) for part in split]
+        # longest-first greedy: within the largest single cost of the average, and never
+        # worse than the round-robin blocks of 8
+        total = sum(costs[v] for v in views)
+        assert max(loads) <= total / world + max(costs[v] for v in views) + 1e-9
+        blocks = [sum(costs[v] for v in views[8 * r:8 * r + 8]) for r in range(world)]
+        assert max(loads) <= max(blocks) + 1e-9
 
 
 def test_bound_views_and_fallback_packing_on_one_process():

@@ -253,18 +253,23 @@ def test_cpu_inputs_are_rejected_without_fallback():
         rasterize(view.means, view.quats, view.scales, view.opacities, view.sh, 3, cams[0], RasterSettings())
 
 
-@pytest.mark.parametrize("n", [420, 700])
-def test_l1_long_sample_runs_match_the_oracle(n):
+@pytest.mark.parametrize("n,opacity,lo,hi", [
+    (420, 0.004, 257, 512),     # 16 samples per lane, one warp per pixel
+    (700, 0.004, 513, 1024),    # one CTA per pixel, 4 samples per thread in registers
+    (1500, 0.004, 1025, 2048),  # 8 per thread
+    (3000, 0.002, 2049, 4096),  # 16 per thread
+    (5000, 0.002, 4097, 8192),  # the shared-memory network
+])
+def test_l1_long_sample_runs_match_the_oracle(n, opacity, lo, hi):
     """n faint, wide Gaussians over a 32x24 image: every pixel composites up to n
-    samples (transmittance never reaches the floor).  420 takes the 16-per-lane register
-    sort of the L1 resolve (257-512 samples), 700 the shared-memory sort of the long
-    runs."""
+    samples (transmittance stays above the floor), which takes each sort of the L1
+    resolve in turn as the runs grow."""
     rng = np.random.default_rng(9)
     means = rng.normal(0.0, 0.15, size=(n, 3))
     log_scales = np.log(rng.uniform(0.25, 0.4, size=(n, 3)))
     quats = rng.normal(size=(n, 4))
     quats /= np.linalg.norm(quats, axis=-1, keepdims=True)
-    logits = np.log(0.004 / 0.996) + rng.normal(0.0, 0.1, size=n)
+    logits = np.log(opacity / (1.0 - opacity)) + rng.normal(0.0, 0.1, size=n)
     sh = rng.normal(0.0, 0.05, size=(n, 16, 3))
     sh[:, 0] = rng.normal(0.5, 0.1, size=(n, 3))
     f = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32))
@@ -276,7 +281,7 @@ def test_l1_long_sample_runs_match_the_oracle(n):
         ups = _ups(cam, 21)
         got, ggrads, out = run_gpu(params, cam, settings, sel, ups)
         most = out["stats"]["l1_max_samples"]
-        assert (256 < most <= 512) if n <= 512 else most > 512, most
+        assert lo <= most <= hi, most
         want, wgrads, _ = run_oracle(params, cam, mode, "l1", sel, ups)
         assert_images(got, want, mode, f"long/{mode}")
         assert_grads(ggrads, wgrads, f"long/{mode}")
