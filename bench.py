@@ -297,6 +297,7 @@ def time_steps(job, steps, warmup, distinct=False):
 
     stats0 = torch.cuda.memory_stats()
     reruns0 = rasterizer.COUNTERS["l1_reruns"]
+    rebins0 = rasterizer.COUNTERS["bin_reruns"]
     host = []
     gc_ms = [0.0]
     gc_t = [0.0]
@@ -327,7 +328,8 @@ def time_steps(job, steps, warmup, distinct=False):
                 "device_allocs": stats1.get("num_device_alloc", 0) - stats0.get("num_device_alloc", 0),
                 "alloc_retries": stats1.get("num_alloc_retries", 0) - stats0.get("num_alloc_retries", 0),
                 "device_frees": stats1.get("num_device_free", 0) - stats0.get("num_device_free", 0),
-                "l1_reruns": rasterizer.COUNTERS["l1_reruns"] - reruns0, "gc_ms": round(gc_ms[0], 2)}
+                "l1_reruns": rasterizer.COUNTERS["l1_reruns"] - reruns0,
+                "bin_reruns": rasterizer.COUNTERS["bin_reruns"] - rebins0, "gc_ms": round(gc_ms[0], 2)}
     return ev[0].elapsed_time(ev[-1]) / steps, per
 
 

@@ -160,6 +160,18 @@ int sf_b200_bin_emit(const int32_t* order, const int64_t* offsets, const int32_t
                      int32_t* isect_ids, int32_t* tile_ranges, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* sf_b200_bin_emit without the host read of the intersection count: the count is
+ * offsets[n] on the device and `capacity` sizes isect_ids and the workspace
+ * (sf_b200_bin_workspace_bytes(0, capacity, n_tiles)).  A count above capacity emits
+ * nothing, leaves every tile range empty and sets *overflow to 1 (a device int32 the
+ * caller zeroes and reads back with its next synchronisation, then re-bins with the
+ * exact count).  No counterpart in the reference (it bins on the host,
+ * src/splatforge/studio/tile_binning.py:10-34). */
+int sf_b200_bin_emit_bounded(const int32_t* order, const int64_t* offsets, const int32_t* tile_rect,
+                             int64_t n, int64_t capacity, int32_t tiles_x, int32_t n_tiles,
+                             int32_t* isect_ids, int32_t* tile_ranges, void* workspace,
+                             size_t workspace_bytes, int32_t* overflow, void* stream);
+
 /* Same result as sf_b200_bin_order, for callers that cannot allocate device memory
  * (for instance a host application that owns the whole device budget through its own
  * pool and lets no plugin call cudaMalloc).  No counterpart in the reference: it has

@@ -79,6 +79,10 @@ _SIGNATURES = {
         ctypes.c_int,
         [P, P, P, c_int64, c_int64, c_int32, c_int32, P, P, P, c_size_t, P],
     ),
+    "sf_b200_bin_emit_bounded": (
+        ctypes.c_int,
+        [P, P, P, c_int64, c_int64, c_int32, c_int32, P, P, P, c_size_t, P, P],
+    ),
     "sf_b200_bin_keys": (ctypes.c_int, [P, P, P, c_int32, c_int64, P, P]),
     "sf_b200_bin_order_static": (ctypes.c_int, [P, P, c_int64, P, P, P]),
     "sf_b200_opacity_field_workspace_bytes": (ctypes.c_int, [c_int64, POINTER(c_size_t)]),

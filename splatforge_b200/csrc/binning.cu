@@ -136,14 +136,24 @@ constexpr int RADIX = 256;
 
 // Per-block digit histograms.  Each thread reads its keys four at a time (128-bit
 // loads) when the block's slab is 16-byte aligned.
+// Element counts: n, or with n_dev the count on the device (bounded by n; a count
+// above n means "nothing": the binning that produced it overflowed its capacity).
+__device__ __forceinline__ int64_t live_count(int64_t n, const int64_t* n_dev) {
+  if (!n_dev) return n;
+  const int64_t t = *n_dev;
+  return t > n ? 0 : t;
+}
+
 __global__ void __launch_bounds__(RS_THREADS) radix_upsweep_kernel(const uint32_t* keys, int64_t n,
-                                                                   int shift, int nb, uint32_t* hist) {
+                                                                   const int64_t* n_dev, int shift, int nb,
+                                                                   uint32_t* hist) {
+  n = live_count(n, n_dev);
   __shared__ uint32_t s_hist[RS_WARPS][RADIX];
   const int wid = threadIdx.x >> 5;
   for (int k = threadIdx.x; k < RS_WARPS * RADIX; k += RS_THREADS) (&s_hist[0][0])[k] = 0;
   __syncthreads();
   const int64_t block0 = (int64_t)blockIdx.x * RS_CHUNK;
-  const int rows = (int)min((int64_t)RS_CHUNK, n - block0);
+  const int rows = (int)max((int64_t)0, min((int64_t)RS_CHUNK, n - block0));
   if (rows == RS_CHUNK && (reinterpret_cast<uintptr_t>(keys + block0) & 15) == 0) {
     const uint4* k4 = reinterpret_cast<const uint4*>(keys + block0);
 #pragma unroll
@@ -171,8 +181,9 @@ __global__ void __launch_bounds__(RS_THREADS) radix_upsweep_kernel(const uint32_
 // memory and written out from there, so consecutive threads store consecutive
 // addresses of one digit's run instead of 32 scattered runs per instruction.
 __global__ void __launch_bounds__(RS_THREADS, RS_ROUNDS <= 8 ? 4 : 2) radix_downsweep_kernel(
-    const uint32_t* keys_in, const int32_t* vals_in, int64_t n, int shift, int nb,
+    const uint32_t* keys_in, const int32_t* vals_in, int64_t n, const int64_t* n_dev, int shift, int nb,
     const uint32_t* offsets, uint32_t* keys_out, int32_t* vals_out) {
+  n = live_count(n, n_dev);
   __shared__ uint32_t s_cnt[RS_WARPS][RADIX];
   __shared__ uint32_t s_off[RADIX];    // this block's first output slot per digit
   __shared__ uint32_t s_local[RADIX];  // first slot of each digit inside the block
@@ -185,7 +196,7 @@ __global__ void __launch_bounds__(RS_THREADS, RS_ROUNDS <= 8 ? 4 : 2) radix_down
   __syncthreads();
   const int64_t block0 = (int64_t)blockIdx.x * RS_CHUNK;
   const int64_t base = block0 + (int64_t)wid * (RS_CHUNK / RS_WARPS);
-  const int rows = (int)min((int64_t)RS_CHUNK, n - block0);
+  const int rows = (int)max((int64_t)0, min((int64_t)RS_CHUNK, n - block0));
   const unsigned lt = (1u << lane) - 1u;
   uint32_t key[RS_ROUNDS];
   int32_t val[RS_ROUNDS];
@@ -265,9 +276,10 @@ struct RadixScratch {
 // Stable sort of (key, value) pairs by key bits [0, bits).  Ping-pongs between
 // (k0, v0) and (k1, v1); the result lands in (k_final, v_final) which is one of the two
 // buffers, or v_out when given (the last pass then writes values there).
+// With n_dev, n is the buffers' capacity and the live count is read on the device.
 cudaError_t radix_sort(uint32_t* k0, int32_t* v0, uint32_t* k1, int32_t* v1, int64_t n, int bits,
                        RadixScratch sc, uint32_t** k_final, int32_t** v_final, int32_t* v_out,
-                       cudaStream_t s) {
+                       cudaStream_t s, const int64_t* n_dev = nullptr) {
   const int passes = (bits + 7) / 8;
   uint32_t* ki = k0; int32_t* vi = v0; uint32_t* ko = k1; int32_t* vo = v1;
   const int64_t nb = radix_blocks(n);
@@ -276,10 +288,11 @@ cudaError_t radix_sort(uint32_t* k0, int32_t* v0, uint32_t* k1, int32_t* v1, int
     const int shift = 8 * p;
     int32_t* vdst = (p == passes - 1 && v_out) ? v_out : vo;
     count_launches(2);
-    radix_upsweep_kernel<<<(unsigned)nb, RS_THREADS, 0, s>>>(ki, n, shift, (int)nb, sc.hist);
+    radix_upsweep_kernel<<<(unsigned)nb, RS_THREADS, 0, s>>>(ki, n, n_dev, shift, (int)nb, sc.hist);
     cudaError_t e = exclusive_scan<uint32_t, uint32_t>(sc.hist, RADIX * nb, sc.hist, sc.partial, nullptr, s);
     if (e != cudaSuccess) return e;
-    radix_downsweep_kernel<<<(unsigned)nb, RS_THREADS, 0, s>>>(ki, vi, n, shift, (int)nb, sc.hist, ko, vdst);
+    radix_downsweep_kernel<<<(unsigned)nb, RS_THREADS, 0, s>>>(ki, vi, n, n_dev, shift, (int)nb, sc.hist, ko,
+                                                                vdst);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     ki = ko; vi = vdst;
@@ -309,11 +322,16 @@ __global__ void gather_counts_kernel(const int32_t* order, const int32_t* count,
 
 // One warp per 32 depth-ordered Gaussians: the warp writes each Gaussian's run of
 // intersections in turn, lanes covering consecutive entries (coalesced stores).
+// A total (offsets[n]) above cap writes nothing and raises *overflow.
 __global__ void emit_kernel(const int32_t* order, const int64_t* offsets, const int32_t* rect,
-                            int64_t n, int tiles_x, uint32_t* tiles, int32_t* ids) {
+                            int64_t n, int tiles_x, int64_t cap, int32_t* overflow, uint32_t* tiles, int32_t* ids) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t first = warp * 32;
+  if (offsets[n] > cap) {
+    if (blockIdx.x == 0 && threadIdx.x == 0 && overflow) *overflow = 1;
+    return;
+  }
   if (first >= n) return;
   const int64_t i = first + lane;
   int g = 0, x0 = 0, y0 = 0, w = 1;
@@ -347,7 +365,8 @@ __global__ void emit_kernel(const int32_t* order, const int64_t* offsets, const 
 
 // Per-tile [begin, end) of the sorted tile indices: each thread checks four
 // consecutive entries (one 128-bit load plus its two neighbours) for boundaries.
-__global__ void ranges_kernel(const uint32_t* tiles, int64_t n, int2* ranges) {
+__global__ void ranges_kernel(const uint32_t* tiles, int64_t n, const int64_t* n_dev, int2* ranges) {
+  n = live_count(n, n_dev);
   const int64_t i0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (i0 >= n) return;
   constexpr uint32_t NONE = 0xffffffffu;  // never a tile index
@@ -452,9 +471,12 @@ cudaError_t bin_order(const int32_t* count, const uint32_t* depth_key, int64_t n
   return exclusive_scan<int32_t, int64_t>(cs, n, offsets, spart, offsets + n, s);
 }
 
+// m is the intersection count, or with `overflow` the capacity of the buffers: the count
+// offsets[n] is then read on the device, and one above m emits nothing, leaves every
+// tile range empty and sets *overflow.
 cudaError_t bin_emit(const int32_t* order, const int64_t* offsets, const int32_t* rect, int64_t n,
                      int64_t m, int tiles_x, int n_tiles, int32_t* ids, int32_t* ranges, void* ws,
-                     size_t ws_bytes, cudaStream_t s) {
+                     size_t ws_bytes, cudaStream_t s, int32_t* overflow) {
   if (ws_bytes < emit_bytes(m)) return cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(ranges, 0, sizeof(int2) * (size_t)n_tiles, s);
   if (e != cudaSuccess || m == 0) return e;
@@ -467,14 +489,15 @@ cudaError_t bin_emit(const int32_t* order, const int64_t* offsets, const int32_t
   sc.hist = c.take<uint32_t>(RADIX * radix_blocks(m));
   sc.partial = c.take<uint32_t>(scan_blocks(RADIX * radix_blocks(m)) + 1);
   count_launches(1);
-  emit_kernel<<<grid_for(n, 256), 256, 0, s>>>(order, offsets, rect, n, tiles_x, tA, vA);
+  const int64_t* live = overflow ? offsets + n : nullptr;
+  emit_kernel<<<grid_for(n, 256), 256, 0, s>>>(order, offsets, rect, n, tiles_x, m, overflow, tA, vA);
   int bits = 1;
   while ((1 << bits) < n_tiles) ++bits;
   uint32_t* kf; int32_t* vf;
-  e = radix_sort(tA, vA, tB, vB, m, bits, sc, &kf, &vf, ids, s);
+  e = radix_sort(tA, vA, tB, vB, m, bits, sc, &kf, &vf, ids, s, live);
   if (e != cudaSuccess) return e;
   count_launches(1);
-  ranges_kernel<<<grid_for((m + 3) / 4, 256), 256, 0, s>>>(kf, m, reinterpret_cast<int2*>(ranges));
+  ranges_kernel<<<grid_for((m + 3) / 4, 256), 256, 0, s>>>(kf, m, live, reinterpret_cast<int2*>(ranges));
   return cudaGetLastError();
 }
 
@@ -511,7 +534,7 @@ cudaError_t key_ranges(const uint32_t* keys, int64_t n, int64_t n_keys, int32_t*
   cudaError_t e = cudaMemsetAsync(ranges, 0, sizeof(int2) * (size_t)n_keys, s);
   if (e != cudaSuccess || n == 0) return e;
   count_launches(1);
-  ranges_kernel<<<grid_for((n + 3) / 4, 256), 256, 0, s>>>(keys, n, reinterpret_cast<int2*>(ranges));
+  ranges_kernel<<<grid_for((n + 3) / 4, 256), 256, 0, s>>>(keys, n, nullptr, reinterpret_cast<int2*>(ranges));
   return cudaGetLastError();
 }
 

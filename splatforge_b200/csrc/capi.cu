@@ -194,6 +194,23 @@ int sf_b200_bin_emit(const int32_t* order, const int64_t* offsets, const int32_t
                      "bin_emit");
 }
 
+int sf_b200_bin_emit_bounded(const int32_t* order, const int64_t* offsets, const int32_t* tile_rect, int64_t n,
+                             int64_t capacity, int32_t tiles_x, int32_t n_tiles, int32_t* isect_ids,
+                             int32_t* tile_ranges, void* workspace, size_t workspace_bytes, int32_t* overflow,
+                             void* stream) {
+  if (n < 0 || capacity <= 0 || n_tiles <= 0 || tiles_x <= 0 || !tile_ranges || !overflow || !order ||
+      !offsets || !tile_rect || !isect_ids || !workspace)
+    return fail(SF_ERR_ARGUMENT, "bin_emit_bounded: bad arguments");
+  if (capacity > 0x7fffffffLL) return fail(SF_ERR_CAPACITY, "bin_emit_bounded: capacity above 32-bit lists");
+  if (workspace_bytes < sf::bin_workspace_bytes(0, capacity, n_tiles))
+    return fail(SF_ERR_CAPACITY, "bin_emit_bounded: workspace of %zu bytes, %zu needed", workspace_bytes,
+                sf::bin_workspace_bytes(0, capacity, n_tiles));
+  if (!aligned(tile_rect, 16) || !aligned(tile_ranges, 8)) return fail(SF_ERR_ARGUMENT, "bin_emit_bounded: alignment");
+  return cuda_status(sf::bin_emit(order, offsets, tile_rect, n, capacity, tiles_x, n_tiles, isect_ids, tile_ranges,
+                                  workspace, workspace_bytes, as_stream(stream), overflow),
+                     "bin_emit_bounded");
+}
+
 int sf_b200_bin_keys(const int32_t* isect_ids, const int32_t* tile_ranges, const uint32_t* depth_key, int32_t n_tiles,
                      int64_t n_isect, uint64_t* keys, void* stream) {
   if (n_tiles < 0 || n_isect < 0 || (n_isect > 0 && (!isect_ids || !tile_ranges || !depth_key || !keys)))

@@ -34,6 +34,13 @@ constexpr int REC4 = SF_RECORD_FLOATS / 4;  // float4 per record
 #ifndef SF_FWD_MIN_CTAS
 #define SF_FWD_MIN_CTAS 4
 #endif
+// record access: 0 = batches staged in shared memory, 1 = per-warp walk
+#ifndef SF_FWD_WARP_WALK
+#define SF_FWD_WARP_WALK 0
+#endif
+#ifndef SF_BWD_WARP_WALK
+#define SF_BWD_WARP_WALK 0
+#endif
 
 constexpr int FWD_BATCH = SF_FWD_BATCH;
 constexpr int BWD_BATCH = SF_BWD_BATCH;
@@ -156,6 +163,31 @@ __global__ void __launch_bounds__(TILE_PIXELS, SF_FWD_MIN_CTAS) raster_forward_k
   if (tid == 0) s_max = 0;
   __syncthreads();
 
+#if SF_FWD_WARP_WALK
+  // Each warp walks the tile's list on its own, 32 entries at a time, reading the
+  // records from global memory (L1-cached; the CTA's other warps read the same ones):
+  // no shared staging and no barrier, so a warp never waits for a slower one and stops
+  // as soon as its own pixels are done.
+  {
+    const int lane = tid & 31;
+    for (int base = rg.x; base < rg.y; base += 32) {
+      if (__all_sync(FULL, done)) break;
+      int gid = 0;
+      bool hit = false;
+      if (base + lane < rg.y) {
+        gid = __ldg(a.ids + base + lane);
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(a.records) + (int64_t)gid * REC4);
+        const float qc = __ldg(a.records + (int64_t)gid * SF_RECORD_FLOATS + R_QC);
+        hit = box_may_pass(w0.z, w0.w, qc, w0.x, w0.y, wx0, wx1, wy0, wy1, ext2);
+      }
+      unsigned m = __ballot_sync(FULL, hit);
+      while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1;
+        const int gj = __shfl_sync(FULL, gid, j);
+        if (done) continue;
+        const float* rec = a.records + (int64_t)gj * SF_RECORD_FLOATS;
+#else
   for (int base = rg.x; base < rg.y; base += FWD_BATCH) {
     if (__syncthreads_count(done) == TILE_PIXELS) break;
     const int n_in = min(FWD_BATCH, rg.y - base);
@@ -174,6 +206,7 @@ __global__ void __launch_bounds__(TILE_PIXELS, SF_FWD_MIN_CTAS) raster_forward_k
         m &= m - 1;
         if (done) continue;
         const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
+#endif
         Sample s;
         ++evaluated;
         if (!eval_sample<MODE>(rec, pr, ext2, nearp, farp, s)) continue;
@@ -1045,6 +1078,30 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
   const int maxlast = s_max;
   float S = 0.f;
 
+#if SF_BWD_WARP_WALK
+  // Each warp walks back from its own last contributing position, 32 entries at a
+  // time, reading the records from global memory (L1-cached), and adds each (warp,
+  // Gaussian) sum straight to the global gradient: no shared staging, no barrier.
+  (void)maxlast;
+  for (int hi = warp_max(last); hi > rg.x; hi -= 32) {
+    const int lo = max(rg.x, hi - 32);
+    {
+     int gid = 0;
+     bool hit = false;
+     if (lane < hi - lo) {
+       gid = __ldg(a.ids + lo + lane);
+       const float4 w0 = __ldg(reinterpret_cast<const float4*>(a.records) + (int64_t)gid * REC4);
+       const float qc = __ldg(a.records + (int64_t)gid * SF_RECORD_FLOATS + R_QC);
+       hit = box_may_pass(w0.z, w0.w, qc, w0.x, w0.y, wx0, wx1, wy0, wy1, ext2);
+     }
+     unsigned m = __ballot_sync(FULL, hit);
+     while (m) {
+      const int jb = 31 - __clz(m);
+      m &= ~(1u << jb);
+      const int j = jb;
+      const int gj = __shfl_sync(FULL, gid, jb);
+      const int pos = lo + j;
+#else
   for (int hi = maxlast; hi > rg.x; hi -= BWD_BATCH) {
     const int lo = max(rg.x, hi - BWD_BATCH);
     const int n_in = hi - lo;
@@ -1064,12 +1121,17 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
       m &= ~(1u << jb);
       const int j = g * 32 + jb;
       const int pos = lo + j;
+#endif
       float vals[NV];
 #pragma unroll
       for (int q = 0; q < NV; ++q) vals[q] = 0.f;
       bool act = false;
       if (pos < last) {
+#if SF_BWD_WARP_WALK
+        const float* rec = a.records + (int64_t)gj * SF_RECORD_FLOATS;
+#else
         const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
+#endif
         Sample s;
         float auxw = 0.f, auxd = 0.f;
         // the sample evaluation is a fixed function of its inputs (explicit rounding
@@ -1110,6 +1172,23 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
         for (int q = 0; q < 16; ++q) v16[q] = q < NV ? vals[q] : 0.f;
         const float r = reduce16_transposed(v16, lane);
         const int qi = lane >> 1;
+#if SF_BWD_WARP_WALK
+        // record slots 0..19 to the gradient record, 20..21 to absgrad
+        float* const grec = a.grad_records + (int64_t)gj * SF_RECORD_FLOATS;
+        float* const gabs = a.absgrad + (int64_t)gj * 2;
+        if ((lane & 1) == 0 && qi < NV && qi < 16 && r != 0.f) {
+          const int sl = SampleLayout<MODE>::slot(qi);
+          atomicAdd(sl < SF_RECORD_FLOATS ? grec + sl : gabs + (sl - SF_RECORD_FLOATS), r);
+        }
+#pragma unroll
+        for (int q = 16; q < NV; ++q) {
+          const float t = warp_sum(vals[q]);
+          if (lane == 2 * (q - 16) + 1 && t != 0.f) {
+            const int sl = SampleLayout<MODE>::slot(q);
+            atomicAdd(sl < SF_RECORD_FLOATS ? grec + sl : gabs + (sl - SF_RECORD_FLOATS), t);
+          }
+        }
+#else
         if ((lane & 1) == 0 && qi < NV && qi < 16 && r != 0.f)
           atomicAdd(&s_acc[j * AN + SampleLayout<MODE>::slot(qi) - AB], r);
 #pragma unroll
@@ -1117,9 +1196,11 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
           const float t = warp_sum(vals[q]);
           if (lane == 2 * (q - 16) + 1 && t != 0.f) atomicAdd(&s_acc[j * AN + SampleLayout<MODE>::slot(q) - AB], t);
         }
+#endif
       }
      }
     }
+#if !SF_BWD_WARP_WALK
     __syncthreads();
     for (int q = tid; q < n_in * (AN / 4); q += TILE_PIXELS) {
       const int slot = q / (AN / 4), c4 = q - slot * (AN / 4) + AB / 4;
@@ -1132,6 +1213,7 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
         atomicAdd(reinterpret_cast<float2*>(a.absgrad + (int64_t)id * 2), make_float2(val.x, val.y));
       }
     }
+#endif
   }
   if ((DIST & SF_DIST_L1) && inside && k != -1 && a.error_word) atomicOr(a.error_word, 1);
 }
@@ -1183,7 +1265,7 @@ cudaError_t configure_smem(K kernel, size_t bytes, size_t fixed, int ctas, bool&
 
 template <int MODE, int DIST>
 cudaError_t fwd_launch(const RasterFwdArgs& a, int n_tiles, cudaStream_t s) {
-  constexpr size_t bytes = sizeof(float4) * FWD_BATCH * REC4;
+  constexpr size_t bytes = SF_FWD_WARP_WALK ? 0 : sizeof(float4) * FWD_BATCH * REC4;
   constexpr size_t ring = sizeof(float) * ((DIST & SF_DIST_L1) ? 2 : 1) * L1_RING * TILE_PIXELS;
   static bool configured = false;
   cudaError_t e = configure_smem(raster_forward_kernel<MODE, DIST>, bytes, ring, SF_FWD_MIN_CTAS, configured);
@@ -1205,7 +1287,7 @@ cudaError_t fwd_dispatch(const RasterFwdArgs& a, int n_tiles, cudaStream_t s) {
 
 template <int MODE, int DIST>
 cudaError_t bwd_launch(const RasterBwdArgs& a, int n_tiles, cudaStream_t s) {
-  constexpr size_t bytes =
+  constexpr size_t bytes = SF_BWD_WARP_WALK ? 0 :
       sizeof(float4) * BWD_BATCH * REC4 + sizeof(float) * BWD_BATCH * AccWindow<MODE>::N + sizeof(int) * BWD_BATCH;
   static bool configured = false;
   cudaError_t e = configure_smem(raster_backward_kernel<MODE, DIST>, bytes, 16, 3, configured);

@@ -137,9 +137,12 @@ size_t bin_workspace_bytes(int64_t n, int64_t n_isect, int n_tiles);
 cudaError_t bin_order(const int32_t* count, const uint32_t* depth_key, int64_t n,
                       int32_t* order, int64_t* offsets, void* ws, size_t ws_bytes,
                       cudaStream_t s);
+// overflow == nullptr: n_isect is the exact count; else it is the buffers' capacity and
+// the count is read on the device (see binning.cu)
 cudaError_t bin_emit(const int32_t* order, const int64_t* offsets, const int32_t* rect,
                      int64_t n, int64_t n_isect, int tiles_x, int n_tiles, int32_t* ids,
-                     int32_t* ranges, void* ws, size_t ws_bytes, cudaStream_t s);
+                     int32_t* ranges, void* ws, size_t ws_bytes, cudaStream_t s,
+                     int32_t* overflow = nullptr);
 cudaError_t bin_keys(const int32_t* ids, const int32_t* ranges, const uint32_t* depth_key,
                      int n_tiles, int64_t n_isect, uint64_t* keys, cudaStream_t s);
 // stable sort of n (key, value) pairs by key bits [0, bits), in place (keys, vals)

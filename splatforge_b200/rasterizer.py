@@ -38,8 +38,11 @@ AMBISUR_DISTORTION_FLOOR = 1e-30
 PROFILE = None
 # largest per-pixel L1 sample count seen, per image size (capacity of the next render)
 _L1_SEEN = {}
-# renders whose L1 samples overflowed the fixed capacity and were rerun with exact offsets
-COUNTERS = {"l1_reruns": 0}
+# intersection capacity per (Gaussian count, image size), learned from earlier renders
+_ISECT_SEEN = {}
+# renders whose L1 samples overflowed the fixed capacity and were rerun with exact
+# offsets; renders whose intersections overflowed the learned capacity and were re-binned
+COUNTERS = {"l1_reruns": 0, "bin_reruns": 0}
 
 
 def _ptr(t):
@@ -139,6 +142,8 @@ class _Plan:
     ids: torch.Tensor | None = None
     ranges: torch.Tensor | None = None
     n_isect: int = 0
+    # bounded binning: (order, offsets, overflow flag) until the forward's read-back
+    pending: tuple | None = None
     absgrad: torch.Tensor | None = None
     l1_capacity: int | None = None
     error_word: torch.Tensor | None = None
@@ -251,38 +256,104 @@ def _pinned_scratch(dtype=torch.int64):
     return buf
 
 
+def _isect_capacity(total):
+    """Intersection capacity for a count: 1.2x, in the allocator's size classes."""
+    return _size_class(int(total * 1.2) + 1024)
+
+
 def bin_gaussians(plan):
-    """Device tile binning; one host read (intersection count + non-finite flag)."""
+    """Device tile binning.
+
+    The first render of a (Gaussian count, image size) reads the intersection count
+    back (one host synchronisation) and sizes the lists exactly.  Later renders size
+    them by the capacity learned from the earlier ones and read nothing back here: the
+    count sits on the device (offsets[n]) for ``sf_b200_bin_emit_bounded``, and the
+    count, the non-finite flag and the overflow flag come back with the raster
+    forward's one read-back (``_Raster.forward``), which re-bins exactly and reruns the
+    forward if the capacity was exceeded."""
     n, dev = plan.n, plan.device
     size = ctypes.c_size_t()
     call("sf_b200_bin_workspace_bytes", n, 0, plan.n_tiles, ctypes.byref(size))
-    ws = torch.empty((max(size.value, 1),), device=dev, dtype=torch.uint8)
+    ws = _class_empty(max(size.value, 1), torch.uint8, dev)
     order = torch.empty((n,), device=dev, dtype=torch.int32)
     offsets = torch.empty((n + 1,), device=dev, dtype=torch.int64)
     call(
         "sf_b200_bin_order", _ptr(plan.count), _ptr(plan.depth_key), n, _ptr(order), _ptr(offsets),
         _ptr(ws), size.value, _stream(dev),
     )
-    # the one read-back of the binning: two small async copies into pinned memory
-    host, host32 = _pinned_scratch(), _pinned_scratch(torch.int32)
-    host[0:1].copy_(offsets[n:n + 1], non_blocking=True)
-    host32[0:1].copy_(plan.nonfinite[0:1], non_blocking=True)
-    torch.cuda.current_stream(dev).synchronize()
-    total, bad = int(host[0]), int(host32[0])
-    if bad:
-        raise FloatingPointError("non-finite projected bounds")
-    plan.n_isect = int(total)
-    call("sf_b200_bin_workspace_bytes", n, plan.n_isect, plan.n_tiles, ctypes.byref(size))
+    plan.ranges = torch.empty((plan.n_tiles, 2), device=dev, dtype=torch.int32)
+    cap = _ISECT_SEEN.get((n, plan.cam.width, plan.cam.height))
+    if cap is None:
+        # the read-back: two small async copies into pinned memory
+        host, host32 = _pinned_scratch(), _pinned_scratch(torch.int32)
+        host[0:1].copy_(offsets[n:n + 1], non_blocking=True)
+        host32[0:1].copy_(plan.nonfinite[0:1], non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        if int(host32[0]):
+            raise FloatingPointError("non-finite projected bounds")
+        _emit_exact(plan, order, offsets, int(host[0]))
+        return plan
+    call("sf_b200_bin_workspace_bytes", n, cap, plan.n_tiles, ctypes.byref(size))
     if size.value > ws.numel():
         ws = _class_empty(size.value, torch.uint8, dev)
+    plan.ids = _class_empty(cap, torch.int32, dev)
+    overflow = torch.zeros((1,), device=dev, dtype=torch.int32)
+    call(
+        "sf_b200_bin_emit_bounded", _ptr(order), _ptr(offsets), _ptr(plan.rect), n, cap,
+        plan.tiles_x, plan.n_tiles, _ptr(plan.ids), _ptr(plan.ranges), _ptr(ws), size.value,
+        _ptr(overflow), _stream(dev),
+    )
+    plan.pending = (order, offsets, overflow)
+    return plan
+
+
+def _emit_exact(plan, order, offsets, total):
+    n, dev = plan.n, plan.device
+    plan.n_isect = int(total)
+    _ISECT_SEEN[(n, plan.cam.width, plan.cam.height)] = _isect_capacity(total)
+    size = ctypes.c_size_t()
+    call("sf_b200_bin_workspace_bytes", n, plan.n_isect, plan.n_tiles, ctypes.byref(size))
+    ws = _class_empty(max(size.value, 1), torch.uint8, dev)
     plan.ids = _class_empty(max(plan.n_isect, 1), torch.int32, dev)
-    plan.ranges = torch.empty((plan.n_tiles, 2), device=dev, dtype=torch.int32)
     call(
         "sf_b200_bin_emit", _ptr(order), _ptr(offsets), _ptr(plan.rect), n, plan.n_isect,
         plan.tiles_x, plan.n_tiles, _ptr(plan.ids), _ptr(plan.ranges), _ptr(ws), size.value,
         _stream(dev),
     )
-    return plan
+
+
+def _settle_binning(plan, needed):
+    """The forward's one read-back: the largest L1 sample count (when ``needed``) and,
+    after bounded binning, the intersection count and the non-finite and overflow
+    flags.  Returns (largest L1 count or 0, whether the lists were re-binned)."""
+    dev = plan.device
+    host, host32 = _pinned_scratch(), _pinned_scratch(torch.int32)
+    if needed is not None:
+        host32[1:2].copy_(needed, non_blocking=True)
+    if plan.pending is not None:
+        order, offsets, overflow = plan.pending
+        host[0:1].copy_(offsets[plan.n:plan.n + 1], non_blocking=True)
+        host32[0:1].copy_(plan.nonfinite[0:1], non_blocking=True)
+        host32[2:3].copy_(overflow, non_blocking=True)
+    torch.cuda.current_stream(dev).synchronize()
+    most = int(host32[1]) if needed is not None else 0
+    if plan.pending is None:
+        return most, False
+    order, offsets, _ = plan.pending
+    plan.pending = None
+    if int(host32[0]):
+        raise FloatingPointError("non-finite projected bounds")
+    total = int(host[0])
+    key = (plan.n, plan.cam.width, plan.cam.height)
+    if int(host32[2]):
+        # the learned capacity was too small: exact lists, and the caller reruns
+        COUNTERS["bin_reruns"] += 1
+        _emit_exact(plan, order, offsets, total)
+        return most, True
+    plan.n_isect = total
+    if _isect_capacity(total) > _ISECT_SEEN.get(key, 0):
+        _ISECT_SEEN[key] = _isect_capacity(total)
+    return most, False
 
 
 class _Raster(torch.autograd.Function):
@@ -335,11 +406,16 @@ class _Raster(torch.autograd.Function):
             PROFILE.setdefault("counters", []).append(counters)
         else:
             run()
+        if use_l1 or plan.pending is not None:
+            most, rebinned = _settle_binning(plan, needed)
+            if rebinned:
+                plan.stats["bin_rerun"] = True
+                if needed is not None:
+                    needed.zero_()
+                run()
+                if use_l1:
+                    most, _ = _settle_binning(plan, needed)
         if use_l1:
-            host32 = _pinned_scratch(torch.int32)
-            host32[1:2].copy_(needed, non_blocking=True)
-            torch.cuda.current_stream(dev).synchronize()
-            most = int(host32[1])
             plan.stats["l1_max_samples"] = most
             plan.stats["l1_capacity"] = cap
             if plan.l1_capacity is None:

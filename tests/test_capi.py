@@ -53,6 +53,25 @@ def test_abi_version_and_error_paths_without_a_device():
     assert lib.sf_b200_bin_workspace_bytes(1000, 1 << 33, 64, ctypes.byref(size)) == 3
     with pytest.raises(ValueError):
         _lib.call("sf_b200_sh_color_forward", None, 4, None, 10, 7, None, None)
+    # the bounded emit refuses a missing overflow flag or a capacity of zero before any launch
+    rc = lib.sf_b200_bin_emit_bounded(None, None, None, 10, 1000, 4, 16, None, None, None, 0, None, None)
+    assert rc == 1 and b"bin_emit_bounded" in lib.sf_b200_last_error()
+    rc = lib.sf_b200_bin_emit_bounded(None, None, None, 10, 0, 4, 16, None, None, None, 0, None, None)
+    assert rc == 1
+
+
+def test_size_classes_and_intersection_capacity():
+    from splatforge_b200 import rasterizer
+
+    seen = set()
+    for n in range(1, 1 << 24, 99991):
+        c = rasterizer._size_class(n)
+        assert n <= c <= max(n, int(n * 1.125) + 1)
+        seen.add(c)
+    assert len(seen) < ((1 << 24) // 99991) // 3  # few distinct sizes
+    for total in (0, 5000, 52_349_663):
+        cap = rasterizer._isect_capacity(total)
+        assert cap >= 1.2 * total and cap == rasterizer._size_class(cap)
 
 
 def test_rasterize_rejects_cpu_tensors_without_fallback():
