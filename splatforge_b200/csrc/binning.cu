@@ -133,6 +133,7 @@ constexpr int RS_WARPS = RS_THREADS / 32;
 constexpr int RS_ROUNDS = SF_RS_ROUNDS;               // 32-key rounds per warp
 constexpr int RS_CHUNK = RS_THREADS * RS_ROUNDS;      // keys per CTA
 constexpr int RADIX = 256;
+static_assert(RS_THREADS == RADIX, "one thread per digit in the histogram stages");
 
 // Per-block digit histograms.  Each thread reads its keys four at a time (128-bit
 // loads) when the block's slab is 16-byte aligned.
@@ -148,6 +149,10 @@ __global__ void __launch_bounds__(RS_THREADS) radix_upsweep_kernel(const uint32_
                                                                    const int64_t* n_dev, int shift, int nb,
                                                                    uint32_t* hist) {
   n = live_count(n, n_dev);
+  if ((int64_t)blockIdx.x * RS_CHUNK >= n) {  // a block past the live count: empty histogram
+    hist[(int64_t)threadIdx.x * nb + blockIdx.x] = 0;  // RS_THREADS == RADIX
+    return;
+  }
   __shared__ uint32_t s_hist[RS_WARPS][RADIX];
   const int wid = threadIdx.x >> 5;
   for (int k = threadIdx.x; k < RS_WARPS * RADIX; k += RS_THREADS) (&s_hist[0][0])[k] = 0;
@@ -184,6 +189,7 @@ __global__ void __launch_bounds__(RS_THREADS, RS_ROUNDS <= 8 ? 4 : 2) radix_down
     const uint32_t* keys_in, const int32_t* vals_in, int64_t n, const int64_t* n_dev, int shift, int nb,
     const uint32_t* offsets, uint32_t* keys_out, int32_t* vals_out) {
   n = live_count(n, n_dev);
+  if ((int64_t)blockIdx.x * RS_CHUNK >= n) return;  // past the live count: nothing to move
   __shared__ uint32_t s_cnt[RS_WARPS][RADIX];
   __shared__ uint32_t s_off[RADIX];    // this block's first output slot per digit
   __shared__ uint32_t s_local[RADIX];  // first slot of each digit inside the block

@@ -34,12 +34,10 @@ constexpr int REC4 = SF_RECORD_FLOATS / 4;  // float4 per record
 #ifndef SF_FWD_MIN_CTAS
 #define SF_FWD_MIN_CTAS 4
 #endif
-// record access: 0 = batches staged in shared memory, 1 = per-warp walk
-#ifndef SF_FWD_WARP_WALK
-#define SF_FWD_WARP_WALK 0
-#endif
+// backward record access: 1 = each warp walks the tile list on its own (records read
+// through L1, sums added straight to global memory), 0 = batches staged in shared memory
 #ifndef SF_BWD_WARP_WALK
-#define SF_BWD_WARP_WALK 0
+#define SF_BWD_WARP_WALK 1
 #endif
 
 constexpr int FWD_BATCH = SF_FWD_BATCH;
@@ -163,31 +161,6 @@ __global__ void __launch_bounds__(TILE_PIXELS, SF_FWD_MIN_CTAS) raster_forward_k
   if (tid == 0) s_max = 0;
   __syncthreads();
 
-#if SF_FWD_WARP_WALK
-  // Each warp walks the tile's list on its own, 32 entries at a time, reading the
-  // records from global memory (L1-cached; the CTA's other warps read the same ones):
-  // no shared staging and no barrier, so a warp never waits for a slower one and stops
-  // as soon as its own pixels are done.
-  {
-    const int lane = tid & 31;
-    for (int base = rg.x; base < rg.y; base += 32) {
-      if (__all_sync(FULL, done)) break;
-      int gid = 0;
-      bool hit = false;
-      if (base + lane < rg.y) {
-        gid = __ldg(a.ids + base + lane);
-        const float4 w0 = __ldg(reinterpret_cast<const float4*>(a.records) + (int64_t)gid * REC4);
-        const float qc = __ldg(a.records + (int64_t)gid * SF_RECORD_FLOATS + R_QC);
-        hit = box_may_pass(w0.z, w0.w, qc, w0.x, w0.y, wx0, wx1, wy0, wy1, ext2);
-      }
-      unsigned m = __ballot_sync(FULL, hit);
-      while (m) {
-        const int j = __ffs(m) - 1;
-        m &= m - 1;
-        const int gj = __shfl_sync(FULL, gid, j);
-        if (done) continue;
-        const float* rec = a.records + (int64_t)gj * SF_RECORD_FLOATS;
-#else
   for (int base = rg.x; base < rg.y; base += FWD_BATCH) {
     if (__syncthreads_count(done) == TILE_PIXELS) break;
     const int n_in = min(FWD_BATCH, rg.y - base);
@@ -206,7 +179,6 @@ __global__ void __launch_bounds__(TILE_PIXELS, SF_FWD_MIN_CTAS) raster_forward_k
         m &= m - 1;
         if (done) continue;
         const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
-#endif
         Sample s;
         ++evaluated;
         if (!eval_sample<MODE>(rec, pr, ext2, nearp, farp, s)) continue;
@@ -610,7 +582,10 @@ __device__ __forceinline__ bool l1_sort_pixel_packed(float* col_d, float* col_w,
 // register budget of the rarer long runs does not limit the occupancy of the common case.
 // Longer runs go to l1_resolve_long_kernel.
 template <int CLASS>
-__global__ void __launch_bounds__(128) l1_resolve_kernel(
+#ifndef SF_RESOLVE0_MIN_CTAS
+#define SF_RESOLVE0_MIN_CTAS 7  // 72 registers (7 CTAs of 4 warps per SM)
+#endif
+__global__ void __launch_bounds__(128, CLASS == 0 ? SF_RESOLVE0_MIN_CTAS : 4) l1_resolve_kernel(
     sf_camera cam, float* state, float* l1s, int64_t slots, const int64_t* off, int cap, int smem_k,
     float* out_l1) {
   (void)smem_k;
@@ -1003,6 +978,7 @@ __global__ void __launch_bounds__(LONG_THREADS, 2) l1_resolve_long_kernel(
 // ------------------------------------------------------------------ backward
 template <int MODE, int DIST>
 __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const RasterBwdArgs a) {
+#if !SF_BWD_WARP_WALK
   constexpr int AB = AccWindow<MODE>::BASE, AN = AccWindow<MODE>::N;
   // the batch's records (BWD_BATCH * REC4 float4), gradient accumulator (BWD_BATCH * AN
   // floats) and Gaussian ids (BWD_BATCH ints), in dynamic shared memory
@@ -1011,6 +987,7 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
   float* s_acc = reinterpret_cast<float*>(s_dyn + BWD_BATCH * REC4);
   int* s_id = reinterpret_cast<int*>(s_dyn + BWD_BATCH * REC4 + BWD_BATCH * AN / 4);
   __shared__ int s_max;
+#endif
   constexpr int NV = SampleLayout<MODE>::NV;
   const int tile = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31;
@@ -1068,6 +1045,7 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
     pg.W = pg.D = 0.f;
     pg.med_pos = -1;
   }
+#if !SF_BWD_WARP_WALK
   if (tid == 0) s_max = rg.x;
   __syncthreads();
   {
@@ -1076,13 +1054,13 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
   }
   __syncthreads();
   const int maxlast = s_max;
+#endif
   float S = 0.f;
 
 #if SF_BWD_WARP_WALK
   // Each warp walks back from its own last contributing position, 32 entries at a
   // time, reading the records from global memory (L1-cached), and adds each (warp,
   // Gaussian) sum straight to the global gradient: no shared staging, no barrier.
-  (void)maxlast;
   for (int hi = warp_max(last); hi > rg.x; hi -= 32) {
     const int lo = max(rg.x, hi - 32);
     {
@@ -1265,7 +1243,7 @@ cudaError_t configure_smem(K kernel, size_t bytes, size_t fixed, int ctas, bool&
 
 template <int MODE, int DIST>
 cudaError_t fwd_launch(const RasterFwdArgs& a, int n_tiles, cudaStream_t s) {
-  constexpr size_t bytes = SF_FWD_WARP_WALK ? 0 : sizeof(float4) * FWD_BATCH * REC4;
+  constexpr size_t bytes = sizeof(float4) * FWD_BATCH * REC4;
   constexpr size_t ring = sizeof(float) * ((DIST & SF_DIST_L1) ? 2 : 1) * L1_RING * TILE_PIXELS;
   static bool configured = false;
   cudaError_t e = configure_smem(raster_forward_kernel<MODE, DIST>, bytes, ring, SF_FWD_MIN_CTAS, configured);
