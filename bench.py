@@ -123,10 +123,11 @@ class ClockSampler:
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant
-# kernel: a single-pass capture of the 100k-Gaussian 800x800 case (496.65 + 8.68 MB per
-# launch, 43.28M contributing samples) scaled by the 1080p frame's contributing samples
-# (291.08M): the backward's traffic is the per-sample L1 factors plus per-pixel state.
-MEASURED_TRAFFIC = {("surfaces1m_1080p", "gof", "both", "raster_backward"): round((496.65e6 + 8.68e6) * 291.08 / 43.28)}
+# kernel: an ncu capture of one launch on the 100k-Gaussian 800x800 case (520.40 + 14.94
+# MB, 43.28M contributing samples) scaled by the 1080p frame's contributing samples
+# (291.08M): the backward's traffic is the per-sample L1 factors plus per-pixel state
+# and the records its warps read.
+MEASURED_TRAFFIC = {("surfaces1m_1080p", "gof", "both", "raster_backward"): round((520.40e6 + 14.94e6) * 291.08 / 43.28)}
 
 
 def algorithmic_flops(mode, n_pairs_fwd):

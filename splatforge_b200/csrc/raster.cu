@@ -403,38 +403,66 @@ __device__ __noinline__ float l1_sort_pixel(float* col_d, float* col_w, int64_t 
 // their room is a multiple of 8, so it never leaves the pixel's run.
 template <int I>
 __device__ __forceinline__ void l1_load_run(const float* col, int64_t base, int n, int lane, bool vec, float (&v)[I]) {
-#pragma unroll
-  for (int q = 0; q < I / 4; ++q) {
-    const int e0 = lane * I + 4 * q;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+  if constexpr (I == 2) {  // one 8-byte load per lane
+    const int e0 = lane * 2;
+    float2 x = make_float2(0.f, 0.f);
     if (e0 < n) {
       if (vec) {
-        x = *reinterpret_cast<const float4*>(col + base + e0);
+        x = *reinterpret_cast<const float2*>(col + base + e0);
       } else {
         x.x = col[base + e0];
         x.y = e0 + 1 < n ? col[base + e0 + 1] : 0.f;
-        x.z = e0 + 2 < n ? col[base + e0 + 2] : 0.f;
-        x.w = e0 + 3 < n ? col[base + e0 + 3] : 0.f;
       }
     }
-    v[4 * q] = x.x; v[4 * q + 1] = x.y; v[4 * q + 2] = x.z; v[4 * q + 3] = x.w;
+    v[0] = x.x;
+    v[1] = x.y;
+  } else {
+#pragma unroll
+    for (int q = 0; q < I / 4; ++q) {
+      const int e0 = lane * I + 4 * q;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e0 < n) {
+        if (vec) {
+          x = *reinterpret_cast<const float4*>(col + base + e0);
+        } else {
+          x.x = col[base + e0];
+          x.y = e0 + 1 < n ? col[base + e0 + 1] : 0.f;
+          x.z = e0 + 2 < n ? col[base + e0 + 2] : 0.f;
+          x.w = e0 + 3 < n ? col[base + e0 + 3] : 0.f;
+        }
+      }
+      v[4 * q] = x.x; v[4 * q + 1] = x.y; v[4 * q + 2] = x.z; v[4 * q + 3] = x.w;
+    }
   }
 }
 
 template <int I>
 __device__ __forceinline__ void l1_store_run(float* col, int64_t base, int n, int lane, bool vec, const float* s) {
+  if constexpr (I == 2) {
+    const int e0 = lane * 2;
+    if (e0 < n) {
+      const float2 x = *reinterpret_cast<const float2*>(s + e0);
+      if (vec && e0 + 2 <= n) {
+        *reinterpret_cast<float2*>(col + base + e0) = x;
+      } else {
+        col[base + e0] = x.x;
+        if (e0 + 1 < n) col[base + e0 + 1] = x.y;
+      }
+    }
+  } else {
 #pragma unroll
-  for (int q = 0; q < I / 4; ++q) {
-    const int e0 = lane * I + 4 * q;
-    if (e0 >= n) continue;
-    const float4 x = *reinterpret_cast<const float4*>(s + e0);
-    if (vec && e0 + 4 <= n) {
-      *reinterpret_cast<float4*>(col + base + e0) = x;
-    } else {
-      col[base + e0] = x.x;
-      if (e0 + 1 < n) col[base + e0 + 1] = x.y;
-      if (e0 + 2 < n) col[base + e0 + 2] = x.z;
-      if (e0 + 3 < n) col[base + e0 + 3] = x.w;
+    for (int q = 0; q < I / 4; ++q) {
+      const int e0 = lane * I + 4 * q;
+      if (e0 >= n) continue;
+      const float4 x = *reinterpret_cast<const float4*>(s + e0);
+      if (vec && e0 + 4 <= n) {
+        *reinterpret_cast<float4*>(col + base + e0) = x;
+      } else {
+        col[base + e0] = x.x;
+        if (e0 + 1 < n) col[base + e0 + 1] = x.y;
+        if (e0 + 2 < n) col[base + e0 + 2] = x.z;
+        if (e0 + 3 < n) col[base + e0 + 3] = x.w;
+      }
     }
   }
 }
@@ -443,7 +471,7 @@ template <int I>
 __device__ __forceinline__ bool l1_sort_pixel_packed(float* col_d, float* col_w, int64_t base, int n, int lane,
                                                      bool vec, float* s_w, float* s_o, float& raw_out) {
   constexpr int NN = 32 * I;
-  constexpr int LOGN = (NN == 128) ? 7 : (NN == 256 ? 8 : 9);
+  constexpr int LOGN = (NN == 64) ? 6 : (NN == 128) ? 7 : (NN == 256 ? 8 : 9);
   static_assert(NN == (1 << LOGN), "power of two");
   uint32_t key[I];
   uint32_t lo = 0xffffffffu, hi = 0u;
@@ -457,10 +485,14 @@ __device__ __forceinline__ bool l1_sort_pixel_packed(float* col_d, float* col_w,
       key[j] = e < n ? __float_as_uint(dv[j]) : 0u;
       if (e < n) { lo = min(lo, key[j]); hi = max(hi, key[j]); }
     }
+    if constexpr (I == 2) {
+      *reinterpret_cast<float2*>(s_w + lane * 2) = make_float2(wv[0], wv[1]);
+    } else {
 #pragma unroll
-    for (int q = 0; q < I / 4; ++q)
-      *reinterpret_cast<float4*>(s_w + lane * I + 4 * q) =
-          make_float4(wv[4 * q], wv[4 * q + 1], wv[4 * q + 2], wv[4 * q + 3]);
+      for (int q = 0; q < I / 4; ++q)
+        *reinterpret_cast<float4*>(s_w + lane * I + 4 * q) =
+            make_float4(wv[4 * q], wv[4 * q + 1], wv[4 * q + 2], wv[4 * q + 3]);
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -642,7 +674,10 @@ __global__ void __launch_bounds__(128, CLASS == 0 ? SF_RESOLVE0_MIN_CTAS : 4) l1
       const int64_t base = __shfl_sync(FULL, my_base, l);
       float raw = 0.f;
       if (CLASS == 0) {
-        if (n <= 128) {
+        if (n <= 64) {
+          if (!l1_sort_pixel_packed<2>(col_d, col_w, base, n, lane, vec, s_w, s_o, raw))
+            raw = l1_sort_pixel<2>(col_d, col_w, base, n, lane);
+        } else if (n <= 128) {
           if (!l1_sort_pixel_packed<4>(col_d, col_w, base, n, lane, vec, s_w, s_o, raw))
             raw = l1_sort_pixel<4>(col_d, col_w, base, n, lane);
         } else {
