@@ -704,23 +704,23 @@ constexpr int LONG_THREADS = 256;
 __device__ __forceinline__ unsigned long long kmin(unsigned long long a, unsigned long long b) { return a < b ? a : b; }
 __device__ __forceinline__ unsigned long long kmax(unsigned long long a, unsigned long long b) { return a < b ? b : a; }
 
-// Runs of 513 .. 256 I samples, I = 4, 8, 16: the CTA sorts the pixel's exact 64-bit
-// (depth bits, compositing index) keys as one bitonic network of NN = 256 I positions
-// held in registers, thread t owning positions t I .. t I + I - 1.  The network is the
+// Runs of up to T I samples (T threads, I = 4, 8, 16 per thread): the CTA sorts the
+// pixel's exact 64-bit (depth bits, compositing index) keys as one bitonic network of
+// NN = T I positions held in registers, thread t owning positions t I .. t I + I - 1.  The network is the
 // all-ascending form of l1_sort_pixel_packed (a merge of size s first compares p with
 // its mirror p ^ (s - 1), then half-cleaners p vs p ^ h, the lower position taking the
 // minimum).  A compare-exchange whose partner is in the same thread is a register
 // min/max, one in the same warp a shuffle, and only the stages whose partner is in
 // another warp (6 of the 78 stages at NN = 4096) exchange through shared memory, where
-// the keys sit striped (position t I + j at j * 256 + t: conflict-free for every
-// partner distance).  The weights are parked by compositing index in s_w; after the
+// the keys sit striped (position t I + j at j T + t: conflict-free for every partner
+// distance).  The weights are parked by compositing index in s_w; after the
 // sort each thread scans its I sorted samples, a block scan of the per-thread totals
 // gives each its prefix, and both factors are assembled in shared memory by compositing
 // index and leave in blocked layout.  Returns this thread's share of the L1 value.
-template <int I>
+template <int T, int I>
 __device__ float l1_sort_pixel_cta(float* col_d, float* col_w, int64_t base, int n, bool vec,
-                                   unsigned long long* s_key, float* s_w, float (*s_tot)[LONG_THREADS / 32]) {
-  constexpr int NN = LONG_THREADS * I;
+                                   unsigned long long* s_key, float* s_w, float (*s_tot)[T / 32]) {
+  constexpr int NN = T * I;
   constexpr int WI = 32 * I;  // positions per warp
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   unsigned long long key[I];
@@ -781,11 +781,11 @@ __device__ float l1_sort_pixel_cta(float* col_d, float* col_w, int64_t base, int
       const bool take_min = (tid & (size / (2 * I))) == 0;
       __syncthreads();  // the previous exchange has been read
 #pragma unroll
-      for (int j = 0; j < I; ++j) s_key[j * LONG_THREADS + tid] = key[j];
+      for (int j = 0; j < I; ++j) s_key[j * T + tid] = key[j];
       __syncthreads();
 #pragma unroll
       for (int j = 0; j < I; ++j) {
-        const unsigned long long o = s_key[(I - 1 - j) * LONG_THREADS + (tid ^ tm)];
+        const unsigned long long o = s_key[(I - 1 - j) * T + (tid ^ tm)];
         key[j] = take_min ? kmin(key[j], o) : kmax(key[j], o);
       }
     }
@@ -796,11 +796,11 @@ __device__ float l1_sort_pixel_cta(float* col_d, float* col_w, int64_t base, int
       if (h >= WI) {
         __syncthreads();
 #pragma unroll
-        for (int j = 0; j < I; ++j) s_key[j * LONG_THREADS + tid] = key[j];
+        for (int j = 0; j < I; ++j) s_key[j * T + tid] = key[j];
         __syncthreads();
 #pragma unroll
         for (int j = 0; j < I; ++j) {
-          const unsigned long long o = s_key[j * LONG_THREADS + (tid ^ ts)];
+          const unsigned long long o = s_key[j * T + (tid ^ ts)];
           key[j] = take_min ? kmin(key[j], o) : kmax(key[j], o);
         }
       } else {
@@ -844,7 +844,7 @@ __device__ float l1_sort_pixel_cta(float* col_d, float* col_w, int64_t base, int
   __syncthreads();  // also: every thread has read its weights from s_w
   float pw = iw - lw, pwd = iwd - lwd, Wt = 0.f, Dt = 0.f;
 #pragma unroll
-  for (int q = 0; q < LONG_THREADS / 32; ++q) {
+  for (int q = 0; q < T / 32; ++q) {
     if (q < wid) { pw += s_tot[0][q]; pwd += s_tot[1][q]; }
     Wt += s_tot[0][q];
     Dt += s_tot[1][q];
@@ -923,9 +923,9 @@ __global__ void __launch_bounds__(LONG_THREADS, 2) l1_resolve_long_kernel(
     while (nn < n) nn <<= 1;
     float raw;
     if (nn <= 4096) {
-      raw = nn == 1024 ? l1_sort_pixel_cta<4>(col_d, col_w, base, n, vec, s_long, s_w, s_tot)
-          : nn == 2048 ? l1_sort_pixel_cta<8>(col_d, col_w, base, n, vec, s_long, s_w, s_tot)
-                       : l1_sort_pixel_cta<16>(col_d, col_w, base, n, vec, s_long, s_w, s_tot);
+      raw = nn == 1024 ? l1_sort_pixel_cta<LONG_THREADS, 4>(col_d, col_w, base, n, vec, s_long, s_w, s_tot)
+          : nn == 2048 ? l1_sort_pixel_cta<LONG_THREADS, 8>(col_d, col_w, base, n, vec, s_long, s_w, s_tot)
+                       : l1_sort_pixel_cta<LONG_THREADS, 16>(col_d, col_w, base, n, vec, s_long, s_w, s_tot);
     } else {
       float Wt = 0.f, Dt = 0.f;
       for (int k = tid; k < nn; k += LONG_THREADS) {
