@@ -617,7 +617,10 @@ template <int CLASS>
 #ifndef SF_RESOLVE0_MIN_CTAS
 #define SF_RESOLVE0_MIN_CTAS 7  // 72 registers (7 CTAs of 4 warps per SM)
 #endif
-__global__ void __launch_bounds__(128, CLASS == 0 ? SF_RESOLVE0_MIN_CTAS : 4) l1_resolve_kernel(
+#ifndef SF_RESOLVE1_MIN_CTAS
+#define SF_RESOLVE1_MIN_CTAS 4  // 128 registers
+#endif
+__global__ void __launch_bounds__(128, CLASS == 0 ? SF_RESOLVE0_MIN_CTAS : SF_RESOLVE1_MIN_CTAS) l1_resolve_kernel(
     sf_camera cam, float* state, float* l1s, int64_t slots, const int64_t* off, int cap, int smem_k,
     float* out_l1) {
   (void)smem_k;
@@ -1266,7 +1269,9 @@ template <typename K>
 cudaError_t configure_smem(K kernel, size_t bytes, size_t fixed, int ctas, bool& done) {
   if (done) return cudaSuccess;
   cudaError_t e = cudaSuccess;
-  if (bytes > 48 * 1024) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  // above 48 KB of static + dynamic shared memory a launch needs the opt-in
+  if (bytes + fixed > 48 * 1024)
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
   const size_t need = (size_t)ctas * (bytes + fixed + 1024);
   if (e == cudaSuccess && need > 132 * 1024) {
     const int pct = (int)((need * 100 + 228 * 1024 - 1) / (228 * 1024));
