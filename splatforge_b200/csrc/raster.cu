@@ -39,6 +39,11 @@ constexpr int REC4 = SF_RECORD_FLOATS / 4;  // float4 per record
 #ifndef SF_BWD_WARP_WALK
 #define SF_BWD_WARP_WALK 1
 #endif
+// with the walk: 1 = each group's hit records staged in the warp's own shared-memory
+// slice, 0 = read from global memory at every use
+#ifndef SF_BWD_WARP_STAGE
+#define SF_BWD_WARP_STAGE 1
+#endif
 
 constexpr int FWD_BATCH = SF_FWD_BATCH;
 constexpr int BWD_BATCH = SF_BWD_BATCH;
@@ -1016,6 +1021,11 @@ __global__ void __launch_bounds__(LONG_THREADS, 2) l1_resolve_long_kernel(
 // ------------------------------------------------------------------ backward
 template <int MODE, int DIST>
 __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const RasterBwdArgs a) {
+#if SF_BWD_WARP_WALK && SF_BWD_WARP_STAGE
+  // per warp: the records of its current group's hits (32 slots of REC4 float4)
+  __shared__ float4 s_wrec[(TILE_PIXELS / 32) * 32 * REC4];
+  const int wid = threadIdx.x >> 5;
+#endif
 #if !SF_BWD_WARP_WALK
   constexpr int AB = AccWindow<MODE>::BASE, AN = AccWindow<MODE>::N;
   // the batch's records (BWD_BATCH * REC4 float4), gradient accumulator (BWD_BATCH * AN
@@ -1109,8 +1119,22 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
        const float4 w0 = __ldg(reinterpret_cast<const float4*>(a.records) + (int64_t)gid * REC4);
        const float qc = __ldg(a.records + (int64_t)gid * SF_RECORD_FLOATS + R_QC);
        hit = box_may_pass(w0.z, w0.w, qc, w0.x, w0.y, wx0, wx1, wy0, wy1, ext2);
+#if SF_BWD_WARP_STAGE
+       // a hit's whole record into the warp's slice of shared memory, all lanes' loads
+       // in flight together
+       if (hit) {
+         const float4* src = reinterpret_cast<const float4*>(a.records) + (int64_t)gid * REC4;
+         float4* dst = s_wrec + (wid * 32 + lane) * REC4;
+         dst[0] = w0;
+#pragma unroll
+         for (int c = 1; c < REC4; ++c) dst[c] = __ldg(src + c);
+       }
+#endif
      }
      unsigned m = __ballot_sync(FULL, hit);
+#if SF_BWD_WARP_STAGE
+     __syncwarp();
+#endif
      while (m) {
       const int jb = 31 - __clz(m);
       m &= ~(1u << jb);
@@ -1143,7 +1167,9 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
       for (int q = 0; q < NV; ++q) vals[q] = 0.f;
       bool act = false;
       if (pos < last) {
-#if SF_BWD_WARP_WALK
+#if SF_BWD_WARP_WALK && SF_BWD_WARP_STAGE
+        const float* rec = reinterpret_cast<const float*>(s_wrec + (wid * 32 + j) * REC4);
+#elif SF_BWD_WARP_WALK
         const float* rec = a.records + (int64_t)gj * SF_RECORD_FLOATS;
 #else
         const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
@@ -1215,6 +1241,9 @@ __global__ void __launch_bounds__(TILE_PIXELS, 3) raster_backward_kernel(const R
 #endif
       }
      }
+#if SF_BWD_WARP_STAGE
+     __syncwarp();  // the slice is read before the next group overwrites it
+#endif
     }
 #if !SF_BWD_WARP_WALK
     __syncthreads();
