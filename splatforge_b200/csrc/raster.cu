@@ -34,6 +34,11 @@ constexpr int REC4 = SF_RECORD_FLOATS / 4;  // float4 per record
 #ifndef SF_FWD_MIN_CTAS
 #define SF_FWD_MIN_CTAS 4
 #endif
+// forward record access: 1 = each warp walks the tile list on its own and stages its
+// hits' records in its shared-memory slice, 0 = CTA batches of FWD_BATCH records
+#ifndef SF_FWD_WARP_WALK
+#define SF_FWD_WARP_WALK 1
+#endif
 // backward record access: 1 = each warp walks the tile list on its own (records read
 // through L1, sums added straight to global memory), 0 = batches staged in shared memory
 #ifndef SF_BWD_WARP_WALK
@@ -74,6 +79,7 @@ __device__ __forceinline__ void tile_pixel(int tid, int tx, int ty, int& u, int&
   ptid = ly * TILE + lx;  // row-major index of the pixel inside its tile
 }
 
+#if !(SF_FWD_WARP_WALK && SF_BWD_WARP_WALK)
 // Warp-level culling of batch slots g*32 .. g*32+31: bit l is set when the Gaussian in
 // slot g*32+l may pass squared <= extent^2 at a pixel of this warp (box_may_pass over
 // the box spanned by the warp's pixel centres).
@@ -87,6 +93,7 @@ __device__ __forceinline__ unsigned warp_cull(const float4* s_rec, int n_in, int
   }
   return __ballot_sync(FULL, hit);
 }
+#endif
 
 __device__ __forceinline__ float warp_minf(float v) {
 #pragma unroll
@@ -166,6 +173,38 @@ __global__ void __launch_bounds__(TILE_PIXELS, SF_FWD_MIN_CTAS) raster_forward_k
   if (tid == 0) s_max = 0;
   __syncthreads();
 
+#if SF_FWD_WARP_WALK
+  // Each warp walks the tile's list on its own, 32 entries at a time: lane l tests
+  // entry l against the warp's box, each passing lane copies its record into the warp's
+  // own slice of shared memory, and the hits are evaluated from there.  No CTA barrier:
+  // a warp never waits for a slower one and stops when its own pixels are done.
+  {
+    const int lane = tid & 31;
+    float4* const s_w = s_rec + (tid >> 5) * 32 * REC4;
+    for (int base = rg.x; base < rg.y; base += 32) {
+      if (__all_sync(FULL, done)) break;
+      bool hit = false;
+      if (base + lane < rg.y) {
+        const int gid = __ldg(a.ids + base + lane);
+        const float4* src = reinterpret_cast<const float4*>(a.records) + (int64_t)gid * REC4;
+        const float4 w0 = __ldg(src);
+        const float qc = __ldg(a.records + (int64_t)gid * SF_RECORD_FLOATS + R_QC);
+        hit = box_may_pass(w0.z, w0.w, qc, w0.x, w0.y, wx0, wx1, wy0, wy1, ext2);
+        if (hit) {
+          float4* dst = s_w + lane * REC4;
+          dst[0] = w0;
+#pragma unroll
+          for (int c = 1; c < REC4; ++c) dst[c] = __ldg(src + c);
+        }
+      }
+      unsigned m = __ballot_sync(FULL, hit);
+      __syncwarp();
+      while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1;
+        if (done) continue;
+        const float* rec = reinterpret_cast<const float*>(&s_w[j * REC4]);
+#else
   for (int base = rg.x; base < rg.y; base += FWD_BATCH) {
     if (__syncthreads_count(done) == TILE_PIXELS) break;
     const int n_in = min(FWD_BATCH, rg.y - base);
@@ -184,6 +223,7 @@ __global__ void __launch_bounds__(TILE_PIXELS, SF_FWD_MIN_CTAS) raster_forward_k
         m &= m - 1;
         if (done) continue;
         const float* rec = reinterpret_cast<const float*>(&s_rec[j * REC4]);
+#endif
         Sample s;
         ++evaluated;
         if (!eval_sample<MODE>(rec, pr, ext2, nearp, farp, s)) continue;
@@ -217,6 +257,9 @@ __global__ void __launch_bounds__(TILE_PIXELS, SF_FWD_MIN_CTAS) raster_forward_k
         Td *= (double)(1.f - s.alpha);
         if (Td < t_stop) done = true;
       }
+#if SF_FWD_WARP_WALK
+      __syncwarp();  // the slice is read before the next group overwrites it
+#endif
     }
   }
 
@@ -1312,7 +1355,7 @@ cudaError_t configure_smem(K kernel, size_t bytes, size_t fixed, int ctas, bool&
 
 template <int MODE, int DIST>
 cudaError_t fwd_launch(const RasterFwdArgs& a, int n_tiles, cudaStream_t s) {
-  constexpr size_t bytes = sizeof(float4) * FWD_BATCH * REC4;
+  constexpr size_t bytes = sizeof(float4) * (SF_FWD_WARP_WALK ? TILE_PIXELS : FWD_BATCH) * REC4;
   constexpr size_t ring = sizeof(float) * ((DIST & SF_DIST_L1) ? 2 : 1) * L1_RING * TILE_PIXELS;
   static bool configured = false;
   cudaError_t e = configure_smem(raster_forward_kernel<MODE, DIST>, bytes, ring, SF_FWD_MIN_CTAS, configured);
