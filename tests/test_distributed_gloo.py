@@ -65,7 +65,9 @@ def _worker(rank, world, port, mode, queue):
             reducer = distributed.GradientAllReduce(p.tensors())
         assert reducer.floats_per_gaussian == 59
         reducer()
-        queue.put((rank, "ok", [t.grad.clone() for t in p.tensors()]))
+        # numpy arrays travel by value: a torch tensor would be shared through a file
+        # descriptor that dies with this process, racing the parent's read
+        queue.put((rank, "ok", [t.grad.detach().cpu().numpy().copy() for t in p.tensors()]))
     except Exception as exc:  # report to the parent instead of hanging
         queue.put((rank, "error", f"{type(exc).__name__}: {exc}\n{traceback.format_exc()[-400:]}"))
     finally:
@@ -88,7 +90,7 @@ def _run(mode):
         pr.join(timeout=60)
         if pr.is_alive():
             pr.kill()
-    return results
+    return {r: (st, [torch.from_numpy(a) for a in pl] if st == "ok" else pl) for r, (st, pl) in results.items()}
 
 
 def test_allreduced_gradients_equal_full_batch_gradients():
