@@ -123,11 +123,11 @@ class ClockSampler:
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant
-# kernel: an ncu capture of one launch on the 100k-Gaussian 800x800 case (520.40 + 14.94
+# kernel: an ncu capture of one launch on the 100k-Gaussian 800x800 case (485.92 + 16.24
 # MB, 43.28M contributing samples) scaled by the 1080p frame's contributing samples
 # (291.08M): the backward's traffic is the per-sample L1 factors plus per-pixel state
 # and the records its warps read.
-MEASURED_TRAFFIC = {("surfaces1m_1080p", "gof", "both", "raster_backward"): round((520.40e6 + 14.94e6) * 291.08 / 43.28)}
+MEASURED_TRAFFIC = {("surfaces1m_1080p", "gof", "both", "raster_backward"): round((485.92e6 + 16.24e6) * 291.08 / 43.28)}
 
 
 def algorithmic_flops(mode, n_pairs_fwd):
